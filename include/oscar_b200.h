@@ -1,0 +1,168 @@
+/*
+ * oscar_b200.h -- C ABI of the B200-native OSCAR INT2 rotated KV-cache hot path.
+ *
+ * Every entry point takes plain pointers and sizes (no framework types), runs
+ * asynchronously on the CUDA stream passed as `stream` (a cudaStream_t; NULL =
+ * legacy default stream) and returns a status code:
+ *
+ *   OSCAR_OK (0)            launched
+ *   OSCAR_ERR_INVALID (1)   invalid layout, size or geometry (the Python layer raises ValueError)
+ *   OSCAR_ERR_UNSUPPORTED(2) a valid layout this build has no kernel for
+ *   OSCAR_ERR_CUDA (3)      the CUDA runtime reported an error (RuntimeError)
+ *
+ * oscar_last_error() returns the message of the last failure on the calling thread.
+ *
+ * Device pointers: every tensor argument is device memory unless it is marked
+ * HOST.  Caches are byte views of the paged KV caches, shape
+ * [num_blocks, block_size, num_kv_heads, slot_bytes] with strides in bytes.
+ * Slot layout (oscar_ascend/format.py:19-38, kernels/store_kernel.py:4-9):
+ *   K slot: [0:2] K scale fp16 LE | [2:4] K zero | [4:6] V scale | [6:8] V zero
+ *           | [8:32] pad (never written) | [32:32+D/4] K codes (4 per byte, low index in low bits)
+ *   V slot: [0:D/4] V codes
+ *
+ * Indices read from device memory (slot_mapping, block tables, owner tags)
+ * are bounds-checked inside the kernels: an out-of-range index skips the
+ * access and latches a device error flag that oscar_device_error() reads.
+ */
+#ifndef OSCAR_B200_H
+#define OSCAR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { OSCAR_OK = 0, OSCAR_ERR_INVALID = 1, OSCAR_ERR_UNSUPPORTED = 2, OSCAR_ERR_CUDA = 3 };
+enum { OSCAR_DTYPE_F32 = 0, OSCAR_DTYPE_BF16 = 1, OSCAR_DTYPE_F16 = 2 };
+
+/* ABI version of this header (bumped on any signature change). */
+int oscar_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* oscar_last_error(void);
+
+/* Number of kernels this library has launched in this process (all devices). */
+uint64_t oscar_launch_count(void);
+
+/* Synchronises `stream`, returns and clears the device-side bounds flag of the
+ * current device: 0 = clean, otherwise a bitmask (1 = slot out of range,
+ * 2 = block-table entry out of range, 8 = merge target row out of range).
+ * Debug/test helper; the hot path never synchronises. */
+int oscar_device_error(void* stream);
+
+/* ------------------------------------------------------------------------
+ * K1  INT2 store: clip -> per-vector asymmetric INT2 quantize -> pack -> scatter.
+ *
+ * Replaces kernels/store_kernel.py:54-102 (oscar_store_ref) and :247-279
+ * (oscar_store_triton); the clamp of backend.py:140-146 (_rotate_clip) is
+ * folded in (clip ratio 0 = no clamp, so with 0/0 this is oscar_store_ref).
+ * Codes and scale/zero bytes are bit-exact with the reference for identical
+ * rotated fp32 input.  slot_mapping < 0 skips the token.
+ */
+int oscar_store_int2(const float* k_rot, const float* v_rot, /* [n_tokens, num_kv_heads, head_dim] fp32 */
+                     int64_t n_tokens, int32_t num_kv_heads, int32_t head_dim,
+                     float k_clip_ratio, float v_clip_ratio,
+                     uint8_t* k_cache, uint8_t* v_cache, int64_t num_blocks, int32_t block_size,
+                     int64_t k_stride_block, int64_t k_stride_token, int64_t k_stride_head,
+                     int64_t v_stride_block, int64_t v_stride_token, int64_t v_stride_head,
+                     const int64_t* slot_mapping, /* [n_tokens] */
+                     void* stream);
+
+/* ------------------------------------------------------------------------
+ * K5  FP32 sink/recent staging window.
+ *
+ * oscar_staging_invalidate replaces the owner invalidation of
+ * backend.py:172-176 (do_kv_cache_update): owner[seat(slot)] = -1 for every
+ * slot >= 0, seat = (slot / block_size % stage_rows, slot % block_size).
+ *
+ * oscar_staging_write replaces backend.py:513-555 (_staging_write): for every
+ * seat written this call the LAST token (in token order) wins; its owner tag
+ * becomes slot / block_size if the token is inside the sink or recent window
+ * (pos < sink_eff || pos >= seq - recent) else -1, and kept tokens store
+ * their rotated, UNCLIPPED fp32 K/V in the arena.  Token t belongs to request
+ * r with qsl[r] <= t < qsl[r+1]; its position is seqs[r] - qsl[r+1] + t.
+ * `seat_winner` is caller-owned scratch of stage_rows*block_size uint64,
+ * zeroed once; `epoch` must increase by one per call on the same arena
+ * (first call: 1).  The scratch is never cleared between calls.
+ */
+int oscar_staging_invalidate(const int64_t* slot_mapping, int64_t n_tokens,
+                             int64_t* owner, int64_t stage_rows, int32_t block_size,
+                             void* stream);
+
+int oscar_staging_write(const float* k_rot, const float* v_rot, /* [n_tokens, num_kv_heads, head_dim] */
+                        int64_t n_tokens, int32_t num_kv_heads, int32_t head_dim,
+                        const int64_t* slot_mapping,           /* [n_tokens] */
+                        const int32_t* qsl, const int32_t* seqs, int32_t num_requests, /* device [B+1], [B] */
+                        int32_t sink_eff, int32_t recent_tokens,
+                        float* stage_k, float* stage_v, int64_t* owner, /* [rows, bs, Hk, D], [rows, bs] */
+                        int64_t stage_rows, int32_t block_size,
+                        uint64_t* seat_winner, uint32_t epoch,
+                        void* stream);
+
+/* ------------------------------------------------------------------------
+ * K2/K3/K4  streaming attention over paged INT2 history.
+ *
+ * Replaces kernels/slab_attention.py:376-476 (slab_attention) -- semantics of
+ * kernels/streaming_attention.py:134-196 (streaming_attention_ref): exact
+ * softmax attention of q over [history from the packed cache, with fp32
+ * staged overrides where owner[seat] == block] followed by the current chunk
+ * (k_new/v_new, causal, right-aligned).  History values are rounded to fp16
+ * and then to the query dtype before use (streaming_attention.py:124).
+ * Without k_new (cache-only), request r's keys are [0, seqs[r]) and query i
+ * of the request sees keys [0, seqs[r] - q_len + i].
+ *
+ * q        [n_tokens, num_q_heads, head_dim] (dtype: BF16 or F16)
+ * k_new/v_new [n_tokens, num_kv_heads, head_dim] same dtype, or both NULL
+ * block_table [bt_rows, bt_stride] int32 (kernel-granular block ids)
+ * qsl/seqs HOST int32 arrays [num_requests + 1] / [num_requests]
+ * stage_k/stage_v/owner: staging arena or all NULL (stage_rows = 0)
+ * out      [n_tokens, num_q_heads, head_dim] fp32 (rotated space)
+ * lse      [n_tokens, num_q_heads] fp32, natural log, scale included
+ * workspace: device scratch for split-KV partials; any size (0 included)
+ *   is valid -- a small workspace only lowers parallelism.  The planned
+ *   size for full parallelism is oscar_slab_attention_workspace().
+ */
+int oscar_slab_attention(const void* q, const void* k_new, const void* v_new, int32_t dtype,
+                         int64_t n_tokens, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                         const uint8_t* k_cache, const uint8_t* v_cache, int64_t num_blocks, int32_t block_size,
+                         int64_t k_stride_block, int64_t k_stride_token, int64_t k_stride_head,
+                         int64_t v_stride_block, int64_t v_stride_token, int64_t v_stride_head,
+                         const int32_t* block_table, int64_t bt_rows, int64_t bt_stride,
+                         const int32_t* qsl, const int32_t* seqs, int32_t num_requests,
+                         float scale,
+                         const float* stage_k, const float* stage_v, const int64_t* owner, int64_t stage_rows,
+                         float* out, float* lse,
+                         void* workspace, int64_t workspace_bytes,
+                         void* stream);
+
+/* Workspace bytes the planner would use for full split-KV parallelism. */
+int64_t oscar_slab_attention_workspace(const int32_t* qsl, const int32_t* seqs, int32_t num_requests,
+                                       int32_t has_new, int32_t num_q_heads, int32_t num_kv_heads,
+                                       int32_t head_dim);
+
+/* ------------------------------------------------------------------------
+ * K4  LSE merge of a partial (O, LSE) into a running (O, LSE), in place.
+ *
+ * Replaces kernels/slab_attention.py:341-373 (merge_slab) / :156-194
+ * (_merge_slab): m = max(l1, l2); a = e^(l1-m), b = e^(l2-m);
+ * O = (a*O1 + b*O2) / (a+b); LSE = m + log(a+b).  -inf partials contribute
+ * nothing (their O is never read), a zero denominator becomes 1, NaN
+ * propagates.  Target rows: query_start + i, or query_ids[i] if non-NULL.
+ * Also the combine step for split-KV sequence shards across GPUs.
+ * out/lse hold out_rows query rows; ids outside [0, out_rows) are skipped
+ * and latch device error bit 8.
+ */
+int oscar_merge_slab(float* out, float* lse, int64_t out_rows, /* [out_rows, num_q_heads, head_dim], [out_rows, num_q_heads] */
+                     const void* part, int32_t part_dtype,  /* [n, num_q_heads, head_dim] */
+                     const float* part_lse,                 /* [n, num_q_heads] */
+                     int64_t n, int32_t num_q_heads, int32_t head_dim,
+                     int64_t query_start, const int32_t* query_ids,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OSCAR_B200_H */

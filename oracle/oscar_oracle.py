@@ -186,6 +186,11 @@ def store(k_rot, v_rot, k8, v8, slot_mapping) -> None:
     kp, ks, kz = quantize(k_rot)
     vp, vs, vz = quantize(v_rot)
     meta = np.concatenate([f16_bytes(ks), f16_bytes(kz), f16_bytes(vs), f16_bytes(vz)], -1)
+    if np.unique(slots).size == slots.size:
+        k8[blk, off, :, 0:META_BYTES] = meta
+        k8[blk, off, :, K_IDX_OFF : K_IDX_OFF + db] = kp
+        v8[blk, off, :, 0:db] = vp
+        return
     # index_put_ with duplicate slots: the last occurrence wins on the CPU path.
     for i in range(slots.size):
         k8[blk[i], off[i], :, 0:META_BYTES] = meta[i]

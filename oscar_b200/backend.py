@@ -1,0 +1,317 @@
+"""OSCAR INT2 FULL-attention implementation for vLLM on B200.
+
+Drop-in for oscar_ascend/backend.py:96-572 (AscendOscarAttentionBackendImpl):
+the plugin swaps ``layer.impl.__class__`` to a subclass of the impl's own
+class with :class:`OscarAttentionImplMixin` in front (see plugin.py), so only
+``forward`` / ``do_kv_cache_update`` and the OSCAR store / staging / read
+paths change.  Everything on the device runs in the CUDA kernels of
+``csrc/`` through :mod:`oscar_b200.kernels`; the rotations are plain cuBLAS
+GEMMs.  There is no dense-history path and no CPU fallback.
+"""
+from __future__ import annotations
+
+from itertools import pairwise
+
+import numpy as np
+import torch
+
+from . import kernels
+from .config import OscarConfig
+from .format import K_IDX_OFF, VALUES_PER_BYTE, check_d
+from .rotation import get_layer_rotation
+
+
+def metadata_batch_lists(attn_metadata) -> tuple[list, list]:
+    """Host (query_start_loc, seq_lens) lists (backend.py:26-56).
+
+    Host-side fields are preferred so the hot path never reads device
+    metadata; a device tensor is only converted when nothing else exists."""
+
+    def _as_list(x, name: str) -> list:
+        if x is None:
+            raise RuntimeError(f"attn_metadata.{name} is missing")
+        if hasattr(x, "tolist"):
+            return x.tolist()
+        return list(x)
+
+    q_sl_cpu = getattr(attn_metadata, "query_start_loc_cpu", None)
+    ends = getattr(attn_metadata, "actual_seq_lengths_q", None)
+    if q_sl_cpu is not None:
+        qsl = _as_list(q_sl_cpu, "query_start_loc_cpu")
+    elif ends is not None:
+        qsl = [0] + _as_list(ends, "actual_seq_lengths_q")
+    else:
+        qsl = _as_list(attn_metadata.query_start_loc, "query_start_loc")
+    seq_cpu = getattr(attn_metadata, "seq_lens_cpu", None)
+    if seq_cpu is None:
+        seq_cpu = getattr(attn_metadata, "_seq_lens_cpu", None)
+    seq_list = getattr(attn_metadata, "seq_lens_list", None)
+    seqs = _as_list(seq_list if seq_list is not None else (seq_cpu if seq_cpu is not None else attn_metadata.seq_lens),
+                    "seq_lens")
+    return qsl, seqs
+
+
+def block_table_of(attn_metadata) -> torch.Tensor:
+    """vLLM-Ascend names it ``block_tables``, vLLM-CUDA ``block_table``."""
+    bt = getattr(attn_metadata, "block_tables", None)
+    if bt is None:
+        bt = getattr(attn_metadata, "block_table", None)
+    if bt is None:
+        raise RuntimeError("attn_metadata has no block table")
+    return bt
+
+
+def _device_ints(values, device) -> torch.Tensor:
+    t = torch.from_numpy(np.asarray(values, dtype=np.int32))
+    if device.type == "cuda":
+        return t.pin_memory().to(device, non_blocking=True)
+    return t.to(device)
+
+
+class OscarAttentionImplMixin:
+    """The OSCAR read/write/window paths.  Placed first in the MRO of a
+    subclass of the running vLLM attention impl (plugin.install_impl)."""
+
+    # ------------------------------------------------------------------ setup
+    def _oscar_setup(self) -> None:
+        """backend.py:100-123."""
+        if getattr(self, "_oscar_cfg", None) is not None:
+            return
+        cfg = OscarConfig.from_env(head_dim=self.head_size)
+        check_d(cfg.head_dim)
+        if self.num_heads % self.num_kv_heads:
+            raise ValueError("OSCAR requires Hq divisible by Hk")
+        self._oscar_cfg = cfg
+        self._oscar_stage_ready = False
+        self._oscar_stats = {"writes": 0, "kv_bytes_written": 0, "reads": 0}
+        if cfg.verbose:
+            print(f"[oscar-b200] OSCAR active: D={self.head_size} Hq={self.num_heads} Hk={self.num_kv_heads} "
+                  f"slot=160B (K 96B + V 64B) K-rot={'loaded' if cfg.k_rotation_path else 'identity'} "
+                  f"V-rot={'loaded' if cfg.v_rotation_path else 'identity'} "
+                  f"window(sink={cfg.sink_tokens}, recent={cfg.recent_tokens}) clip={cfg.k_clip_ratio}/{cfg.v_clip_ratio}")
+
+    @property
+    def _oscar(self) -> OscarConfig:
+        return self._oscar_cfg
+
+    # ------------------------------------------------------------------ caches / rotations
+    def _set_caches(self, kv_cache) -> None:
+        """backend.py:200-236: bind (K, V) caches and check the slot geometry once."""
+        if isinstance(kv_cache, (tuple, list)) and len(kv_cache) >= 2:
+            self.key_cache, self.value_cache = kv_cache[0], kv_cache[1]
+        elif isinstance(kv_cache, torch.Tensor) and kv_cache.dim() > 0:
+            self.key_cache, self.value_cache = kv_cache[0], kv_cache[1]
+        if getattr(self, "key_cache", None) is None or getattr(self, "value_cache", None) is None:
+            raise ValueError("OSCAR: KV cache is not bound")
+        if not getattr(self, "_oscar_geo_ok", False):
+            k8 = self.key_cache.view(torch.uint8)
+            v8 = self.value_cache.view(torch.uint8)
+            if k8.ndim != 4 or v8.ndim != 4 or not k8.is_contiguous() or not v8.is_contiguous():
+                raise ValueError("OSCAR requires contiguous [blocks, tokens, heads, bytes] caches")
+            slot_k, slot_v = int(k8.stride(2)), int(v8.stride(2))
+            need_k = K_IDX_OFF + self.head_size // VALUES_PER_BYTE
+            need_v = self.head_size // VALUES_PER_BYTE
+            if slot_k not in (self.head_size, 2 * self.head_size):
+                raise ValueError(f"OSCAR geometry: K slot of {slot_k} B (expected {self.head_size} packed or "
+                                 f"{2 * self.head_size} legacy)")
+            if need_k > slot_k or need_v > slot_v:
+                raise ValueError(f"OSCAR geometry: K needs {need_k} B / V {need_v} B, slots are {slot_k}/{slot_v} B")
+            self._oscar_geo_ok = True
+
+    def _layer_rots(self, layer, device):
+        """backend.py:238-246: per-layer (R_k, R_v), loaded once, strict."""
+        rots = getattr(layer, "_oscar_rots", None)
+        if not rots:
+            cfg = self._oscar
+            rk = get_layer_rotation(cfg.k_rotation_path, layer.layer_name, self.head_size, device, mode="k", strict=True)
+            rv = get_layer_rotation(cfg.v_rotation_path, layer.layer_name, self.head_size, device, mode="v", strict=True)
+            layer._oscar_rots = (rk, rv)
+            rots = layer._oscar_rots
+        rk, rv = rots
+        if rk.device != device:
+            rk, rv = rk.to(device), rv.to(device)
+            layer._oscar_rots = (rk, rv)
+        return rk, rv
+
+    def _rotate(self, x: torch.Tensor, rot: torch.Tensor) -> torch.Tensor:
+        """x @ R in fp32 (plain library GEMM), [N, H, D] -> fp32 [N, H, D]."""
+        n, h, d = x.shape
+        return torch.matmul(x.reshape(n * h, d).float(), rot).view(n, h, d)
+
+    # ------------------------------------------------------------------ write path
+    def _store(self, layer, key, value, slot_mapping, *, invalidate: bool):
+        n = slot_mapping.shape[0]
+        hk, d = self.num_kv_heads, self.head_size
+        k = key[:n].reshape(n, hk, d)
+        v = value[:n].reshape(n, hk, d)
+        if invalidate and getattr(layer, "_oscar_stage_ready", False):
+            kernels.staging_invalidate(slot_mapping, layer._oscar_slot_owner, self.stage_block)
+        rk, rv = self._layer_rots(layer, k.device)
+        k_rot, v_rot = self._rotate(k, rk), self._rotate(v, rv)
+        kernels.oscar_store(k_rot, v_rot, self.key_cache, self.value_cache, slot_mapping,
+                            self._oscar.k_clip_ratio, self._oscar.v_clip_ratio)
+        self._oscar_stats["writes"] += 1
+        self._oscar_stats["kv_bytes_written"] += n * hk * 160
+        return k_rot, v_rot
+
+    def do_kv_cache_update(self, layer, key, value, kv_cache, slot_mapping) -> None:
+        """backend.py:151-198: owner invalidation -> rotate -> clip/INT2 store."""
+        if key is None or value is None:
+            return
+        slot_mapping = slot_mapping.to(device=key.device, dtype=torch.int64)
+        if slot_mapping.shape[0] <= 0:
+            return
+        self._set_caches(kv_cache)
+        self._store(layer, key, value, slot_mapping, invalidate=True)
+
+    # ------------------------------------------------------------------ staging window
+    def _ensure_staging(self, layer, kv_cache) -> None:
+        """backend.py:492-511."""
+        if getattr(layer, "_oscar_stage_ready", False):
+            return
+        bs = self.key_cache.shape[1]
+        cfg = self._oscar
+        self.stage_block = bs
+        self.sink_eff = (cfg.sink_tokens // bs) * bs
+        self.sink_pages = self.sink_eff // bs
+        self.tail_pages = (cfg.recent_tokens + bs - 1) // bs + 1
+        rows = max((cfg.staging_tokens + bs - 1) // bs, self.sink_pages + self.tail_pages + 2)
+        dev = self.key_cache.device
+        layer._oscar_stage_k = torch.zeros(rows, bs, self.num_kv_heads, self.head_size, dtype=torch.float32, device=dev)
+        layer._oscar_stage_v = torch.zeros_like(layer._oscar_stage_k)
+        layer._oscar_slot_owner = torch.full((rows, bs), -1, dtype=torch.int64, device=dev)
+        layer._oscar_seat_winner = torch.zeros(rows * bs, dtype=torch.int64, device=dev)
+        layer._oscar_stage_epoch = 0
+        layer._oscar_stage_rows = rows
+        layer._oscar_stage_ready = True
+        self._oscar_stage_ready = True
+
+    def _staging_write(self, layer, key, value, attn_metadata, rotated=None) -> None:
+        """backend.py:513-555: last writer per seat; kept rows store rotated
+        unclipped fp32.  ``rotated`` reuses the store path's x @ R."""
+        n = attn_metadata.num_actual_tokens
+        if n == 0:
+            return
+        dev = key.device
+        slot = attn_metadata.slot_mapping[:n].to(device=dev, dtype=torch.int64)
+        qsl, seqs = metadata_batch_lists(attn_metadata)
+        if rotated is None:
+            rk, rv = self._layer_rots(layer, dev)
+            hk, d = self.num_kv_heads, self.head_size
+            rotated = (self._rotate(key[:n].reshape(n, hk, d), rk), self._rotate(value[:n].reshape(n, hk, d), rv))
+        k_rot, v_rot = rotated
+        layer._oscar_stage_epoch += 1
+        kernels.staging_write(k_rot, v_rot, slot, _device_ints(qsl, dev), _device_ints(seqs[: len(qsl) - 1], dev),
+                              self.sink_eff, self._oscar.recent_tokens, layer._oscar_stage_k, layer._oscar_stage_v,
+                              layer._oscar_slot_owner, layer._oscar_seat_winner, layer._oscar_stage_epoch)
+
+    def _stage(self, layer):
+        if self._oscar.window_enabled and getattr(self, "_oscar_stage_ready", False) and \
+                getattr(layer, "_oscar_stage_ready", False):
+            return layer._oscar_stage_k, layer._oscar_stage_v, layer._oscar_slot_owner
+        return None
+
+    # ------------------------------------------------------------------ main entry
+    def forward(self, layer, query, key, value, kv_cache, attn_metadata, output=None, output_scale=None,
+                output_block_scale=None):
+        """backend.py:249-282 (streaming mode)."""
+        if output is None:
+            raise ValueError("Output tensor must be provided.")
+        if output_scale is not None or output_block_scale is not None:
+            raise NotImplementedError("OSCAR fused output quantization is unsupported")
+        if attn_metadata is None:
+            return output.fill_(0)
+        self._set_caches(kv_cache)
+        if key is not None and value is not None:
+            n = attn_metadata.num_actual_tokens
+            slots = attn_metadata.slot_mapping[:n].to(device=key.device, dtype=torch.int64)
+            rotated = None
+            if slots.shape[0] > 0:
+                rotated = self._store(layer, key, value, slots, invalidate=not self._oscar.window_enabled)
+            if self._oscar.window_enabled:
+                self._ensure_staging(layer, kv_cache)
+                self._staging_write(layer, key, value, attn_metadata, rotated=rotated)
+        return self._streaming_attention(layer, query, key, value, kv_cache, attn_metadata, output)
+
+    def _streaming_attention(self, layer, query, key, value, kv_cache, metadata, output):
+        """backend.py:334-393: prefix-free requests attend their own chunk in
+        the model's domain; cached requests go through the rotated INT2 path."""
+        if (key is None) != (value is None):
+            raise ValueError("Both new K and V must be supplied together")
+        actual = min(query.shape[0], metadata.num_actual_tokens)
+        out_rows = output.view(output.shape[0], -1)
+        if actual == 0:
+            return output.zero_()
+        starts, seqs = metadata_batch_lists(metadata)
+        starts = [min(x, actual) for x in starts]
+        covered = starts[-1]
+        if covered < out_rows.shape[0]:
+            out_rows[covered:].zero_()
+        active = [i for i, (a, b) in enumerate(pairwise(starts)) if b > a]
+        fresh_only = [i for i in active if key is not None and seqs[i] == starts[i + 1] - starts[i]]
+        fresh_set = set(fresh_only)
+        cached = [i for i in active if i not in fresh_set]
+        table = block_table_of(metadata)
+        hq, hk, d = self.num_heads, self.num_kv_heads, self.head_size
+        q_all = query[:actual].view(actual, hq, d)
+        k_all = None if key is None else key[:actual].view(actual, hk, d)
+        v_all = None if value is None else value[:actual].view(actual, hk, d)
+        for group, rotate in ((fresh_only, False), (cached, True)):
+            if not group:
+                continue
+            if len(group) == len(active):
+                # the whole batch takes this path: no gather, inactive requests are skipped by the kernel
+                ids, sub_starts, sub_seqs, sub_table = None, starts, seqs[: len(starts) - 1], table
+                q_in = q_all[:covered]
+                k_in = None if k_all is None else k_all[:covered]
+                v_in = None if v_all is None else v_all[:covered]
+            else:
+                tok = [t for i in group for t in range(starts[i], starts[i + 1])]
+                ids = torch.as_tensor(tok, device=query.device)
+                lengths = [starts[i + 1] - starts[i] for i in group]
+                sub_starts = [0]
+                for length in lengths:
+                    sub_starts.append(sub_starts[-1] + length)
+                sub_seqs = [seqs[i] for i in group]
+                sub_table = table[torch.as_tensor(group, device=table.device)]
+                q_in = q_all[ids]
+                k_in = None if k_all is None else k_all[ids]
+                v_in = None if v_all is None else v_all[ids]
+            if rotate:
+                rk, rv = self._layer_rots(layer, query.device)
+                q_in = self._rotate(q_in, rk).to(query.dtype)
+                k_in = None if k_in is None else self._rotate(k_in, rk).to(query.dtype)
+                v_in = None if v_in is None else self._rotate(v_in, rv).to(query.dtype)
+                stage = self._stage(layer)
+            else:
+                stage = None
+            out, _ = kernels.slab_attention(q_in, k_in, v_in, self.key_cache, self.value_cache, sub_table, sub_starts,
+                                            sub_seqs, self.scale, stage,
+                                            workspace_bytes=self._oscar.stream_workspace_bytes)
+            if rotate:
+                m = out.shape[0]
+                out = torch.matmul(out.view(m * hq, d), rv.t()).view(m, hq, d)
+            result = out.to(output.dtype).view(out.shape[0], hq * d)
+            if ids is None:
+                out_rows[: result.shape[0]].copy_(result)
+            else:
+                out_rows[ids] = result
+        return output
+
+
+class OscarAttentionBackendImpl(OscarAttentionImplMixin):
+    """Stand-alone impl (no vLLM base class) used by tests, probes and the bench:
+    construct with ``OscarAttentionBackendImpl.create(num_heads, num_kv_heads, head_size, scale)``."""
+
+    @classmethod
+    def create(cls, num_heads: int, num_kv_heads: int, head_size: int, scale: float | None = None):
+        impl = cls.__new__(cls)
+        impl.num_heads, impl.num_kv_heads, impl.head_size = num_heads, num_kv_heads, head_size
+        impl.scale = head_size**-0.5 if scale is None else scale
+        impl.key_cache = impl.value_cache = None
+        impl._oscar_setup()
+        return impl
+
+
+# the reference's class name, for code that imports it by name
+AscendOscarAttentionBackendImpl = OscarAttentionBackendImpl

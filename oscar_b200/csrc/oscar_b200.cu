@@ -1,0 +1,463 @@
+// C ABI of the B200-native OSCAR INT2 KV-cache hot path (declarations and
+// contracts: include/oscar_b200.h).  One translation unit; kernels live in the
+// included headers.
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include "../../include/oscar_b200.h"
+#include "attention.cuh"
+#include "store.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_status(const char* what, int launches = 1) {
+  g_launches.fetch_add((uint64_t)launches, std::memory_order_relaxed);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(OSCAR_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return OSCAR_OK;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+};
+
+DeviceInfo& device_info() {
+  static thread_local int cached_dev = -1;
+  static thread_local DeviceInfo info;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != cached_dev) {
+    cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, dev);
+    cached_dev = dev;
+  }
+  return info;
+}
+
+inline int clip_index(float ratio, int d) {
+  if (!(ratio > 0.0f)) return -1;
+  // backend.py:141-143: idx = min(int(ratio * D), D - 1), computed in double like Python
+  const double prod = (double)ratio * (double)d;
+  const int idx = (int)prod;
+  return std::min(idx, d - 1);
+}
+
+}  // namespace
+
+extern "C" {
+
+int oscar_abi_version(void) { return 1; }
+
+const char* oscar_last_error(void) { return g_last_error.c_str(); }
+
+uint64_t oscar_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int oscar_device_error(void* stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(s) != cudaSuccess) return -fail(OSCAR_ERR_CUDA, "stream sync failed");
+  unsigned int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, oscar::g_bounds_error, sizeof(v)) != cudaSuccess) return -OSCAR_ERR_CUDA;
+  cudaMemcpyToSymbol(oscar::g_bounds_error, &zero, sizeof(zero));
+  return (int)v;
+}
+
+// ---------------------------------------------------------------------------
+int oscar_store_int2(const float* k_rot, const float* v_rot, int64_t n_tokens, int32_t num_kv_heads,
+                     int32_t head_dim, float k_clip_ratio, float v_clip_ratio, uint8_t* k_cache,
+                     uint8_t* v_cache, int64_t num_blocks, int32_t block_size, int64_t k_stride_block,
+                     int64_t k_stride_token, int64_t k_stride_head, int64_t v_stride_block,
+                     int64_t v_stride_token, int64_t v_stride_head, const int64_t* slot_mapping, void* stream) {
+  if (n_tokens < 0 || num_kv_heads < 1 || block_size < 1 || num_blocks < 0)
+    return fail(OSCAR_ERR_INVALID, "store: invalid geometry");
+  if (head_dim % 4 != 0 || head_dim / 4 > 64 || head_dim < 4)
+    return fail(OSCAR_ERR_INVALID, "store: D=%d must be a multiple of 4 and at most 256", head_dim);
+  if (!(k_clip_ratio >= 0.0f && k_clip_ratio <= 1.0f && v_clip_ratio >= 0.0f && v_clip_ratio <= 1.0f))
+    return fail(OSCAR_ERR_INVALID, "store: clip ratios must be in [0, 1]");
+  if (k_stride_head < 32 + head_dim / 4 || v_stride_head < head_dim / 4)
+    return fail(OSCAR_ERR_INVALID, "store: slot of %lld/%lld bytes cannot hold the K (%d B) / V (%d B) layout",
+                (long long)k_stride_head, (long long)v_stride_head, 32 + head_dim / 4, head_dim / 4);
+  if (n_tokens == 0) return OSCAR_OK;
+  if (!k_rot || !v_rot || !k_cache || !v_cache || !slot_mapping) return fail(OSCAR_ERR_INVALID, "store: null pointer");
+  if ((reinterpret_cast<uintptr_t>(k_rot) | reinterpret_cast<uintptr_t>(v_rot)) & 15)
+    return fail(OSCAR_ERR_INVALID, "store: k_rot/v_rot must be 16-byte aligned");
+  oscar::StoreGeom g{k_cache, v_cache, num_blocks, block_size, k_stride_block, k_stride_token, k_stride_head,
+                     v_stride_block, v_stride_token, v_stride_head};
+  const int kidx = clip_index(k_clip_ratio, head_dim), vidx = clip_index(v_clip_ratio, head_dim);
+  const int64_t vecs = n_tokens * num_kv_heads;
+  const int64_t blocks = std::min<int64_t>((vecs + 7) / 8, (int64_t)device_info().sms * 32);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int grid = (int)std::max<int64_t>(blocks, 1);
+  if (head_dim > 128)
+    oscar::store_int2_kernel<2><<<grid, 256, 0, s>>>(k_rot, v_rot, n_tokens, num_kv_heads, head_dim, kidx, vidx, g,
+                                                      slot_mapping);
+  else
+    oscar::store_int2_kernel<1><<<grid, 256, 0, s>>>(k_rot, v_rot, n_tokens, num_kv_heads, head_dim, kidx, vidx, g,
+                                                      slot_mapping);
+  return cuda_status("store_int2_kernel");
+}
+
+int oscar_staging_invalidate(const int64_t* slot_mapping, int64_t n_tokens, int64_t* owner, int64_t stage_rows,
+                             int32_t block_size, void* stream) {
+  if (n_tokens < 0 || stage_rows < 1 || block_size < 1) return fail(OSCAR_ERR_INVALID, "staging: invalid geometry");
+  if (n_tokens == 0) return OSCAR_OK;
+  if (!slot_mapping || !owner) return fail(OSCAR_ERR_INVALID, "staging: null pointer");
+  const int grid = (int)std::min<int64_t>((n_tokens + 255) / 256, 4096);
+  oscar::staging_invalidate_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      slot_mapping, n_tokens, owner, stage_rows, block_size);
+  return cuda_status("staging_invalidate_kernel");
+}
+
+int oscar_staging_write(const float* k_rot, const float* v_rot, int64_t n_tokens, int32_t num_kv_heads,
+                        int32_t head_dim, const int64_t* slot_mapping, const int32_t* qsl, const int32_t* seqs,
+                        int32_t num_requests, int32_t sink_eff, int32_t recent_tokens, float* stage_k,
+                        float* stage_v, int64_t* owner, int64_t stage_rows, int32_t block_size,
+                        uint64_t* seat_winner, uint32_t epoch, void* stream) {
+  if (n_tokens < 0 || num_kv_heads < 1 || head_dim < 4 || head_dim % 4 || stage_rows < 1 || block_size < 1 ||
+      num_requests < 0 || n_tokens >= (int64_t)0xffffffffLL)
+    return fail(OSCAR_ERR_INVALID, "staging: invalid geometry");
+  if (epoch == 0) return fail(OSCAR_ERR_INVALID, "staging: epoch must start at 1");
+  if (n_tokens == 0) return OSCAR_OK;
+  if (!k_rot || !v_rot || !slot_mapping || !stage_k || !stage_v || !owner || !seat_winner ||
+      (num_requests > 0 && (!qsl || !seqs)))
+    return fail(OSCAR_ERR_INVALID, "staging: null pointer");
+  if ((reinterpret_cast<uintptr_t>(k_rot) | reinterpret_cast<uintptr_t>(v_rot) | reinterpret_cast<uintptr_t>(stage_k) |
+       reinterpret_cast<uintptr_t>(stage_v)) & 15)
+    return fail(OSCAR_ERR_INVALID, "staging: fp32 arrays must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int grid1 = (int)std::min<int64_t>((n_tokens + 255) / 256, 4096);
+  oscar::staging_winner_kernel<<<grid1, 256, 0, s>>>(slot_mapping, n_tokens, stage_rows, block_size,
+                                                      reinterpret_cast<unsigned long long*>(seat_winner), epoch);
+  const int grid2 = (int)std::min<int64_t>((n_tokens + 7) / 8, (int64_t)device_info().sms * 16);
+  oscar::staging_write_kernel<<<std::max(grid2, 1), 256, 0, s>>>(
+      k_rot, v_rot, n_tokens, num_kv_heads, head_dim, slot_mapping, qsl, seqs, num_requests, sink_eff,
+      recent_tokens, stage_k, stage_v, owner, stage_rows, block_size,
+      reinterpret_cast<const unsigned long long*>(seat_winner), epoch);
+  return cuda_status("staging kernels", 2);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// attention
+
+namespace {
+
+struct ReqInfo {
+  int req, q_start, q_len, seq, prefix;
+};
+
+template <int D, typename T, int NW>
+size_t attn_smem_bytes() {
+  return (size_t)(16 * NW + 2 * oscar::kKT) * D * sizeof(T);
+}
+
+template <int D, typename T, int NW>
+int attn_ctas_per_sm() {
+  static thread_local int cached_dev = -1, cached = 1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != cached_dev) {
+    const size_t smem = attn_smem_bytes<D, T, NW>();
+    cudaFuncSetAttribute(oscar::paged_attn_kernel<D, T, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int n = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, oscar::paged_attn_kernel<D, T, NW>, NW * 32, smem) !=
+        cudaSuccess)
+      n = 1;
+    cached = std::max(n, 1);
+    cached_dev = dev;
+  }
+  return cached;
+}
+
+// Host planner: q-blocks per request, then split-KV factors so that the grid
+// covers about `target` CTAs with near-equal key tiles per CTA; the partial
+// workspace must fit `ws_bytes` (splits shrink until it does, down to 1).
+struct Planned {
+  oscar::AttnPlan plan;
+  int64_t part_bytes;
+};
+
+Planned plan_batch(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1, int rows, int group, int hk, int d,
+                   int target, int64_t ws_bytes) {
+  Planned out{};
+  oscar::AttnPlan& p = out.plan;
+  p.num_req = (int)(b1 - b0);
+  p.rows = rows;
+  p.tpb = rows / group;
+  int64_t work = 0;
+  for (size_t i = b0; i < b1; ++i) {
+    const int qb = (reqs[i].q_len + p.tpb - 1) / p.tpb;
+    const int nt = std::max(1, (reqs[i].seq + oscar::kKT - 1) / oscar::kKT);
+    work += (int64_t)qb * nt;
+  }
+  int64_t budget = std::max<int64_t>(1, (work * hk + target - 1) / std::max(target, 1));
+  for (;;) {
+    int items = 0, merge = 0, parts = 0;
+    int64_t part_bytes = 0;
+    for (size_t i = b0; i < b1; ++i) {
+      const int j = (int)(i - b0);
+      const ReqInfo& r = reqs[i];
+      const int qb = (r.q_len + p.tpb - 1) / p.tpb;
+      const int nt = std::max(1, (r.seq + oscar::kKT - 1) / oscar::kKT);
+      int s = (int)std::max<int64_t>(1, (nt + budget - 1) / budget);
+      int chunk_tiles = (nt + s - 1) / s;
+      s = (nt + chunk_tiles - 1) / chunk_tiles;
+      p.req_id[j] = r.req;
+      p.q_start[j] = r.q_start;
+      p.q_len[j] = r.q_len;
+      p.seq[j] = r.seq;
+      p.prefix[j] = r.prefix;
+      p.splits[j] = s;
+      p.chunk[j] = chunk_tiles * oscar::kKT;
+      p.item_begin[j] = items;
+      p.merge_begin[j] = merge;
+      p.part_begin[j] = parts;
+      items += qb * s;
+      if (s > 1) {
+        merge += qb;
+        parts += qb * s;
+        part_bytes += (int64_t)qb * s * hk * rows * (d + 1) * 4;
+      }
+    }
+    p.item_begin[p.num_req] = items;
+    p.merge_begin[p.num_req] = merge;
+    p.part_begin[p.num_req] = parts;
+    p.total_items = items;
+    p.total_merge_rows = merge * rows;
+    out.part_bytes = part_bytes;
+    if (part_bytes <= ws_bytes || parts == 0) break;
+    budget *= 2;
+  }
+  return out;
+}
+
+int attn_target(int d, int nw) {
+  const int sms = device_info().sms;
+  if (d == 256) return sms * (nw == 2 ? attn_ctas_per_sm<256, __nv_bfloat16, 2>() : attn_ctas_per_sm<256, __nv_bfloat16, 4>());
+  if (d == 128) return sms * (nw == 2 ? attn_ctas_per_sm<128, __nv_bfloat16, 2>() : attn_ctas_per_sm<128, __nv_bfloat16, 4>());
+  return sms * (nw == 2 ? attn_ctas_per_sm<64, __nv_bfloat16, 2>() : attn_ctas_per_sm<64, __nv_bfloat16, 4>());
+}
+
+inline int rows_for(int max_q, int group) { return ((int64_t)max_q * group <= 32 && group <= 32) ? 32 : 64; }
+
+template <int D, typename T, int NW>
+int run_attention(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs, void* workspace,
+                  int64_t ws_bytes, cudaStream_t s) {
+  constexpr int ROWS = 16 * NW;
+  const size_t smem = attn_smem_bytes<D, T, NW>();
+  attn_ctas_per_sm<D, T, NW>();  // sets the dynamic shared-memory attribute
+  const int target = attn_target(D, NW);
+  for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
+    const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
+    Planned pl = plan_batch(reqs, b0, b1, ROWS, base.group, base.hk, D, target, ws_bytes);
+    oscar::AttnArgs a = base;
+    if (pl.part_bytes > 0) {
+      const int64_t parts = pl.plan.part_begin[pl.plan.num_req];
+      a.part_o = reinterpret_cast<float*>(workspace);
+      a.part_lse = a.part_o + parts * base.hk * ROWS * D;
+    }
+    dim3 grid(pl.plan.total_items, base.hk);
+    oscar::paged_attn_kernel<D, T, NW><<<grid, NW * 32, smem, s>>>(a, pl.plan);
+    int st = cuda_status("paged_attn_kernel");
+    if (st) return st;
+    if (pl.plan.total_merge_rows > 0) {
+      dim3 mgrid(pl.plan.total_merge_rows, base.hk);
+      oscar::split_combine_kernel<D><<<mgrid, D / 4, 0, s>>>(a, pl.plan);
+      st = cuda_status("split_combine_kernel");
+      if (st) return st;
+    }
+  }
+  return OSCAR_OK;
+}
+
+template <int D, typename T>
+int dispatch_rows(const oscar::AttnArgs& a, const std::vector<ReqInfo>& reqs, int max_q, void* ws, int64_t wsb,
+                  cudaStream_t s) {
+  if (rows_for(max_q, a.group) == 32) return run_attention<D, T, 2>(a, reqs, ws, wsb, s);
+  return run_attention<D, T, 4>(a, reqs, ws, wsb, s);
+}
+
+template <int D>
+int dispatch_dtype(int dtype, const oscar::AttnArgs& a, const std::vector<ReqInfo>& reqs, int max_q, void* ws,
+                   int64_t wsb, cudaStream_t s) {
+  if (dtype == OSCAR_DTYPE_BF16) return dispatch_rows<D, __nv_bfloat16>(a, reqs, max_q, ws, wsb, s);
+  return dispatch_rows<D, __half>(a, reqs, max_q, ws, wsb, s);
+}
+
+int collect_requests(const int32_t* qsl, const int32_t* seqs, int32_t num_requests, int64_t n_tokens, bool has_new,
+                     int64_t bt_rows, int64_t bt_stride, int block_size, std::vector<ReqInfo>& reqs, int& max_q,
+                     bool& any_history) {
+  if (num_requests < 0 || !qsl || (num_requests > 0 && !seqs)) return fail(OSCAR_ERR_INVALID, "Invalid slab query layout");
+  if (qsl[0] != 0 || qsl[num_requests] != n_tokens) return fail(OSCAR_ERR_INVALID, "Invalid slab query layout");
+  if (bt_rows < num_requests) return fail(OSCAR_ERR_INVALID, "Missing request block-table rows");
+  max_q = 0;
+  any_history = false;
+  for (int r = 0; r < num_requests; ++r) {
+    const int a = qsl[r], b = qsl[r + 1], seq = seqs[r];
+    if (a > b || seq < 0 || (has_new && seq < b - a))
+      return fail(OSCAR_ERR_INVALID, "Sequence length must cover its query chunk");
+    const int prefix = has_new ? seq - (b - a) : seq;
+    if (b > a && (int64_t)((prefix + block_size - 1) / block_size) > bt_stride)
+      return fail(OSCAR_ERR_INVALID, "Block table cannot cover the history");
+    if (b > a) {
+      reqs.push_back(ReqInfo{r, a, b - a, seq, prefix});
+      max_q = std::max(max_q, b - a);
+      any_history = any_history || prefix > 0;
+    }
+  }
+  return OSCAR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int oscar_slab_attention(const void* q, const void* k_new, const void* v_new, int32_t dtype, int64_t n_tokens,
+                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, const uint8_t* k_cache,
+                         const uint8_t* v_cache, int64_t num_blocks, int32_t block_size, int64_t k_stride_block,
+                         int64_t k_stride_token, int64_t k_stride_head, int64_t v_stride_block,
+                         int64_t v_stride_token, int64_t v_stride_head, const int32_t* block_table, int64_t bt_rows,
+                         int64_t bt_stride, const int32_t* qsl, const int32_t* seqs, int32_t num_requests,
+                         float scale, const float* stage_k, const float* stage_v, const int64_t* owner,
+                         int64_t stage_rows, float* out, float* lse, void* workspace, int64_t workspace_bytes,
+                         void* stream) {
+  if (num_q_heads < 1 || num_kv_heads < 1 || num_q_heads % num_kv_heads || n_tokens < 0 || block_size < 1)
+    return fail(OSCAR_ERR_INVALID, "Invalid slab query layout");
+  if ((k_new == nullptr) != (v_new == nullptr)) return fail(OSCAR_ERR_INVALID, "Both new K and V must be supplied together");
+  if (dtype != OSCAR_DTYPE_BF16 && dtype != OSCAR_DTYPE_F16)
+    return fail(OSCAR_ERR_UNSUPPORTED, "query dtype must be bf16 or fp16");
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+    return fail(OSCAR_ERR_UNSUPPORTED, "head_dim %d: kernels exist for 64, 128, 256", head_dim);
+  const int group = num_q_heads / num_kv_heads;
+  if (group > 64) return fail(OSCAR_ERR_UNSUPPORTED, "GQA group %d > 64", group);
+  if ((stage_k == nullptr) != (owner == nullptr) || (stage_v == nullptr) != (owner == nullptr) ||
+      (owner != nullptr && stage_rows < 1))
+    return fail(OSCAR_ERR_INVALID, "Invalid streaming staging geometry");
+  const bool has_new = k_new != nullptr;
+  std::vector<ReqInfo> reqs;
+  int max_q = 0;
+  bool any_history = false;
+  int st = collect_requests(qsl, seqs, num_requests, n_tokens, has_new, bt_rows, bt_stride, block_size, reqs, max_q,
+                            any_history);
+  if (st) return st;
+  if (any_history) {
+    if (!k_cache || !v_cache || !block_table) return fail(OSCAR_ERR_INVALID, "history requires caches and a block table");
+    if (k_stride_head < 32 + head_dim / 4 || v_stride_head < head_dim / 4)
+      return fail(OSCAR_ERR_INVALID, "cache slot too small for the packed layout");
+  }
+  if (!out || !lse || (n_tokens > 0 && !q)) return fail(OSCAR_ERR_INVALID, "null output or query");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new) |
+       reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(stage_k) | reinterpret_cast<uintptr_t>(stage_v) |
+       reinterpret_cast<uintptr_t>(workspace)) & 15)
+    return fail(OSCAR_ERR_INVALID, "tensors must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // Every query row belongs to exactly one active request (qsl covers
+  // [0, n_tokens)), and every q-block writes all of its rows, so out/lse need
+  // no initialisation.
+  if (n_tokens == 0) return OSCAR_OK;
+  oscar::AttnArgs a{};
+  a.q = q;
+  a.k_new = k_new;
+  a.v_new = v_new;
+  a.hq = num_q_heads;
+  a.hk = num_kv_heads;
+  a.group = group;
+  a.kc = k_cache;
+  a.vc = v_cache;
+  a.num_blocks = num_blocks;
+  a.bs = block_size;
+  a.ksb = k_stride_block;
+  a.kst = k_stride_token;
+  a.ksh = k_stride_head;
+  a.vsb = v_stride_block;
+  a.vst = v_stride_token;
+  a.vsh = v_stride_head;
+  a.bt = block_table;
+  a.bt_stride = bt_stride;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.stage_k = stage_k;
+  a.stage_v = stage_v;
+  a.owner = owner;
+  a.stage_rows = owner ? stage_rows : 1;
+  a.out = out;
+  a.lse = lse;
+  if (reqs.empty()) return OSCAR_OK;
+  if (head_dim == 256) return dispatch_dtype<256>(dtype, a, reqs, max_q, workspace, workspace_bytes, s);
+  if (head_dim == 128) return dispatch_dtype<128>(dtype, a, reqs, max_q, workspace, workspace_bytes, s);
+  return dispatch_dtype<64>(dtype, a, reqs, max_q, workspace, workspace_bytes, s);
+}
+
+int64_t oscar_slab_attention_workspace(const int32_t* qsl, const int32_t* seqs, int32_t num_requests, int32_t has_new,
+                                       int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim) {
+  if (num_q_heads < 1 || num_kv_heads < 1 || num_q_heads % num_kv_heads || num_requests < 0 || !qsl) return -1;
+  std::vector<ReqInfo> reqs;
+  int max_q = 0;
+  bool hist = false;
+  const int64_t n = qsl[num_requests];
+  if (collect_requests(qsl, seqs, num_requests, n, has_new != 0, num_requests, INT32_MAX, 1, reqs, max_q, hist))
+    return -1;
+  const int group = num_q_heads / num_kv_heads;
+  const int rows = rows_for(max_q, group);
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256) return -1;
+  const int target = attn_target(head_dim, rows / 16);
+  int64_t worst = 0;
+  for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
+    const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
+    Planned pl = plan_batch(reqs, b0, b1, rows, group, num_kv_heads, head_dim, target, INT64_MAX);
+    worst = std::max(worst, pl.part_bytes);
+  }
+  return worst;
+}
+
+// ---------------------------------------------------------------------------
+int oscar_merge_slab(float* out, float* lse, int64_t out_rows, const void* part, int32_t part_dtype,
+                     const float* part_lse, int64_t n, int32_t num_q_heads, int32_t head_dim, int64_t query_start,
+                     const int32_t* query_ids, void* stream) {
+  if (n < 0 || num_q_heads < 1 || head_dim < 1 || query_start < 0 || out_rows < 0)
+    return fail(OSCAR_ERR_INVALID, "merge: invalid geometry");
+  if (query_ids == nullptr && query_start + n > out_rows)
+    return fail(OSCAR_ERR_INVALID, "merge: rows [%lld, %lld) exceed the %lld output rows", (long long)query_start,
+                (long long)(query_start + n), (long long)out_rows);
+  if (n == 0) return OSCAR_OK;
+  if (!out || !lse || !part || !part_lse) return fail(OSCAR_ERR_INVALID, "merge: null pointer");
+  const int64_t warps = n * num_q_heads;
+  const int grid = (int)((warps * 32 + 255) / 256);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (part_dtype) {
+    case OSCAR_DTYPE_F32:
+      oscar::merge_slab_kernel<float><<<grid, 256, 0, s>>>(out, lse, out_rows, reinterpret_cast<const float*>(part), part_lse,
+                                                             n, num_q_heads, head_dim, query_start, query_ids);
+      break;
+    case OSCAR_DTYPE_F16:
+      oscar::merge_slab_kernel<__half><<<grid, 256, 0, s>>>(out, lse, out_rows, reinterpret_cast<const __half*>(part), part_lse,
+                                                              n, num_q_heads, head_dim, query_start, query_ids);
+      break;
+    case OSCAR_DTYPE_BF16:
+      oscar::merge_slab_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+          out, lse, out_rows, reinterpret_cast<const __nv_bfloat16*>(part), part_lse, n, num_q_heads, head_dim, query_start,
+          query_ids);
+      break;
+    default:
+      return fail(OSCAR_ERR_INVALID, "merge: unknown part dtype");
+  }
+  return cuda_status("merge_slab_kernel");
+}
+
+}  // extern "C"

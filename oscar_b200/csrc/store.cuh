@@ -1,0 +1,230 @@
+// K1 INT2 store and K5 staging-window kernels.
+//
+// K1 restates kernels/store_kernel.py:54-102 (oscar_store_ref, built on
+// format.py:51-88) with the clamp of backend.py:140-146 folded in.  One warp
+// owns one (token, kv-head) vector; lane L owns code bytes L and L+32
+// (dims 4L..4L+3 and 4L+128..4L+131), so loads are float4-coalesced and each
+// code byte is produced by exactly one lane.  All arithmetic is IEEE fp32 with
+// explicit round-to-nearest intrinsics (no FMA contraction), which makes the
+// codes and fp16 scale/zero bytes bit-identical to the torch CPU reference.
+#pragma once
+
+#include "common.cuh"
+
+namespace oscar {
+
+constexpr int kMetaBytes = 8;
+constexpr int kKIdxOff = 32;
+constexpr float kScaleFloor = 6.103515625e-05f;  // 2^-14, format.py:38
+
+struct StoreGeom {
+  uint8_t* kc;
+  uint8_t* vc;
+  int64_t num_blocks;
+  int block_size;
+  int64_t ksb, kst, ksh;  // K cache strides in bytes
+  int64_t vsb, vst, vsh;  // V cache strides in bytes
+};
+
+// k-th smallest |x| (k = clip_idx, 0-based) over the warp's vector, as the
+// bit pattern descent of a lower bound: the smallest u with #{|x| <= u} > k.
+// Non-negative floats order like their uint32 bit patterns.
+template <int BPL>
+OSCAR_DEVINL float kth_abs(const float (&x)[BPL][4], const bool (&act)[BPL], int k) {
+  uint32_t a[BPL][4];
+#pragma unroll
+  for (int j = 0; j < BPL; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) a[j][e] = act[j] ? (__float_as_uint(x[j][e]) & 0x7fffffffu) : 0xffffffffu;
+  uint32_t ans = 0;
+  for (int b = 30; b >= 0; --b) {
+    uint32_t probe = ans + ((1u << b) - 1u);
+    int c = 0;
+#pragma unroll
+    for (int j = 0; j < BPL; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) c += (a[j][e] <= probe) ? 1 : 0;
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (c <= k) ans += (1u << b);
+  }
+  return __uint_as_float(ans);
+}
+
+// Quantize the warp's vector (format.quantize, format.py:67-88).
+// Returns fp16 bits of scale (low 16) and zero (high 16); writes code bytes.
+template <int BPL>
+OSCAR_DEVINL uint32_t quantize_vec(float (&x)[BPL][4], const bool (&act)[BPL], int clip_idx,
+                                   uint8_t (&code)[BPL]) {
+  if (clip_idx >= 0) {
+    const float thr = kth_abs<BPL>(x, act, clip_idx);
+#pragma unroll
+    for (int j = 0; j < BPL; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[j][e] = fminf(fmaxf(x[j][e], -thr), thr);
+  }
+  float mn = __int_as_float(0x7f800000), mx = -__int_as_float(0x7f800000);
+#pragma unroll
+  for (int j = 0; j < BPL; ++j)
+    if (act[j])
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        mn = fminf(mn, x[j][e]);
+        mx = fmaxf(mx, x[j][e]);
+      }
+  mn = warp_min(mn);
+  mx = warp_max(mx);
+  float scale = __fdiv_rn(__fsub_rn(mx, mn), 3.0f);
+  scale = (scale > kScaleFloor) ? scale : kScaleFloor;
+  const __half sh = __float2half_rn(scale);
+  const __half zh = __float2half_rn(mn);
+  const float s = __half2float(sh), z = __half2float(zh);
+#pragma unroll
+  for (int j = 0; j < BPL; ++j) {
+    uint32_t byte = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float q = floorf(__fadd_rn(__fdiv_rn(__fsub_rn(x[j][e], z), s), 0.5f));
+      q = fminf(fmaxf(q, 0.0f), 3.0f);
+      byte |= ((uint32_t)(int)q & 3u) << (2 * e);
+    }
+    code[j] = (uint8_t)byte;
+  }
+  return (uint32_t)__half_as_ushort(sh) | ((uint32_t)__half_as_ushort(zh) << 16);
+}
+
+template <int BPL>
+__global__ void __launch_bounds__(256) store_int2_kernel(const float* __restrict__ k_rot,
+                                                         const float* __restrict__ v_rot, int64_t n, int hk, int D,
+                                                         int k_clip_idx, int v_clip_idx, StoreGeom g,
+                                                         const int64_t* __restrict__ slots) {
+  const int NB = D / 4;  // code bytes per vector; BPL = code bytes per lane (1 or 2)
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t vec = warp; vec < n * hk; vec += nwarps) {
+    const int64_t tok = vec / hk;
+    const int h = (int)(vec - tok * hk);
+    const int64_t slot = slots[tok];
+    if (slot < 0) continue;
+    const int64_t blk = slot / g.block_size, off = slot - blk * g.block_size;
+    if (blk >= g.num_blocks) {
+      if (lane == 0) flag_error(1u);
+      continue;
+    }
+    float kx[BPL][4], vx[BPL][4];
+    bool act[BPL];
+#pragma unroll
+    for (int j = 0; j < BPL; ++j) {
+      const int b = lane + 32 * j;
+      act[j] = b < NB;
+      if (act[j]) {
+        const float4 a = *reinterpret_cast<const float4*>(k_rot + vec * (int64_t)D + 4 * b);
+        const float4 c = *reinterpret_cast<const float4*>(v_rot + vec * (int64_t)D + 4 * b);
+        kx[j][0] = a.x; kx[j][1] = a.y; kx[j][2] = a.z; kx[j][3] = a.w;
+        vx[j][0] = c.x; vx[j][1] = c.y; vx[j][2] = c.z; vx[j][3] = c.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) kx[j][e] = vx[j][e] = 0.0f;
+      }
+    }
+    uint8_t kcode[BPL], vcode[BPL];
+    const uint32_t kmeta = quantize_vec<BPL>(kx, act, k_clip_idx, kcode);
+    const uint32_t vmeta = quantize_vec<BPL>(vx, act, v_clip_idx, vcode);
+    uint8_t* kslot = g.kc + blk * g.ksb + off * g.kst + (int64_t)h * g.ksh;
+    uint8_t* vslot = g.vc + blk * g.vsb + off * g.vst + (int64_t)h * g.vsh;
+#pragma unroll
+    for (int j = 0; j < BPL; ++j) {
+      const int b = lane + 32 * j;
+      if (act[j]) {
+        kslot[kKIdxOff + b] = kcode[j];
+        vslot[b] = vcode[j];
+      }
+    }
+    if (lane < 4) {
+      // [0:2] K scale, [2:4] K zero, [4:6] V scale, [6:8] V zero (little endian)
+      const uint32_t m = (lane < 2) ? kmeta : vmeta;
+      const uint16_t bits = (uint16_t)((lane & 1) ? (m >> 16) : (m & 0xffffu));
+      kslot[2 * lane] = (uint8_t)(bits & 0xffu);
+      kslot[2 * lane + 1] = (uint8_t)(bits >> 8);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// K5 staging window
+
+OSCAR_DEVINL int64_t staging_seat(int64_t slot, int bs, int64_t rows, int64_t* blk_out) {
+  const int64_t blk = slot / bs;
+  *blk_out = blk;
+  return (blk % rows) * bs + (slot - blk * bs);
+}
+
+__global__ void staging_invalidate_kernel(const int64_t* __restrict__ slots, int64_t n, int64_t* __restrict__ owner,
+                                          int64_t rows, int bs) {
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t slot = slots[t];
+    if (slot < 0) continue;
+    int64_t blk;
+    owner[staging_seat(slot, bs, rows, &blk)] = -1;
+  }
+}
+
+// pass 1: the last token (largest index) of every seat wins (stable sort +
+// last-of-run in backend.py:537-544); the epoch tag makes stale entries from
+// earlier calls lose without clearing the scratch.
+__global__ void staging_winner_kernel(const int64_t* __restrict__ slots, int64_t n, int64_t rows, int bs,
+                                      unsigned long long* __restrict__ winner, uint32_t epoch) {
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t slot = slots[t];
+    if (slot < 0) continue;
+    int64_t blk;
+    const int64_t seat = staging_seat(slot, bs, rows, &blk);
+    atomicMax(winner + seat, ((unsigned long long)epoch << 32) | (unsigned long long)(uint32_t)t);
+  }
+}
+
+// pass 2: one warp per token; the winner writes the owner tag and, when the
+// token is inside the sink/recent window, its fp32 rotated K/V (backend.py:545-555).
+__global__ void __launch_bounds__(256) staging_write_kernel(
+    const float* __restrict__ k_rot, const float* __restrict__ v_rot, int64_t n, int hk, int d,
+    const int64_t* __restrict__ slots, const int32_t* __restrict__ qsl, const int32_t* __restrict__ seqs,
+    int num_req, int sink_eff, int recent, float* __restrict__ stage_k, float* __restrict__ stage_v,
+    int64_t* __restrict__ owner, int64_t rows, int bs, const unsigned long long* __restrict__ winner,
+    uint32_t epoch) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t t = warp; t < n; t += nwarps) {
+    const int64_t slot = slots[t];
+    if (slot < 0) continue;
+    int64_t blk;
+    const int64_t seat = staging_seat(slot, bs, rows, &blk);
+    const unsigned long long w = winner[seat];
+    if ((uint32_t)(w >> 32) != epoch || (uint32_t)w != (uint32_t)t) continue;
+    // request of token t: qsl[r] <= t < qsl[r+1]
+    int lo = 0, hi = num_req;  // find the last r with qsl[r] <= t
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (qsl[mid] <= t) lo = mid; else hi = mid;
+    }
+    bool keep = false;
+    if (num_req > 0 && qsl[lo] <= t && t < qsl[lo + 1]) {
+      const int64_t seq = seqs[lo];
+      const int64_t pos = seq - qsl[lo + 1] + t;
+      keep = (pos >= seq - recent) || (pos < sink_eff);
+    }
+    if (lane == 0) owner[seat] = keep ? blk : -1;
+    if (!keep) continue;
+    const int64_t row_elems = (int64_t)hk * d;
+    const float4* ks = reinterpret_cast<const float4*>(k_rot + t * row_elems);
+    const float4* vs = reinterpret_cast<const float4*>(v_rot + t * row_elems);
+    float4* kd = reinterpret_cast<float4*>(stage_k + seat * row_elems);
+    float4* vd = reinterpret_cast<float4*>(stage_v + seat * row_elems);
+    for (int64_t i = lane; i < row_elems / 4; i += 32) {
+      kd[i] = ks[i];
+      vd[i] = vs[i];
+    }
+  }
+}
+
+}  // namespace oscar

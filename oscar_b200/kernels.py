@@ -1,0 +1,244 @@
+"""Kernel-level API over the C ABI (torch tensors in, device work out).
+
+Mirrors the reference's kernel entry points for the hot path:
+  * ``oscar_store``       kernels/store_kernel.py:54-102 / :247-279 (+ clip of backend.py:140-146)
+  * ``staging_invalidate`` backend.py:172-176
+  * ``staging_write``     backend.py:513-555
+  * ``slab_attention``    kernels/slab_attention.py:376-476 (semantics of
+                          kernels/streaming_attention.py:134-196)
+  * ``merge_slab``        kernels/slab_attention.py:341-373
+
+Layout problems raise ValueError with the reference's messages; every call
+is asynchronous on the current CUDA stream and never synchronises the host.
+There is no CPU path: CPU tensors raise.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _native
+from ._native import check
+from .format import check_d
+
+DEFAULT_WORKSPACE_BYTES = 32 * 1024 * 1024
+
+_DTYPES = {torch.float32: _native.DTYPE_F32, torch.bfloat16: _native.DTYPE_BF16, torch.float16: _native.DTYPE_F16}
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if t.device.type != "cuda":
+            raise ValueError("OSCAR B200 kernels require CUDA tensors (there is no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError("all tensors must be on the same CUDA device")
+    if dev is None:
+        raise ValueError("no tensor given")
+    return dev
+
+
+def _byte_view(cache: torch.Tensor) -> torch.Tensor:
+    c8 = cache.view(torch.uint8)
+    if c8.ndim != 4 or not c8.is_contiguous():
+        raise ValueError("OSCAR requires contiguous [blocks, tokens, heads, bytes] caches")
+    return c8
+
+
+def _clip_ok(r: float) -> float:
+    r = float(r)
+    if not 0.0 <= r <= 1.0:
+        raise ValueError("OSCAR clip ratios must be finite and in [0, 1]")
+    return r
+
+
+# ---------------------------------------------------------------------------
+def oscar_store(k_rot: torch.Tensor, v_rot: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                slot_mapping: torch.Tensor, k_clip_ratio: float = 0.0, v_clip_ratio: float = 0.0) -> None:
+    """Clip, INT2-quantize, pack and scatter rotated K/V [N, Hk, D] into the
+    paged caches in place; slot < 0 is skipped.  Bit-exact with
+    oscar_store_ref for identical rotated fp32 input (clip ratios 0)."""
+    dev = _require_cuda(k_rot, v_rot, k_cache, v_cache, slot_mapping)
+    if k_rot.shape != v_rot.shape or k_rot.ndim != 3:
+        raise ValueError("k_rot/v_rot must be [N, H, D] with equal shapes")
+    n, h, d = k_rot.shape
+    check_d(d)
+    k8, v8 = _byte_view(k_cache), _byte_view(v_cache)
+    if k8.shape[:3] != v8.shape[:3] or k8.shape[2] != h:
+        raise ValueError("cache geometry does not match [N, H, D] input")
+    k_rot = k_rot.to(torch.float32).contiguous()
+    v_rot = v_rot.to(torch.float32).contiguous()
+    slots = slot_mapping.to(device=dev, dtype=torch.int64).contiguous()
+    if slots.numel() < n:
+        raise ValueError("slot_mapping shorter than the token count")
+    check(_native.lib().oscar_store_int2(
+        k_rot.data_ptr(), v_rot.data_ptr(), n, h, d, _clip_ok(k_clip_ratio), _clip_ok(v_clip_ratio),
+        k8.data_ptr(), v8.data_ptr(), k8.shape[0], k8.shape[1], *k8.stride()[:3], *v8.stride()[:3],
+        slots.data_ptr(), _stream(dev)))
+
+
+def oscar_store_ref(k_rot, v_rot, k_cache, v_cache, slot_mapping) -> None:
+    """Name-compatible alias of kernels/store_kernel.py:54 (runs on the GPU)."""
+    oscar_store(k_rot, v_rot, k_cache, v_cache, slot_mapping)
+
+
+# ---------------------------------------------------------------------------
+def staging_invalidate(slot_mapping: torch.Tensor, owner: torch.Tensor, block_size: int) -> None:
+    """owner[seat(slot)] = -1 for every slot >= 0 (backend.py:172-176)."""
+    dev = _require_cuda(slot_mapping, owner)
+    if owner.dtype != torch.int64 or owner.ndim != 2 or not owner.is_contiguous():
+        raise ValueError("owner must be a contiguous int64 [rows, block_size] tensor")
+    slots = slot_mapping.to(device=dev, dtype=torch.int64).contiguous()
+    check(_native.lib().oscar_staging_invalidate(slots.data_ptr(), slots.numel(), owner.data_ptr(),
+                                                 owner.shape[0], int(block_size), _stream(dev)))
+
+
+def staging_write(k_rot: torch.Tensor, v_rot: torch.Tensor, slot_mapping: torch.Tensor, qsl: torch.Tensor,
+                  seqs: torch.Tensor, sink_eff: int, recent_tokens: int, stage_k: torch.Tensor,
+                  stage_v: torch.Tensor, owner: torch.Tensor, seat_winner: torch.Tensor, epoch: int) -> None:
+    """Sink/recent staging write of rotated, unclipped fp32 K/V [N, Hk, D]
+    (backend.py:513-555).  qsl/seqs are device int32 tensors [B+1], [B]."""
+    dev = _require_cuda(k_rot, v_rot, slot_mapping, qsl, seqs, stage_k, stage_v, owner, seat_winner)
+    n, h, d = k_rot.shape
+    rows, bs = owner.shape
+    if stage_k.shape != (rows, bs, h, d) or stage_v.shape != stage_k.shape:
+        raise ValueError("Invalid streaming staging geometry")
+    if seat_winner.numel() != rows * bs or seat_winner.dtype != torch.int64:
+        raise ValueError("seat_winner must be int64 [rows * block_size]")
+    for t in (stage_k, stage_v, owner, seat_winner):
+        if not t.is_contiguous():
+            raise ValueError("Streaming staging tensors must be contiguous")
+    k_rot = k_rot.to(torch.float32).contiguous()
+    v_rot = v_rot.to(torch.float32).contiguous()
+    slots = slot_mapping.to(device=dev, dtype=torch.int64).contiguous()
+    qsl = qsl.to(device=dev, dtype=torch.int32).contiguous()
+    seqs = seqs.to(device=dev, dtype=torch.int32).contiguous()
+    check(_native.lib().oscar_staging_write(
+        k_rot.data_ptr(), v_rot.data_ptr(), n, h, d, slots.data_ptr(), qsl.data_ptr(), seqs.data_ptr(),
+        seqs.numel(), int(sink_eff), int(recent_tokens), stage_k.data_ptr(), stage_v.data_ptr(), owner.data_ptr(),
+        rows, bs, seat_winner.data_ptr(), int(epoch) & 0xFFFFFFFF, _stream(dev)))
+
+
+# ---------------------------------------------------------------------------
+def _validate_tensors(q, k, v, kc, vc, bt, qsl, seqs, stage):
+    """streaming_attention._validate_tensors (streaming_attention.py:32-65)."""
+    if q.ndim != 3 or kc.ndim != 4 or kc.shape != vc.shape or kc.shape[3] != q.shape[2]:
+        raise ValueError("Streaming attention requires [tokens,heads,D] queries and native 4-D caches")
+    if not kc.is_contiguous() or not vc.is_contiguous():
+        raise ValueError("Streaming caches must be contiguous")
+    if (k is None) != (v is None):
+        raise ValueError("Both new K and V must be supplied together")
+    if k is not None and (k.shape != v.shape or k.shape != (q.shape[0], kc.shape[2], q.shape[2])
+                          or k.dtype != q.dtype or v.dtype != q.dtype):
+        raise ValueError("Current K/V must match query tokens, dtype and KV geometry")
+    if bt.ndim != 2 or bt.shape[0] < len(seqs):
+        raise ValueError("Missing request block-table rows")
+    for a, b, seq in zip(qsl, qsl[1:], seqs):
+        prefix = seq - (b - a) if k is not None else seq
+        if b > a and -(-prefix // kc.shape[1]) > bt.shape[1]:
+            raise ValueError("Block table cannot cover the history")
+    if stage is not None:
+        sk, sv, owner = stage
+        shape = (owner.shape[0], kc.shape[1], kc.shape[2], q.shape[2])
+        if owner.shape != shape[:2] or sk.shape != shape or sv.shape != shape or shape[0] < 1:
+            raise ValueError("Invalid streaming staging geometry")
+        if not all(t.is_contiguous() for t in stage):
+            raise ValueError("Streaming staging tensors must be contiguous")
+
+
+def slab_attention(q, k_new, v_new, kc, vc, table, qsl, seqs, scale, stage=None, *,
+                   workspace_bytes: int = DEFAULT_WORKSPACE_BYTES, chunk_tokens: int | None = None):
+    """Exact attention of rotated queries over paged INT2 history (+ staged
+    fp32 overrides) and the causal current chunk.  Returns (out [n, Hq, D]
+    fp32, lse [n, Hq] fp32 natural log).  ``qsl``/``seqs`` are host lists.
+
+    ``workspace_bytes`` bounds the split-KV partial buffer (any value is valid;
+    smaller only lowers parallelism).  ``chunk_tokens`` is accepted for
+    signature compatibility: the fused kernel never materialises a slab."""
+    del chunk_tokens
+    qsl = [int(x) for x in qsl]
+    seqs = [int(x) for x in seqs]
+    if (q.ndim != 3 or kc.ndim != 4 or q.shape[1] < 1 or kc.shape[2] < 1 or len(qsl) != len(seqs) + 1
+            or not qsl or qsl[0] != 0 or qsl[-1] != q.shape[0] or q.shape[1] % kc.shape[2]):
+        raise ValueError("Invalid slab query layout")
+    if any(a > b or seq < 0 or (k_new is not None and seq < b - a) for a, b, seq in zip(qsl, qsl[1:], seqs)):
+        raise ValueError("Sequence length must cover its query chunk")
+    _validate_tensors(q, k_new, v_new, kc, vc, table, qsl, seqs, stage)
+    dev = _require_cuda(q, k_new, v_new, kc, vc, table, *(stage or ()))
+    out_dtype = q.dtype
+    if q.dtype == torch.float32:
+        # fp32 queries: fp16 tensor-core operands (history is fp16-exact on this path)
+        q = q.half()
+        k_new = None if k_new is None else k_new.half()
+        v_new = None if v_new is None else v_new.half()
+    if q.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"unsupported query dtype {out_dtype}")
+    n, hq, d = q.shape
+    hk = kc.shape[2]
+    q = q.contiguous()
+    k_new = None if k_new is None else k_new.contiguous()
+    v_new = None if v_new is None else v_new.contiguous()
+    table = table.to(device=dev, dtype=torch.int32).contiguous()
+    k8, v8 = _byte_view(kc), _byte_view(vc)
+    sk = sv = owner = None
+    rows = 0
+    if stage is not None:
+        sk, sv, owner = stage
+        if sk.dtype != torch.float32 or sv.dtype != torch.float32 or owner.dtype != torch.int64:
+            raise ValueError("staging arena must be fp32 K/V and int64 owner tags")
+        rows = owner.shape[0]
+    out = torch.empty(n, hq, d, dtype=torch.float32, device=dev)
+    lse = torch.empty(n, hq, dtype=torch.float32, device=dev)
+    if n == 0:
+        return out, lse
+    lib = _native.lib()
+    qsl_a = np.ascontiguousarray(qsl, dtype=np.int32)
+    seqs_a = np.ascontiguousarray(seqs, dtype=np.int32)
+    qsl_p, seqs_p = qsl_a.ctypes.data, seqs_a.ctypes.data
+    need = lib.oscar_slab_attention_workspace(qsl_p, seqs_p, len(seqs), int(k_new is not None), hq, hk, d)
+    ws_bytes = max(0, min(int(need), int(workspace_bytes)))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    dtype = _DTYPES[q.dtype]
+    check(lib.oscar_slab_attention(
+        q.data_ptr(), _ptr(k_new), _ptr(v_new), dtype, n, hq, hk, d,
+        k8.data_ptr(), v8.data_ptr(), k8.shape[0], k8.shape[1], *k8.stride()[:3], *v8.stride()[:3],
+        table.data_ptr(), table.shape[0], table.stride(0), qsl_p, seqs_p, len(seqs), float(scale),
+        _ptr(sk), _ptr(sv), _ptr(owner), rows, out.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws_bytes,
+        _stream(dev)))
+    return out, lse
+
+
+def merge_slab(output, lse, part, part_lse, start, ids) -> None:
+    """In-place LSE merge of part into output[start:start+n] (or output[ids])."""
+    dev = _require_cuda(output, lse, part, part_lse, ids)
+    n, hq, d = part.shape
+    if output.dtype != torch.float32 or lse.dtype != torch.float32 or not output.is_contiguous() or not lse.is_contiguous():
+        raise ValueError("output/lse must be contiguous fp32")
+    if part.dtype not in _DTYPES:
+        raise ValueError(f"unsupported partial dtype {part.dtype}")
+    part = part.contiguous()
+    part_lse = part_lse.to(torch.float32).contiguous()
+    ids_t = None if ids is None else ids.to(device=dev, dtype=torch.int32).contiguous()
+    if output.shape[1:] != part.shape[1:] or lse.shape != output.shape[:2] or part_lse.shape != part.shape[:2]:
+        raise ValueError("merge: output/lse/part geometry mismatch")
+    check(_native.lib().oscar_merge_slab(output.data_ptr(), lse.data_ptr(), output.shape[0], part.data_ptr(),
+                                         _DTYPES[part.dtype],
+                                         part_lse.data_ptr(), n, hq, d, int(start), _ptr(ids_t), _stream(dev)))
+
+
+def device_error(device=None) -> int:
+    """Synchronise and return/clear the kernels' bounds-violation flag (debug)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    return int(_native.lib().oscar_device_error(_stream(dev)))
