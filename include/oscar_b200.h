@@ -101,6 +101,24 @@ int oscar_staging_write(const float* k_rot, const float* v_rot, /* [n_tokens, nu
                         uint64_t* seat_winner, uint32_t epoch,
                         void* stream);
 
+/* Staging-window write for callers that cannot allocate device memory.
+ * No counterpart in the reference.  Same semantics and arguments as
+ * oscar_staging_write, minus seat_winner/epoch: the scratch is a static
+ * device array inside this library holding at most 65536 seats
+ * (stage_rows * block_size; larger arenas return OSCAR_ERR_INVALID), so an
+ * engine that has given all device memory to its KV cache, or a host that
+ * forbids allocations outside start-up, can still run the write.  Each GPU
+ * that loads the library keeps that 512 KiB for the life of the process.
+ * The first call on a device looks up the array's device address (set-up);
+ * make that first call before any stream capture.  All calls share the one
+ * array (cleared at the start of every call), so calls that overlap on the
+ * GPU -- on different streams, or from different threads -- race. */
+int oscar_staging_write_noalloc(const float* k_rot, const float* v_rot, int64_t n_tokens, int32_t num_kv_heads,
+                                int32_t head_dim, const int64_t* slot_mapping, const int32_t* qsl,
+                                const int32_t* seqs, int32_t num_requests, int32_t sink_eff, int32_t recent_tokens,
+                                float* stage_k, float* stage_v, int64_t* owner, int64_t stage_rows,
+                                int32_t block_size, void* stream);
+
 /* ------------------------------------------------------------------------
  * K2/K3/K4  streaming attention over paged INT2 history.
  *

@@ -461,3 +461,83 @@ int oscar_merge_slab(float* out, float* lse, int64_t out_rows, const void* part,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Staging-window write without caller-provided scratch.
+//
+// Some callers of this library cannot allocate device memory at the point
+// where the staging write runs (an engine whose memory planner has already
+// handed every byte to the KV cache, or a plugin host that forbids cudaMalloc
+// outside start-up).  For them the seat-winner scratch lives in the static
+// device array below, sized for kNoAllocMaxSeats staging seats; every GPU
+// that loads this library holds it (512 KiB) until the process exits.
+
+static constexpr int64_t kNoAllocMaxSeats = 65536;
+static __device__ __align__(256) unsigned long long oscar_noalloc_seat_winner[kNoAllocMaxSeats];
+
+#include <mutex>
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[256] = {};  // device address of the array, per device ordinal
+
+// Once per device, with that device current: the device address of the
+// array.  The host symbol itself is only a host-side stand-in.
+int noalloc_scratch(unsigned long long** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256)
+    return fail(OSCAR_ERR_CUDA, "staging (no-alloc): no current CUDA device");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, oscar_noalloc_seat_winner);
+    if (e != cudaSuccess || ptr == nullptr)
+      return fail(OSCAR_ERR_CUDA, "staging (no-alloc): cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = reinterpret_cast<unsigned long long*>(g_noalloc_ptr[dev]);
+  return OSCAR_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int oscar_staging_write_noalloc(const float* k_rot, const float* v_rot, int64_t n_tokens, int32_t num_kv_heads,
+                                int32_t head_dim, const int64_t* slot_mapping, const int32_t* qsl,
+                                const int32_t* seqs, int32_t num_requests, int32_t sink_eff, int32_t recent_tokens,
+                                float* stage_k, float* stage_v, int64_t* owner, int64_t stage_rows,
+                                int32_t block_size, void* stream) {
+  if (n_tokens < 0 || num_kv_heads < 1 || head_dim < 4 || head_dim % 4 || stage_rows < 1 || block_size < 1 ||
+      num_requests < 0 || n_tokens >= (int64_t)0xffffffffLL)
+    return fail(OSCAR_ERR_INVALID, "staging (no-alloc): invalid geometry");
+  if (stage_rows > kNoAllocMaxSeats / block_size)
+    return fail(OSCAR_ERR_INVALID,
+                "staging (no-alloc): %lld rows x %d block size = %lld seats exceed the built-in scratch of %lld "
+                "seats; use oscar_staging_write with caller-provided scratch",
+                (long long)stage_rows, block_size, (long long)stage_rows * block_size, (long long)kNoAllocMaxSeats);
+  if (n_tokens == 0) return OSCAR_OK;
+  if (!k_rot || !v_rot || !slot_mapping || !stage_k || !stage_v || !owner || (num_requests > 0 && (!qsl || !seqs)))
+    return fail(OSCAR_ERR_INVALID, "staging (no-alloc): null pointer");
+  if ((reinterpret_cast<uintptr_t>(k_rot) | reinterpret_cast<uintptr_t>(v_rot) | reinterpret_cast<uintptr_t>(stage_k) |
+       reinterpret_cast<uintptr_t>(stage_v)) & 15)
+    return fail(OSCAR_ERR_INVALID, "staging (no-alloc): fp32 arrays must be 16-byte aligned");
+  unsigned long long* winner = nullptr;
+  int st = noalloc_scratch(&winner);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t seats = stage_rows * block_size;
+  // The array keeps the previous call's winners; they would outrank this
+  // call's lower token indices, so the seats in use start from zero.
+  if (cudaMemsetAsync(winner, 0, (size_t)seats * sizeof(unsigned long long), s) != cudaSuccess)
+    return fail(OSCAR_ERR_CUDA, "staging (no-alloc): clearing the scratch failed");
+  const uint32_t epoch = 1;
+  const int grid1 = (int)std::min<int64_t>((n_tokens + 255) / 256, 4096);
+  oscar::staging_winner_kernel<<<grid1, 256, 0, s>>>(slot_mapping, n_tokens, stage_rows, block_size, winner, epoch);
+  const int grid2 = (int)std::min<int64_t>((n_tokens + 7) / 8, (int64_t)device_info().sms * 16);
+  oscar::staging_write_kernel<<<std::max(grid2, 1), 256, 0, s>>>(
+      k_rot, v_rot, n_tokens, num_kv_heads, head_dim, slot_mapping, qsl, seqs, num_requests, sink_eff,
+      recent_tokens, stage_k, stage_v, owner, stage_rows, block_size, winner, epoch);
+  return cuda_status("staging kernels (no-alloc)", 2);
+}
+
+}  // extern "C"
