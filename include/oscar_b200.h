@@ -46,6 +46,13 @@ const char* oscar_last_error(void);
 /* Number of kernels this library has launched in this process (all devices). */
 uint64_t oscar_launch_count(void);
 
+/* Selects the attention kernel family for later oscar_slab_attention calls
+ * in this process: 0 = automatic (the decode kernel where eligible: D = 256,
+ * at most 24 query rows per GQA group), 1 = the tile kernel only, 2 = same as
+ * 0.  Both families compute the same function; the switch keeps both
+ * parity-tested. */
+int oscar_set_attention_path(int path);
+
 /* Synchronises `stream`, returns and clears the device-side bounds flag of the
  * current device: 0 = clean, otherwise a bitmask (1 = slot out of range,
  * 2 = block-table entry out of range, 8 = merge target row out of range).

@@ -11,12 +11,14 @@
 
 #include "../../include/oscar_b200.h"
 #include "attention.cuh"
+#include "decode.cuh"
 #include "store.cuh"
 
 namespace {
 
 thread_local std::string g_last_error;
 std::atomic<uint64_t> g_launches{0};
+std::atomic<int> g_attention_path{0};  // 0 auto, 1 tile kernel only, 2 decode kernel where eligible
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -68,6 +70,12 @@ int oscar_abi_version(void) { return 1; }
 const char* oscar_last_error(void) { return g_last_error.c_str(); }
 
 uint64_t oscar_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int oscar_set_attention_path(int path) {
+  if (path < 0 || path > 2) return fail(OSCAR_ERR_INVALID, "attention path must be 0 (auto), 1 (tile) or 2 (decode)");
+  g_attention_path.store(path);
+  return OSCAR_OK;
+}
 
 int oscar_device_error(void* stream) {
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -287,6 +295,136 @@ int run_attention(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs,
   return OSCAR_OK;
 }
 
+// ---- decode / MTP path (decode.cuh): history splits, then combine with the current chunk
+constexpr int kDecodeNoFit = -100;
+
+template <typename T, int NT>
+int decode_ctas_per_sm() {
+  static thread_local int cached_dev = -1, cached = 1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != cached_dev) {
+    cudaFuncSetAttribute(oscar::decode_attn_kernel<T, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sizeof(oscar::DecSmem));
+    int n = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, oscar::decode_attn_kernel<T, NT>, 128,
+                                                      sizeof(oscar::DecSmem)) != cudaSuccess)
+      n = 1;
+    cached = std::max(n, 1);
+    cached_dev = dev;
+  }
+  return cached;
+}
+
+struct DecodePlanned {
+  oscar::AttnPlan plan;
+  int64_t part_bytes;
+  bool fits;
+};
+
+// Splits of each request's history [0, prefix) into page-aligned-free chunks
+// of whole 64-token stages so that about `target` CTAs run; every split
+// writes a partial, so the workspace must hold all of them.
+DecodePlanned plan_decode(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1, int rows, int hk, int bs,
+                          int target, int64_t ws_bytes) {
+  DecodePlanned out{};
+  oscar::AttnPlan& p = out.plan;
+  p.num_req = (int)(b1 - b0);
+  p.rows = rows;
+  p.tpb = 0;
+  const int64_t max_chunk_stages =
+      std::max<int64_t>(1, std::min<int64_t>((int64_t)(oscar::kDecMaxPages - 2) * bs / oscar::kDecStage, 1 << 20));
+  int64_t work = 0;
+  for (size_t i = b0; i < b1; ++i) work += std::max(1, (reqs[i].prefix + oscar::kDecStage - 1) / oscar::kDecStage);
+  int64_t budget = std::max<int64_t>(1, (work * hk + target - 1) / std::max(target, 1));
+  for (;;) {
+    int items = 0;
+    int64_t part_bytes = 0;
+    bool all_single = true;
+    const int64_t per = std::min<int64_t>(budget, max_chunk_stages);
+    for (size_t i = b0; i < b1; ++i) {
+      const int j = (int)(i - b0);
+      const ReqInfo& r = reqs[i];
+      const int ns = std::max(1, (r.prefix + oscar::kDecStage - 1) / oscar::kDecStage);
+      int sp = (int)((ns + per - 1) / per);
+      const int chunk_st = (ns + sp - 1) / sp;
+      sp = (ns + chunk_st - 1) / chunk_st;
+      all_single = all_single && sp == 1;
+      p.req_id[j] = r.req;
+      p.q_start[j] = r.q_start;
+      p.q_len[j] = r.q_len;
+      p.seq[j] = r.seq;
+      p.prefix[j] = r.prefix;
+      p.splits[j] = sp;
+      p.chunk[j] = chunk_st * oscar::kDecStage;
+      p.item_begin[j] = items;
+      p.part_begin[j] = items;
+      p.merge_begin[j] = 0;
+      items += sp;
+      part_bytes += (int64_t)sp * hk * rows * (256 + 1) * 4;
+    }
+    p.item_begin[p.num_req] = items;
+    p.part_begin[p.num_req] = items;
+    p.merge_begin[p.num_req] = 0;
+    p.total_items = items;
+    p.total_merge_rows = 0;
+    out.part_bytes = part_bytes;
+    out.fits = part_bytes <= ws_bytes;
+    if (out.fits || (all_single && budget >= max_chunk_stages)) break;
+    budget *= 2;
+  }
+  return out;
+}
+
+template <typename T, int NT>
+int run_decode(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs, void* workspace, int64_t ws_bytes,
+               cudaStream_t s) {
+  const int target = device_info().sms * decode_ctas_per_sm<T, NT>();
+  // plan every batch first: fall back to the tile kernel before launching anything
+  std::vector<DecodePlanned> plans;
+  for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
+    const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
+    plans.push_back(plan_decode(reqs, b0, b1, NT * 8, base.hk, base.bs, target, ws_bytes));
+    if (!plans.back().fits) return kDecodeNoFit;
+  }
+  for (const DecodePlanned& pl : plans) {
+    oscar::AttnArgs a = base;
+    const int64_t parts = pl.plan.total_items;
+    a.part_o = reinterpret_cast<float*>(workspace);
+    a.part_lse = a.part_o + parts * base.hk * (NT * 8) * 256;
+    dim3 grid(pl.plan.total_items, base.hk);
+    oscar::decode_attn_kernel<T, NT><<<grid, 128, sizeof(oscar::DecSmem), s>>>(a, pl.plan);
+    int st = cuda_status("decode_attn_kernel");
+    if (st) return st;
+    dim3 cgrid(pl.plan.num_req, base.hk);
+    oscar::decode_combine_kernel<T><<<cgrid, 256, 0, s>>>(a, pl.plan, NT * 8);
+    st = cuda_status("decode_combine_kernel");
+    if (st) return st;
+  }
+  return OSCAR_OK;
+}
+
+// The decode kernel serves D = 256 with at most 24 query rows per GQA group
+// and 16-byte aligned packed caches; everything else runs the tile kernel.
+bool decode_eligible(int head_dim, int max_rows, const oscar::AttnArgs& a) {
+  if (head_dim != 256 || max_rows > 24) return false;
+  if (a.kc == nullptr || a.vc == nullptr) return false;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(a.kc) | reinterpret_cast<uintptr_t>(a.vc) | (uintptr_t)a.ksb |
+                       (uintptr_t)a.kst | (uintptr_t)a.ksh | (uintptr_t)a.vsb | (uintptr_t)a.vst | (uintptr_t)a.vsh;
+  if (al & 15) return false;
+  if (a.ksh < 96 || a.vsh < 64) return false;
+  if (a.owner != nullptr && (reinterpret_cast<uintptr_t>(a.owner) & 7)) return false;
+  return true;
+}
+
+template <typename T>
+int run_decode_rows(const oscar::AttnArgs& a, const std::vector<ReqInfo>& reqs, int max_rows, void* ws, int64_t wsb,
+                    cudaStream_t s) {
+  if (max_rows <= 8) return run_decode<T, 1>(a, reqs, ws, wsb, s);
+  if (max_rows <= 16) return run_decode<T, 2>(a, reqs, ws, wsb, s);
+  return run_decode<T, 3>(a, reqs, ws, wsb, s);
+}
+
 template <int D, typename T>
 int dispatch_rows(const oscar::AttnArgs& a, const std::vector<ReqInfo>& reqs, int max_q, void* ws, int64_t wsb,
                   cudaStream_t s) {
@@ -297,6 +435,11 @@ int dispatch_rows(const oscar::AttnArgs& a, const std::vector<ReqInfo>& reqs, in
 template <int D>
 int dispatch_dtype(int dtype, const oscar::AttnArgs& a, const std::vector<ReqInfo>& reqs, int max_q, void* ws,
                    int64_t wsb, cudaStream_t s) {
+  if (D == 256 && g_attention_path.load() != 1 && decode_eligible(D, max_q * a.group, a)) {
+    const int st = (dtype == OSCAR_DTYPE_BF16) ? run_decode_rows<__nv_bfloat16>(a, reqs, max_q * a.group, ws, wsb, s)
+                                               : run_decode_rows<__half>(a, reqs, max_q * a.group, ws, wsb, s);
+    if (st != kDecodeNoFit) return st;
+  }
   if (dtype == OSCAR_DTYPE_BF16) return dispatch_rows<D, __nv_bfloat16>(a, reqs, max_q, ws, wsb, s);
   return dispatch_rows<D, __half>(a, reqs, max_q, ws, wsb, s);
 }
@@ -414,6 +557,20 @@ int64_t oscar_slab_attention_workspace(const int32_t* qsl, const int32_t* seqs, 
   if (collect_requests(qsl, seqs, num_requests, n, has_new != 0, num_requests, INT32_MAX, 1, reqs, max_q, hist))
     return -1;
   const int group = num_q_heads / num_kv_heads;
+  if (head_dim == 256 && max_q * group <= 24 && g_attention_path.load() != 1) {
+    const int nt = (max_q * group + 7) / 8;
+    const int per_sm = nt == 1 ? decode_ctas_per_sm<__nv_bfloat16, 1>()
+                       : nt == 2 ? decode_ctas_per_sm<__nv_bfloat16, 2>()
+                                 : decode_ctas_per_sm<__nv_bfloat16, 3>();
+    const int target = device_info().sms * per_sm;
+    int64_t worst = 0;
+    for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
+      const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
+      DecodePlanned pl = plan_decode(reqs, b0, b1, nt * 8, num_kv_heads, 1 << 20, target, INT64_MAX);
+      worst = std::max(worst, pl.part_bytes);
+    }
+    return worst;
+  }
   const int rows = rows_for(max_q, group);
   if (head_dim != 64 && head_dim != 128 && head_dim != 256) return -1;
   const int target = attn_target(head_dim, rows / 16);

@@ -238,6 +238,15 @@ def merge_slab(output, lse, part, part_lse, start, ids) -> None:
                                          part_lse.data_ptr(), n, hq, d, int(start), _ptr(ids_t), _stream(dev)))
 
 
+_PATHS = {"auto": 0, "tile": 1, "decode": 2}
+
+
+def set_attention_path(path: str) -> None:
+    """Kernel family for slab_attention: "auto"/"decode" (decode kernel where
+    eligible) or "tile" (tile kernel only).  Both compute the same function."""
+    check(_native.lib().oscar_set_attention_path(_PATHS[path]))
+
+
 def device_error(device=None) -> int:
     """Synchronise and return/clear the kernels' bounds-violation flag (debug)."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)

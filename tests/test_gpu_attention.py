@@ -11,6 +11,18 @@ from oscar_b200.synthetic import make_case
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(params=["auto", "tile"])
+def attn_path(request):
+    """Run a test under both attention kernel families (decode kernel where
+    eligible, and the general tile kernel)."""
+    from oscar_b200 import kernels
+
+    need_gpu()
+    kernels.set_attention_path(request.param)
+    yield request.param
+    kernels.set_attention_path("auto")
+
 ATTN_CASES = ["mixed_d256", "mtp_hk2_d256", "nowin_d256", "cache_only_multi", "cache_only_empty", "cached_prefill",
               "legacy_hk2_d64_f16", "hk4_d128_f16", "f32_query_d64"]
 DT = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}
@@ -25,7 +37,7 @@ def assert_attention_close(out, lse, want_out, want_lse):
 
 
 @pytest.mark.parametrize("name", ATTN_CASES)
-def test_attention_matches_reference_golden(golden, name):
+def test_attention_matches_reference_golden(golden, name, attn_path):
     from oscar_b200 import kernels
 
     dev = need_gpu()
@@ -62,7 +74,7 @@ SYNTH = [
 
 
 @pytest.mark.parametrize("prefixes,lengths,opts", SYNTH)
-def test_attention_matches_oracle_on_synthetic_cases(prefixes, lengths, opts):
+def test_attention_matches_oracle_on_synthetic_cases(prefixes, lengths, opts, attn_path):
     from oscar_b200 import kernels
 
     dev = need_gpu()
@@ -75,7 +87,7 @@ def test_attention_matches_oracle_on_synthetic_cases(prefixes, lengths, opts):
     assert_attention_close(out, lse, want_out, want_lse)
 
 
-def test_split_kv_is_invisible_and_workspace_optional():
+def test_split_kv_is_invisible_and_workspace_optional(attn_path):
     """Any workspace size (0 = no split partials) gives the oracle's answer;
     LSE is split-invariant to fp32 rounding (P.V rounds P to fp16 per split)."""
     from oscar_b200 import kernels
@@ -93,7 +105,7 @@ def test_split_kv_is_invisible_and_workspace_optional():
         torch.testing.assert_close(l, full_lse, atol=2e-5, rtol=2e-5)
 
 
-def test_full_size_24k_mtp_matches_oracle():
+def test_full_size_24k_mtp_matches_oracle(attn_path):
     """BASELINE config 2 at full size (1 x 24576 history + 4-token MTP)."""
     from oscar_b200 import kernels
 
@@ -105,7 +117,7 @@ def test_full_size_24k_mtp_matches_oracle():
     assert_attention_close(out, lse, want_out, want_lse)
 
 
-def test_empty_queries_and_nan_propagation():
+def test_empty_queries_and_nan_propagation(attn_path):
     from oscar_b200 import kernels
 
     dev = need_gpu()
@@ -157,7 +169,7 @@ def test_merge_matches_reference_edge_cases(golden, kind):
     np.testing.assert_allclose(lse.cpu().numpy(), c[f"{kind}_lse"], rtol=2e-6, atol=2e-6, equal_nan=True)
 
 
-def test_merge_of_sequence_shards_equals_whole():
+def test_merge_of_sequence_shards_equals_whole(attn_path):
     """Two split-KV sequence shards (page-aligned halves of the history, as a
     2-GPU split would hold them) merged with K4 equal one pass over all keys."""
     from oscar_b200 import kernels
