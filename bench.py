@@ -249,7 +249,7 @@ def run_gpu(args):
     ms_host_paced = timed(torch, dev, step, args.steps, dist, preroll=False)
     clk = clocks.stop()
 
-    # attention pass alone (paged attention + split combine) for the roofline
+    # attention pass alone (decode kernel + combine) for the roofline
     rot = []
     for lay in layers:
         rk, rv = lay.layer._oscar_rots
@@ -317,7 +317,7 @@ def run_gpu(args):
                 "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e / args.steps},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "kernel": "paged attention pass (paged_attn_kernel + split_combine_kernel)",
+                     "traffic": traffic, "kernel": "slab attention pass (decode_attn_kernel with its staged items + decode_combine_kernel)",
                      "launch_us": ms_attn * 1e3, "algorithmic_bytes": alg_bytes,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6650 GB/s"},
         "clocks": clk,

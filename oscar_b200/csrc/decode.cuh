@@ -17,7 +17,8 @@
 // S^T = K Q^T (tokens x rows, query dtype): thread t of a quad owns dims
 // [64t, 64t+64) of its two tokens; k-chunk c pairs dims 64t+4c+{0,1} and
 // 64t+4c+{2,3}; the Q^T fragments (registers, loaded once) follow the same
-// permutation.  Staged tokens substitute their values in the same registers.
+// permutation.  Staged tokens (owner hits) are masked here: staged_item
+// attends them from their fp32 staging rows and writes a separate partial.
 //
 // O^T = V^T P^T (dims x rows, fp16): PRMT selects same-token value pairs and
 // a second PRMT transposes two tokens' pairs into each A register (k runs over
@@ -27,7 +28,7 @@
 // 16w+2g (rows g) and 16w+2g+1 (rows g+8).
 //
 // Only history positions [0, prefix) are processed here; the causal current
-// chunk and the split-KV combine run in decode_combine_kernel.
+// chunk and the merge of all partials run in decode_combine_kernel.
 #pragma once
 
 #include "attention.cuh"
@@ -127,24 +128,285 @@ OSCAR_DEVINL uint2 make_vlut(float s, float z) {
   return lut_from(pack2<__half>(v[0], v[1]), pack2<__half>(v[2], v[3]));
 }
 
-template <typename T>
-OSCAR_DEVINL uint32_t staged_k_pair(const float* p) {
-  const float2 f = *reinterpret_cast<const float2*>(p);
-  return pack2<T>(chain<T>(f.x), chain<T>(f.y));
-}
-template <typename T>
-OSCAR_DEVINL uint32_t staged_v_pair(const float* p) {
-  const float2 f = *reinterpret_cast<const float2*>(p);
-  return pack2<__half>(chain_f16<T>(f.x), chain_f16<T>(f.y));
+// ---------------------------------------------------------------------------
+// Staged tokens.  A history position is staged when its staging seat is owned
+// by its block: owner[(blk % rows) * bs + off] == blk (backend.py:172-176);
+// it then attends with T(fp16(x)) of its fp32 staging rows instead of its
+// INT2 codes (streaming_attention.py:116-124).  The decode CTAs mask staged
+// positions; one staged item per history split lists them in position order,
+// gathers 16 at a time with cp.async (double-buffered) and writes its own
+// normalised partial (O, LSE), or LSE = -inf when its split holds none.
+constexpr int kStWin = 512;      // positions listed per window
+constexpr int kStGroup = 16;     // staged tokens per MMA group
+constexpr int kStKStride = 264;  // floats per staged K row (conflict-free A-fragment loads)
+constexpr int kStVStride = 260;  // floats per staged V row
+
+struct StagedSmem {
+  float k[2][kStGroup][kStKStride];
+  float v[2][kStGroup][kStVStride];
+  int seat[kStWin];
+  int pos[kStWin];
+  float red[4][kStGroup][25];  // per-warp partial S^T [token][row]
+  __half pt[24][24];           // P [row][token]
+  float alpha[24];
+  float lsum[24];
+  float mrow[24];
+  int wsum[4];
+};
+
+template <typename T, int NT>
+OSCAR_DEVINL void staged_item(const AttnArgs& a, const AttnPlan& p, int item, uint8_t* smem_raw) {
+  constexpr int D = 256;
+  StagedSmem& sm = *reinterpret_cast<StagedSmem*>(smem_raw);
+  const int h = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int ri = find_bucket(p.item_begin, p.num_req, item);
+  const int sp = item - p.item_begin[ri];
+  const int req = p.req_id[ri];
+  const int q_start = p.q_start[ri], qlen = p.q_len[ri], seq = p.seq[ri], prefix = p.prefix[ri];
+  const int G = a.group;
+  const int R = qlen * G;
+  const int lo = sp * p.chunk[ri];
+  const int hi = min(lo + p.chunk[ri], prefix);
+  const int bs = a.bs;
+  const int rows_mod = (int)a.stage_rows;
+
+  // Q^T fragments of this warp's dims [64w, 64w + 64): chunk c covers 64w + 16c + [0, 16)
+  uint32_t qf[4][NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int row = 8 * nt + g;
+    const bool ok = row < R;
+    const T* qrow = reinterpret_cast<const T*>(a.q) +
+                    ((int64_t)(q_start + (ok ? row / G : 0)) * a.hq + (int64_t)h * G + (ok ? row % G : 0)) * D;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int k0 = 64 * warp + 16 * c + 2 * t;
+      qf[c][nt][0] = ok ? *reinterpret_cast<const uint32_t*>(qrow + k0) : 0u;
+      qf[c][nt][1] = ok ? *reinterpret_cast<const uint32_t*>(qrow + k0 + 8) : 0u;
+    }
+  }
+
+  // softmax state: threads 4r .. 4r+3 own row r (tokens 4q .. 4q+3 of a group)
+  const int srow = tid >> 2, sq = tid & 3;
+  const bool srow_ok = srow < 8 * NT;
+  const int slim = (srow < R) ? seq - qlen + srow / G + 1 : -1;  // visible positions are < slim
+  float m_r = -INFINITY, l_r = 0.0f;
+  float o[4][NT][4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) o[e][nt][0] = o[e][nt][1] = o[e][nt][2] = o[e][nt][3] = 0.0f;
+
+  for (int w0 = lo; w0 < hi; w0 += kStWin) {
+    __syncthreads();  // the previous window's list is consumed
+    // ---- list the staged positions of [w0, w0 + kStWin), 4 consecutive ones per thread
+    int seats[4];
+    bool hit[4];
+    int cnt = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int pos = w0 + 4 * tid + j;
+      hit[j] = false;
+      seats[j] = 0;
+      if (pos < hi) {
+        const int pg = pos / bs, off = pos - pg * bs;
+        const int blk = a.bt[(int64_t)req * a.bt_stride + pg];
+        if (blk < 0 || blk >= a.num_blocks) {
+          flag_error(2u);
+        } else {
+          seats[j] = (blk % rows_mod) * bs + off;
+          hit[j] = a.owner[seats[j]] == (int64_t)blk;
+        }
+      }
+      cnt += hit[j] ? 1 : 0;
+    }
+    int incl = cnt;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += y;
+    }
+    if (lane == 31) sm.wsum[warp] = incl;
+    __syncthreads();
+    int wbase = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      wbase += (w < warp) ? sm.wsum[w] : 0;
+      total += sm.wsum[w];
+    }
+    int at = wbase + incl - cnt;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (hit[j]) {
+        sm.seat[at] = seats[j];
+        sm.pos[at] = w0 + 4 * tid + j;
+        ++at;
+      }
+    __syncthreads();
+
+    // ---- groups of 16 staged tokens
+    const int ng = (total + kStGroup - 1) / kStGroup;
+    auto issue = [&](int gi) {
+      if (gi < ng) {
+        const int buf = gi & 1;
+#pragma unroll 4
+        for (int tok = 0; tok < kStGroup; ++tok) {
+          const int li = gi * kStGroup + tok;
+          if (li < total) {
+            const int64_t rowoff = ((int64_t)sm.seat[li] * a.hk + h) * D;
+            if (tid < 64)
+              cp_async16(&sm.k[buf][tok][tid * 4], a.stage_k + rowoff + tid * 4);
+            else
+              cp_async16(&sm.v[buf][tok][(tid - 64) * 4], a.stage_v + rowoff + (tid - 64) * 4);
+          } else if (tid >= 64) {
+            *reinterpret_cast<float4*>(&sm.v[buf][tok][(tid - 64) * 4]) = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+      }
+      cp_async_commit();
+    };
+    issue(0);
+    for (int gi = 0; gi < ng; ++gi) {
+      issue(gi + 1);
+      cp_async_wait<1>();
+      __syncthreads();
+      const int buf = gi & 1;
+
+      // partial S^T = K Q^T over this warp's 64 dims
+      float sacc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int k0 = 64 * warp + 16 * c + 2 * t;
+        const float2 f0 = *reinterpret_cast<const float2*>(&sm.k[buf][g][k0]);
+        const float2 f1 = *reinterpret_cast<const float2*>(&sm.k[buf][g + 8][k0]);
+        const float2 f2 = *reinterpret_cast<const float2*>(&sm.k[buf][g][k0 + 8]);
+        const float2 f3 = *reinterpret_cast<const float2*>(&sm.k[buf][g + 8][k0 + 8]);
+        const uint32_t af[4] = {pack2<T>(chain<T>(f0.x), chain<T>(f0.y)), pack2<T>(chain<T>(f1.x), chain<T>(f1.y)),
+                                pack2<T>(chain<T>(f2.x), chain<T>(f2.y)), pack2<T>(chain<T>(f3.x), chain<T>(f3.y))};
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) Mma<T>::run(sacc[nt], af, qf[c][nt][0], qf[c][nt][1]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        sm.red[warp][g][8 * nt + 2 * t] = sacc[nt][0];
+        sm.red[warp][g][8 * nt + 2 * t + 1] = sacc[nt][1];
+        sm.red[warp][g + 8][8 * nt + 2 * t] = sacc[nt][2];
+        sm.red[warp][g + 8][8 * nt + 2 * t + 1] = sacc[nt][3];
+      }
+      __syncthreads();
+
+      // online softmax over the group, row srow, tokens 4sq .. 4sq+3
+      if (srow_ok) {
+        float x[4];
+        float gm = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int tok = 4 * sq + k, li = gi * kStGroup + tok;
+          const float sv = sm.red[0][tok][srow] + sm.red[1][tok][srow] + sm.red[2][tok][srow] + sm.red[3][tok][srow];
+          const bool valid = li < total && sm.pos[li] < slim;
+          x[k] = valid ? sv * a.scale_log2 : -INFINITY;
+          gm = fmaxf(gm, x[k]);
+        }
+        gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 1));
+        gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 2));
+        const float m_new = fmaxf(m_r, gm);
+        const float muse = (m_new == -INFINITY) ? 0.0f : m_new;
+        const float alpha = exp2f(m_r - muse);
+        float ps = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float pk = exp2f(x[k] - muse);
+          ps += pk;
+          sm.pt[srow][4 * sq + k] = __float2half_rn(pk);
+        }
+        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+        l_r = l_r * alpha + ps;
+        m_r = m_new;
+        if (sq == 0) sm.alpha[srow] = alpha;
+      }
+      __syncthreads();
+
+      // O^T += V^T P^T for this warp's dims 64w + 16e + [0, 16)
+      uint32_t bfr[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const float a0 = sm.alpha[8 * nt + 2 * t], a1 = sm.alpha[8 * nt + 2 * t + 1];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          o[e][nt][0] *= a0;
+          o[e][nt][1] *= a1;
+          o[e][nt][2] *= a0;
+          o[e][nt][3] *= a1;
+        }
+        bfr[nt][0] = *reinterpret_cast<const uint32_t*>(&sm.pt[8 * nt + g][2 * t]);
+        bfr[nt][1] = *reinterpret_cast<const uint32_t*>(&sm.pt[8 * nt + g][2 * t + 8]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d0 = 64 * warp + 16 * e + g;
+        const float(*vb)[kStVStride] = sm.v[buf];
+        const uint32_t af[4] = {
+            pack2<__half>(chain_f16<T>(vb[2 * t][d0]), chain_f16<T>(vb[2 * t + 1][d0])),
+            pack2<__half>(chain_f16<T>(vb[2 * t][d0 + 8]), chain_f16<T>(vb[2 * t + 1][d0 + 8])),
+            pack2<__half>(chain_f16<T>(vb[2 * t + 8][d0]), chain_f16<T>(vb[2 * t + 9][d0])),
+            pack2<__half>(chain_f16<T>(vb[2 * t + 8][d0 + 8]), chain_f16<T>(vb[2 * t + 9][d0 + 8]))};
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) Mma<__half>::run(o[e][nt], af, bfr[nt][0], bfr[nt][1]);
+      }
+      __syncthreads();  // buffers, red and pt are rewritten by the next group
+    }
+    cp_async_wait<0>();
+  }
+
+  // ---- epilogue: the staged partial of this split
+  __syncthreads();
+  if (srow_ok && sq == 0) {
+    sm.lsum[srow] = l_r;
+    sm.mrow[srow] = m_r;
+  }
+  __syncthreads();
+  const int64_t pslot = (int64_t)p.total_items + p.part_begin[ri] + sp;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int row = 8 * nt + 2 * t + j;
+      if (row >= R) continue;
+      const float l = sm.lsum[row];
+      if (!(l > 0.0f) && l == l) continue;  // no staged token: the combine skips this O
+      const float inv = 1.0f / l;
+      float* dst = a.part_o + ((pslot * a.hk + h) * (NT * 8) + row) * D;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        dst[64 * warp + 16 * e + g] = o[e][nt][j] * inv;
+        dst[64 * warp + 16 * e + g + 8] = o[e][nt][2 + j] * inv;
+      }
+    }
+  if (tid < R) {
+    const float l = sm.lsum[tid];
+    a.part_lse[(pslot * a.hk + h) * (NT * 8) + tid] =
+        (l > 0.0f || l != l) ? (sm.mrow[tid] + log2f(l)) * 0.69314718055994531f : -INFINITY;
+  }
 }
 
 template <typename T, int NT>
-__global__ void __launch_bounds__(128, 2) decode_attn_kernel(const AttnArgs a, const __grid_constant__ AttnPlan p) {
+__global__ void __launch_bounds__(128, 2)
+    decode_attn_kernel(const AttnArgs a, const __grid_constant__ AttnPlan p, int staged_items) {
   constexpr int D = 256;
   extern __shared__ __align__(128) uint8_t smem_raw[];
+  // the first staged_items CTAs attend the staged tokens of each split
+  if ((int)blockIdx.x < staged_items) {
+    staged_item<T, NT>(a, p, blockIdx.x, smem_raw);
+    return;
+  }
   DecSmem& sm = *reinterpret_cast<DecSmem*>(smem_raw);
 
-  const int item = blockIdx.x, h = blockIdx.y;
+  const int item = blockIdx.x - staged_items, h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int ri = find_bucket(p.item_begin, p.num_req, item);
@@ -250,28 +512,30 @@ __global__ void __launch_bounds__(128, 2) decode_attn_kernel(const AttnArgs a, c
     const int slot = st % kDecNS;
     const int base = lo + st * kDecStage;
 
-    // ---------------- per-token value tables and staged-token bitmask
+    // ---------------- per-token value tables; staged tokens (owner hits) and
+    // positions past the split get zero tables, and a bitmask marks the live ones
     {
       const int tok = tid >> 1, side = tid & 1;
       const uint8_t* mt = sm.k[slot][tok] + 4 * side;
+      const int pos = base + tok;
+      bool live = pos < hi;
+      if (live) {
+        const long long ow = sm.own[slot][tok];
+        live = !(ow >= 0 && ow == (long long)sm.btab[pos / bs - page0]);
+      }
       uint2 lut = make_uint2(0, 0);
-      if (base + tok < hi) {
+      if (live) {
         const float sc = f16_bits_to_f32(ld_u16(mt)), zr = f16_bits_to_f32(ld_u16(mt + 2));
         lut = side ? make_vlut<T>(sc, zr) : make_klut<T>(sc, zr);
       }
       if (side) sm.vlut[tok] = lut; else sm.klut[tok] = lut;
-      if (warp == 0) {
-        auto staged_at = [&](int tk) -> bool {
-          const int pos = base + tk;
-          const long long ow = sm.own[slot][tk];
-          return ow >= 0 && pos < hi && ow == (long long)sm.btab[pos / bs - page0];
-        };
-        const unsigned int b0 = __ballot_sync(0xffffffffu, staged_at(lane));
-        const unsigned int b1 = __ballot_sync(0xffffffffu, staged_at(lane + 32));
-        if (lane == 0) {
-          sm.hits[0] = b0;
-          sm.hits[1] = b1;
-        }
+      // lanes 2i and 2i+1 of a warp share token 16w + i
+      const unsigned int b = __ballot_sync(0xffffffffu, live) & 0x55555555u;
+      if (lane == 0) {
+        unsigned int m16 = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) m16 |= ((b >> (2 * i)) & 1u) << i;
+        reinterpret_cast<unsigned short*>(sm.hits)[warp] = (unsigned short)m16;
       }
     }
     __syncthreads();
@@ -286,22 +550,6 @@ __global__ void __launch_bounds__(128, 2) decode_attn_kernel(const AttnArgs a, c
       const uint2 l0 = sm.klut[tk0], l1 = sm.klut[tk1];
       const uint4 w0 = *reinterpret_cast<const uint4*>(sm.k[slot][tk0] + 32 + 16 * t);
       const uint4 w1 = *reinterpret_cast<const uint4*>(sm.k[slot][tk1] + 32 + 16 * t);
-      const unsigned int hword = (warp < 2) ? hm0 : hm1;
-      const bool st0 = (hword >> (tk0 & 31)) & 1u;
-      const bool st1 = (hword >> (tk1 & 31)) & 1u;
-      const bool any_staged = ((warp & 1) ? (hword >> 16) : (hword & 0xffffu)) != 0u;
-      const float* sk0 = nullptr;
-      const float* sk1 = nullptr;
-      if (st0) {
-        const int pos = base + tk0;
-        const int64_t blk = sm.btab[pos / bs - page0];
-        sk0 = a.stage_k + (((blk % a.stage_rows) * bs + (pos % bs)) * a.hk + h) * (int64_t)D + 64 * t;
-      }
-      if (st1) {
-        const int pos = base + tk1;
-        const int64_t blk = sm.btab[pos / bs - page0];
-        sk1 = a.stage_k + (((blk % a.stage_rows) * bs + (pos % bs)) * a.hk + h) * (int64_t)D + 64 * t;
-      }
       const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w};
       const uint32_t wb[4] = {w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
@@ -317,16 +565,6 @@ __global__ void __launch_bounds__(128, 2) decode_attn_kernel(const AttnArgs a, c
           af[2] = prmt(l0.x, l0.y, sa[2 * cc + 1]);
           af[1] = prmt(l1.x, l1.y, sb[2 * cc]);
           af[3] = prmt(l1.x, l1.y, sb[2 * cc + 1]);
-          if (any_staged) {
-            if (st0) {
-              af[0] = staged_k_pair<T>(sk0 + 4 * c);
-              af[2] = staged_k_pair<T>(sk0 + 4 * c + 2);
-            }
-            if (st1) {
-              af[1] = staged_k_pair<T>(sk1 + 4 * c);
-              af[3] = staged_k_pair<T>(sk1 + 4 * c + 2);
-            }
-          }
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) Mma<T>::run(sacc[nt], af, qf[c][nt][0], qf[c][nt][1]);
         }
@@ -334,13 +572,15 @@ __global__ void __launch_bounds__(128, 2) decode_attn_kernel(const AttnArgs a, c
     }
 
     // ---------------- mask, stage row max over the 4 warps, probabilities
+    const unsigned int hword = (warp < 2) ? hm0 : hm1;
+    const bool live0 = (hword >> (tk0 & 31)) & 1u, live1 = (hword >> (tk1 & 31)) & 1u;
     float mx[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        const float v0 = (base + tk0 < lim[nt][j]) ? sacc[nt][j] * a.scale_log2 : -INFINITY;
-        const float v1 = (base + tk1 < lim[nt][j]) ? sacc[nt][2 + j] * a.scale_log2 : -INFINITY;
+        const float v0 = (live0 && base + tk0 < lim[nt][j]) ? sacc[nt][j] * a.scale_log2 : -INFINITY;
+        const float v1 = (live1 && base + tk1 < lim[nt][j]) ? sacc[nt][2 + j] * a.scale_log2 : -INFINITY;
         sacc[nt][j] = v0;
         sacc[nt][2 + j] = v1;
         float m = fmaxf(v0, v1);
@@ -403,22 +643,6 @@ __global__ void __launch_bounds__(128, 2) decode_attn_kernel(const AttnArgs a, c
           rv[2 * hp][k] = prmt(la.x, la.y, sel[k]);
           rv[2 * hp + 1][k] = prmt(lb.x, lb.y, sel[4 + k]);
         }
-        const unsigned int hbits = (ja < 32) ? hm0 : hm1;  // ja, ja+1 share one 32-token word
-        if ((hbits >> (ja & 31)) & 3u) {
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int jt = ja + q;
-            if (!((hbits >> (jt & 31)) & 1u)) continue;
-            const int pos = base + jt;
-            const int64_t blk = sm.btab[pos / bs - page0];
-            const float* sv = a.stage_v + (((blk % a.stage_rows) * bs + (pos % bs)) * a.hk + h) * (int64_t)D +
-                              4 * (16 * warp + 2 * g);
-            rv[2 * hp + q][0] = staged_v_pair<T>(sv);
-            rv[2 * hp + q][1] = staged_v_pair<T>(sv + 2);
-            rv[2 * hp + q][2] = staged_v_pair<T>(sv + 4);
-            rv[2 * hp + q][3] = staged_v_pair<T>(sv + 6);
-          }
-        }
       }
       uint32_t bfr[NT][2];
 #pragma unroll
@@ -476,81 +700,119 @@ __global__ void __launch_bounds__(128, 2) decode_attn_kernel(const AttnArgs a, c
     }
 }
 
-// Merge the history splits of one request x kv head and attend the causal
-// current chunk (k_new/v_new), one warp per query row; lane owns dims
-// [8*lane, 8*lane+8).  Final rows go to out/lse.
+// Merge every partial of one query row -- the history splits, the staged
+// partials and the causal current chunk (k_new/v_new keys 0 .. tl) -- with
+// one thread per dim.  Final rows go to out/lse.
 template <typename T>
 __global__ void __launch_bounds__(256) decode_combine_kernel(const AttnArgs a, const __grid_constant__ AttnPlan p,
-                                                             int rows_stride) {
+                                                             int rows_stride, int staged) {
   constexpr int D = 256;
-  const int ri = blockIdx.x, h = blockIdx.y;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __shared__ float wsh[256];
+  __shared__ int64_t rsh[256];
+  __shared__ int wcnt[8];
+  __shared__ float ksc[32];
+  __shared__ float red[8];
+  const int ri = blockIdx.x;
+  const int h = blockIdx.y / rows_stride, row = blockIdx.y - (blockIdx.y / rows_stride) * rows_stride;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int q_start = p.q_start[ri], qlen = p.q_len[ri], seq = p.seq[ri], prefix = p.prefix[ri];
   const int G = a.group;
-  const int R = qlen * G;
+  if (row >= qlen * G) return;
+  const int tl = row / G, hg = row - tl * G;
+  const int64_t qrow = (int64_t)(q_start + tl) * a.hq + (int64_t)h * G + hg;
   const int S = p.splits[ri];
+  const int np = (prefix > 0) ? S * (staged ? 2 : 1) : 0;
   const int64_t pbase = p.part_begin[ri];
-  for (int row = warp; row < R; row += 8) {
-    const int tl = row / G, hg = row - (row / G) * G;
-    const int64_t qrow = (int64_t)(q_start + tl) * a.hq + (int64_t)h * G + hg;
-    float acc[8];
+  auto prow_of = [&](int i) -> int64_t {
+    const int64_t slot = (i < S) ? pbase + i : (int64_t)p.total_items + pbase + (i - S);
+    return (slot * a.hk + h) * rows_stride + row;
+  };
+  const int nkeys = (a.k_new != nullptr) ? min(seq - prefix - (qlen - 1 - tl), 32) : 0;
+
+  // current-chunk scores (natural-log units), one warp per key
+  for (int j = warp; j < nkeys; j += 8) {
+    const uint4 qu = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.q) + qrow * D + 8 * lane);
+    const uint4 ku = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) +
+                                                     ((int64_t)(q_start + j) * a.hk + h) * D + 8 * lane);
+    const T* qe = reinterpret_cast<const T*>(&qu);
+    const T* ke = reinterpret_cast<const T*>(&ku);
+    float d = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    float m = -INFINITY, l = 0.f;  // natural-log running max and weight
-    if (prefix > 0) {
-      for (int s = 0; s < S; ++s) {
-        const int64_t prow = ((pbase + s) * a.hk + h) * rows_stride + row;
-        const float ls = a.part_lse[prow];
-        if (ls == -INFINITY) continue;
-        const float mn = nan_max(m, ls);
-        const float sc_old = (m == -INFINITY) ? 0.f : expf(m - mn);
-        const float w = expf(ls - mn);
-        const float4 x0 = *reinterpret_cast<const float4*>(a.part_o + prow * D + 8 * lane);
-        const float4 x1 = *reinterpret_cast<const float4*>(a.part_o + prow * D + 8 * lane + 4);
-        const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    for (int i = 0; i < 8; ++i) d = fmaf(Elem<T>::to_f32(qe[i]), Elem<T>::to_f32(ke[i]), d);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = acc[i] * sc_old + w * xs[i];
-        l = l * sc_old + w;
-        m = mn;
-      }
-    }
-    if (a.k_new != nullptr) {
-      // current chunk: keys j = 0..tl of this request (right-aligned causal)
-      float qv[8];
-      {
-        const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.q) + qrow * D + 8 * lane);
-        const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) qv[i] = Elem<T>::to_f32(e[i]);
-      }
-      const int nkeys = seq - prefix - (qlen - 1 - tl);
-      for (int j = 0; j < nkeys; ++j) {
-        const int64_t kr = ((int64_t)(q_start + j) * a.hk + h) * D + 8 * lane;
-        const uint4 ku = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) + kr);
-        const T* ke = reinterpret_cast<const T*>(&ku);
-        float d = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) d = fmaf(qv[i], Elem<T>::to_f32(ke[i]), d);
-#pragma unroll
-        for (int o2 = 16; o2 > 0; o2 >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o2);
-        const float sc = d * a.scale_log2 * 0.69314718055994531f;
-        const float mn = nan_max(m, sc);
-        const float sc_old = (m == -INFINITY) ? 0.f : expf(m - mn);
-        const float w = expf(sc - mn);
-        const uint4 vu = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v_new) + kr);
-        const T* ve = reinterpret_cast<const T*>(&vu);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = acc[i] * sc_old + w * Elem<T>::to_f32(ve[i]);
-        l = l * sc_old + w;
-        m = mn;
-      }
-    }
-    const float den = (l > 0.f || l != l) ? l : 1.f;
-    float* dst = a.out + qrow * D + 8 * lane;
-    *reinterpret_cast<float4*>(dst) = make_float4(acc[0] / den, acc[1] / den, acc[2] / den, acc[3] / den);
-    *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4] / den, acc[5] / den, acc[6] / den, acc[7] / den);
-    if (lane == 0) a.lse[qrow] = m + logf(den);
+    for (int o2 = 16; o2 > 0; o2 >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o2);
+    if (lane == 0) ksc[j] = d * a.scale_log2 * 0.69314718055994531f;
   }
+  // global max over partial LSEs and key scores (NaN propagates)
+  float mx = -INFINITY;
+  for (int i = tid; i < np; i += 256) mx = nan_max(mx, a.part_lse[prow_of(i)]);
+  __syncthreads();
+  if (tid < nkeys) mx = nan_max(mx, ksc[tid]);
+#pragma unroll
+  for (int o2 = 16; o2 > 0; o2 >>= 1) mx = nan_max(mx, __shfl_xor_sync(0xffffffffu, mx, o2));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  float M = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) M = nan_max(M, red[w]);
+  const float Mu = (M == -INFINITY) ? 0.0f : M;
+
+  // weights of the non-empty partials, compacted in order, then a weighted
+  // sum with independent loads (empty staged partials hold no O)
+  float acc = 0.0f, L = 0.0f;
+  for (int i0 = 0; i0 < np; i0 += 256) {
+    const int i = i0 + tid;
+    float w = 0.0f;
+    int64_t prow = 0;
+    if (i < np) {
+      prow = prow_of(i);
+      const float ls = a.part_lse[prow];
+      w = (ls == -INFINITY) ? 0.0f : expf(ls - Mu);
+    }
+    const bool keep = w != 0.0f;
+    const unsigned int bal = __ballot_sync(0xffffffffu, keep);
+    __syncthreads();  // the previous batch's list is consumed
+    if (lane == 0) wcnt[warp] = __popc(bal);
+    __syncthreads();
+    int at = 0, cnt = 0;
+#pragma unroll
+    for (int w2 = 0; w2 < 8; ++w2) {
+      at += (w2 < warp) ? wcnt[w2] : 0;
+      cnt += wcnt[w2];
+    }
+    if (keep) {
+      const int k = at + __popc(bal & ((1u << lane) - 1u));
+      wsh[k] = w;
+      rsh[k] = prow;
+    }
+    __syncthreads();
+    int k = 0;
+    for (; k + 4 <= cnt; k += 4) {
+      const float x0 = a.part_o[rsh[k] * D + tid], x1 = a.part_o[rsh[k + 1] * D + tid];
+      const float x2 = a.part_o[rsh[k + 2] * D + tid], x3 = a.part_o[rsh[k + 3] * D + tid];
+      acc = fmaf(wsh[k], x0, acc);
+      acc = fmaf(wsh[k + 1], x1, acc);
+      acc = fmaf(wsh[k + 2], x2, acc);
+      acc = fmaf(wsh[k + 3], x3, acc);
+      L += wsh[k];
+      L += wsh[k + 1];
+      L += wsh[k + 2];
+      L += wsh[k + 3];
+    }
+    for (; k < cnt; ++k) {
+      acc = fmaf(wsh[k], a.part_o[rsh[k] * D + tid], acc);
+      L += wsh[k];
+    }
+  }
+  for (int j = 0; j < nkeys; ++j) {
+    const float w = expf(ksc[j] - Mu);
+    const T v = reinterpret_cast<const T*>(a.v_new)[((int64_t)(q_start + j) * a.hk + h) * D + tid];
+    acc = fmaf(w, Elem<T>::to_f32(v), acc);
+    L += w;
+  }
+  const float den = (L > 0.0f || L != L) ? L : 1.0f;
+  a.out[qrow * D + tid] = acc / den;
+  if (tid == 0) a.lse[qrow] = (M == -INFINITY) ? -INFINITY : Mu + logf(den);
 }
 
 }  // namespace oscar

@@ -298,6 +298,8 @@ int run_attention(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs,
 // ---- decode / MTP path (decode.cuh): history splits, then combine with the current chunk
 constexpr int kDecodeNoFit = -100;
 
+constexpr size_t kDecodeSmem = std::max(sizeof(oscar::DecSmem), sizeof(oscar::StagedSmem));
+
 template <typename T, int NT>
 int decode_ctas_per_sm() {
   static thread_local int cached_dev = -1, cached = 1;
@@ -305,10 +307,10 @@ int decode_ctas_per_sm() {
   cudaGetDevice(&dev);
   if (dev != cached_dev) {
     cudaFuncSetAttribute(oscar::decode_attn_kernel<T, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)sizeof(oscar::DecSmem));
+                         (int)kDecodeSmem);
     int n = 1;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, oscar::decode_attn_kernel<T, NT>, 128,
-                                                      sizeof(oscar::DecSmem)) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, oscar::decode_attn_kernel<T, NT>, 128, kDecodeSmem) !=
+        cudaSuccess)
       n = 1;
     cached = std::max(n, 1);
     cached_dev = dev;
@@ -322,11 +324,12 @@ struct DecodePlanned {
   bool fits;
 };
 
-// Splits of each request's history [0, prefix) into page-aligned-free chunks
-// of whole 64-token stages so that about `target` CTAs run; every split
-// writes a partial, so the workspace must hold all of them.
+// Splits of each request's history [0, prefix) into chunks of whole 64-token
+// stages so that about `target` CTAs run; every split writes a partial (two
+// when staging is on: the INT2 one and the staged one), so the workspace must
+// hold all of them.
 DecodePlanned plan_decode(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1, int rows, int hk, int bs,
-                          int target, int64_t ws_bytes) {
+                          int target, int64_t ws_bytes, bool staged) {
   DecodePlanned out{};
   oscar::AttnPlan& p = out.plan;
   p.num_req = (int)(b1 - b0);
@@ -361,7 +364,7 @@ DecodePlanned plan_decode(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1
       p.part_begin[j] = items;
       p.merge_begin[j] = 0;
       items += sp;
-      part_bytes += (int64_t)sp * hk * rows * (256 + 1) * 4;
+      part_bytes += (int64_t)sp * hk * rows * (256 + 1) * 4 * (staged ? 2 : 1);
     }
     p.item_begin[p.num_req] = items;
     p.part_begin[p.num_req] = items;
@@ -380,24 +383,26 @@ template <typename T, int NT>
 int run_decode(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs, void* workspace, int64_t ws_bytes,
                cudaStream_t s) {
   const int target = device_info().sms * decode_ctas_per_sm<T, NT>();
+  const bool staged = base.owner != nullptr;
   // plan every batch first: fall back to the tile kernel before launching anything
   std::vector<DecodePlanned> plans;
   for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
     const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
-    plans.push_back(plan_decode(reqs, b0, b1, NT * 8, base.hk, base.bs, target, ws_bytes));
+    plans.push_back(plan_decode(reqs, b0, b1, NT * 8, base.hk, base.bs, target, ws_bytes, staged));
     if (!plans.back().fits) return kDecodeNoFit;
   }
   for (const DecodePlanned& pl : plans) {
     oscar::AttnArgs a = base;
-    const int64_t parts = pl.plan.total_items;
+    const int64_t parts = (int64_t)pl.plan.total_items * (staged ? 2 : 1);
     a.part_o = reinterpret_cast<float*>(workspace);
     a.part_lse = a.part_o + parts * base.hk * (NT * 8) * 256;
-    dim3 grid(pl.plan.total_items, base.hk);
-    oscar::decode_attn_kernel<T, NT><<<grid, 128, sizeof(oscar::DecSmem), s>>>(a, pl.plan);
+    const int staged_items = staged ? pl.plan.total_items : 0;
+    dim3 grid(staged_items + pl.plan.total_items, base.hk);
+    oscar::decode_attn_kernel<T, NT><<<grid, 128, kDecodeSmem, s>>>(a, pl.plan, staged_items);
     int st = cuda_status("decode_attn_kernel");
     if (st) return st;
-    dim3 cgrid(pl.plan.num_req, base.hk);
-    oscar::decode_combine_kernel<T><<<cgrid, 256, 0, s>>>(a, pl.plan, NT * 8);
+    dim3 cgrid(pl.plan.num_req, base.hk * NT * 8);
+    oscar::decode_combine_kernel<T><<<cgrid, 256, 0, s>>>(a, pl.plan, NT * 8, staged ? 1 : 0);
     st = cuda_status("decode_combine_kernel");
     if (st) return st;
   }
@@ -566,7 +571,8 @@ int64_t oscar_slab_attention_workspace(const int32_t* qsl, const int32_t* seqs, 
     int64_t worst = 0;
     for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
       const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
-      DecodePlanned pl = plan_decode(reqs, b0, b1, nt * 8, num_kv_heads, 1 << 20, target, INT64_MAX);
+      // staging may be on: count the staged partials too
+      DecodePlanned pl = plan_decode(reqs, b0, b1, nt * 8, num_kv_heads, 1 << 20, target, INT64_MAX, true);
       worst = std::max(worst, pl.part_bytes);
     }
     return worst;
