@@ -146,11 +146,11 @@ struct StagedSmem {
   float v[2][kStGroup][kStVStride];
   int seat[kStWin];
   int pos[kStWin];
-  float red[4][kStGroup][25];  // per-warp partial S^T [token][row]
-  __half pt[24][24];           // P [row][token]
-  float alpha[24];
-  float lsum[24];
-  float mrow[24];
+  float red[4][kStGroup][33];  // per-warp partial S^T [token][row]
+  __half pt[32][24];           // P [row][token]
+  float alpha[32];
+  float lsum[32];
+  float mrow[32];
   int wsum[4];
 };
 
@@ -398,7 +398,7 @@ template <typename T, int NT>
 __global__ void __launch_bounds__(128, 2)
     decode_attn_kernel(const AttnArgs a, const __grid_constant__ AttnPlan p, int staged_items) {
   constexpr int D = 256;
-  extern __shared__ __align__(128) uint8_t smem_raw[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
   // the first staged_items CTAs attend the staged tokens of each split
   if ((int)blockIdx.x < staged_items) {
     staged_item<T, NT>(a, p, blockIdx.x, smem_raw);

@@ -6,19 +6,21 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 #include <string>
 #include <vector>
 
 #include "../../include/oscar_b200.h"
 #include "attention.cuh"
 #include "decode.cuh"
+#include "decode_tc.cuh"
 #include "store.cuh"
 
 namespace {
 
 thread_local std::string g_last_error;
 std::atomic<uint64_t> g_launches{0};
-std::atomic<int> g_attention_path{0};  // 0 auto, 1 tile kernel only, 2 decode kernel where eligible
+std::atomic<int> g_attention_path{0};  // 0 auto, 1 tile only, 2 mma.sync decode, 3 tensor-core decode (where eligible)
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -72,7 +74,8 @@ const char* oscar_last_error(void) { return g_last_error.c_str(); }
 uint64_t oscar_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int oscar_set_attention_path(int path) {
-  if (path < 0 || path > 2) return fail(OSCAR_ERR_INVALID, "attention path must be 0 (auto), 1 (tile) or 2 (decode)");
+  if (path < 0 || path > 3)
+    return fail(OSCAR_ERR_INVALID, "attention path must be 0 (auto), 1 (tile), 2 (decode) or 3 (tensor-core decode)");
   g_attention_path.store(path);
   return OSCAR_OK;
 }
@@ -329,16 +332,17 @@ struct DecodePlanned {
 // when staging is on: the INT2 one and the staged one), so the workspace must
 // hold all of them.
 DecodePlanned plan_decode(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1, int rows, int hk, int bs,
-                          int target, int64_t ws_bytes, bool staged) {
+                          int target, int64_t ws_bytes, bool staged, int stage = oscar::kDecStage,
+                          int max_pages = oscar::kDecMaxPages, int max_stages = 1 << 20) {
   DecodePlanned out{};
   oscar::AttnPlan& p = out.plan;
   p.num_req = (int)(b1 - b0);
   p.rows = rows;
   p.tpb = 0;
   const int64_t max_chunk_stages =
-      std::max<int64_t>(1, std::min<int64_t>((int64_t)(oscar::kDecMaxPages - 2) * bs / oscar::kDecStage, 1 << 20));
+      std::max<int64_t>(1, std::min<int64_t>((int64_t)(max_pages - 2) * bs / stage, max_stages));
   int64_t work = 0;
-  for (size_t i = b0; i < b1; ++i) work += std::max(1, (reqs[i].prefix + oscar::kDecStage - 1) / oscar::kDecStage);
+  for (size_t i = b0; i < b1; ++i) work += std::max(1, (reqs[i].prefix + stage - 1) / stage);
   int64_t budget = std::max<int64_t>(1, (work * hk + target - 1) / std::max(target, 1));
   for (;;) {
     int items = 0;
@@ -348,7 +352,7 @@ DecodePlanned plan_decode(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1
     for (size_t i = b0; i < b1; ++i) {
       const int j = (int)(i - b0);
       const ReqInfo& r = reqs[i];
-      const int ns = std::max(1, (r.prefix + oscar::kDecStage - 1) / oscar::kDecStage);
+      const int ns = std::max(1, (r.prefix + stage - 1) / stage);
       int sp = (int)((ns + per - 1) / per);
       const int chunk_st = (ns + sp - 1) / sp;
       sp = (ns + chunk_st - 1) / chunk_st;
@@ -359,7 +363,7 @@ DecodePlanned plan_decode(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1
       p.seq[j] = r.seq;
       p.prefix[j] = r.prefix;
       p.splits[j] = sp;
-      p.chunk[j] = chunk_st * oscar::kDecStage;
+      p.chunk[j] = chunk_st * stage;
       p.item_begin[j] = items;
       p.part_begin[j] = items;
       p.merge_begin[j] = 0;
@@ -430,6 +434,99 @@ int run_decode_rows(const oscar::AttnArgs& a, const std::vector<ReqInfo>& reqs, 
   return run_decode<T, 3>(a, reqs, ws, wsb, s);
 }
 
+// ---- tensor-core decode path (decode_tc.cuh)
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+// A paged cache viewed as a 2D byte matrix [num_blocks * bs tokens, token stride]
+// with boxes of `box_x` bytes x `box_y` tokens.
+bool make_cache_map(CUtensorMap* map, const uint8_t* base, int64_t num_blocks, int bs, int64_t token_stride,
+                    int box_x, int box_y) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)token_stride, (cuuint64_t)(num_blocks * bs)};
+  const cuuint64_t strides[1] = {(cuuint64_t)token_stride};
+  const cuuint32_t box[2] = {(cuuint32_t)box_x, (cuuint32_t)box_y};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The tensor-core kernel needs D = 256, at most 32 query rows per GQA group,
+// power-of-two block sizes, contiguous pages (block stride = bs x token stride)
+// and 16-byte aligned rows, heads and owner tags; TMA coordinates are int32.
+bool tc_eligible(int head_dim, int max_rows, const oscar::AttnArgs& a) {
+  if (head_dim != 256 || max_rows > oscar::kTcRows || a.kc == nullptr || a.vc == nullptr) return false;
+  if (a.bs < 8 || (a.bs & (a.bs - 1)) != 0) return false;
+  if (a.ksb != (int64_t)a.bs * a.kst || a.vsb != (int64_t)a.bs * a.vst) return false;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(a.kc) | reinterpret_cast<uintptr_t>(a.vc) | (uintptr_t)a.kst |
+                       (uintptr_t)a.ksh | (uintptr_t)a.vst | (uintptr_t)a.vsh;
+  if (al & 15) return false;
+  if (a.owner != nullptr && ((reinterpret_cast<uintptr_t>(a.owner) | reinterpret_cast<uintptr_t>(a.stage_k) |
+                              reinterpret_cast<uintptr_t>(a.stage_v)) & 15))
+    return false;  // staged rows are read as float4
+  if (a.ksh < 96 || a.vsh < 64 || a.ksh * (a.hk - 1) + 96 > a.kst || a.vsh * (a.hk - 1) + 64 > a.vst) return false;
+  if (a.num_blocks * a.bs >= ((int64_t)1 << 31) || a.kst >= ((int64_t)1 << 31)) return false;
+  if ((int64_t)(oscar::kTcMaxPages - 2) * a.bs < oscar::kTcStage) return false;
+  return encode_tiled() != nullptr;
+}
+
+template <typename T>
+int run_decode_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs, void* workspace, int64_t ws_bytes,
+                  cudaStream_t s) {
+  static thread_local int cfg_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cfg_dev != dev) {
+    cudaFuncSetAttribute(oscar::decode_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sizeof(oscar::TcSmem));
+    cfg_dev = dev;
+  }
+  // one CTA per SM; the staged tokens are attended inside the kernel
+  const int target = device_info().sms;
+  std::vector<DecodePlanned> plans;
+  for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
+    const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
+    plans.push_back(plan_decode(reqs, b0, b1, oscar::kTcRows, base.hk, base.bs, target, ws_bytes, false,
+                                oscar::kTcStage, oscar::kTcMaxPages, oscar::kTcMaxStages));
+    if (!plans.back().fits) return kDecodeNoFit;
+  }
+  CUtensorMap tmk, tmv;
+  const int box_y = std::min(base.bs, oscar::kTcStage);
+  if (!make_cache_map(&tmk, base.kc, base.num_blocks, base.bs, base.kst, 96, box_y) ||
+      !make_cache_map(&tmv, base.vc, base.num_blocks, base.bs, base.vst, 64, box_y))
+    return kDecodeNoFit;
+  for (const DecodePlanned& pl : plans) {
+    oscar::AttnArgs a = base;
+    a.part_o = reinterpret_cast<float*>(workspace);
+    a.part_lse = a.part_o + (int64_t)pl.plan.total_items * base.hk * oscar::kTcRows * 256;
+    oscar::decode_tc_kernel<T><<<dim3(pl.plan.total_items, base.hk), oscar::kTcThreads, sizeof(oscar::TcSmem), s>>>(
+        a, pl.plan, tmk, tmv);
+    int st = cuda_status("decode_tc_kernel");
+    if (st) return st;
+    oscar::decode_combine_kernel<T><<<dim3(pl.plan.num_req, base.hk * oscar::kTcRows), 256, 0, s>>>(
+        a, pl.plan, oscar::kTcRows, 0);
+    st = cuda_status("decode_combine_kernel");
+    if (st) return st;
+  }
+  return OSCAR_OK;
+}
+
 template <int D, typename T>
 int dispatch_rows(const oscar::AttnArgs& a, const std::vector<ReqInfo>& reqs, int max_q, void* ws, int64_t wsb,
                   cudaStream_t s) {
@@ -440,7 +537,13 @@ int dispatch_rows(const oscar::AttnArgs& a, const std::vector<ReqInfo>& reqs, in
 template <int D>
 int dispatch_dtype(int dtype, const oscar::AttnArgs& a, const std::vector<ReqInfo>& reqs, int max_q, void* ws,
                    int64_t wsb, cudaStream_t s) {
-  if (D == 256 && g_attention_path.load() != 1 && decode_eligible(D, max_q * a.group, a)) {
+  const int path = g_attention_path.load();
+  if (D == 256 && (path == 0 || path == 3) && tc_eligible(D, max_q * a.group, a)) {
+    const int st = (dtype == OSCAR_DTYPE_BF16) ? run_decode_tc<__nv_bfloat16>(a, reqs, ws, wsb, s)
+                                               : run_decode_tc<__half>(a, reqs, ws, wsb, s);
+    if (st != kDecodeNoFit) return st;
+  }
+  if (D == 256 && (path == 0 || path == 2) && decode_eligible(D, max_q * a.group, a)) {
     const int st = (dtype == OSCAR_DTYPE_BF16) ? run_decode_rows<__nv_bfloat16>(a, reqs, max_q * a.group, ws, wsb, s)
                                                : run_decode_rows<__half>(a, reqs, max_q * a.group, ws, wsb, s);
     if (st != kDecodeNoFit) return st;
@@ -562,25 +665,33 @@ int64_t oscar_slab_attention_workspace(const int32_t* qsl, const int32_t* seqs, 
   if (collect_requests(qsl, seqs, num_requests, n, has_new != 0, num_requests, INT32_MAX, 1, reqs, max_q, hist))
     return -1;
   const int group = num_q_heads / num_kv_heads;
-  if (head_dim == 256 && max_q * group <= 24 && g_attention_path.load() != 1) {
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256) return -1;
+  // the path is chosen at launch from the cache layout: size for every candidate
+  const int path = g_attention_path.load();
+  int64_t worst = 0;
+  if (head_dim == 256 && max_q * group <= oscar::kTcRows && (path == 0 || path == 3)) {
+    for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
+      const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
+      DecodePlanned pl = plan_decode(reqs, b0, b1, oscar::kTcRows, num_kv_heads, 1 << 20, device_info().sms,
+                                     INT64_MAX, false, oscar::kTcStage, oscar::kTcMaxPages, oscar::kTcMaxStages);
+      worst = std::max(worst, pl.part_bytes);
+    }
+  }
+  if (head_dim == 256 && max_q * group <= 24 && (path == 0 || path == 2)) {
     const int nt = (max_q * group + 7) / 8;
     const int per_sm = nt == 1 ? decode_ctas_per_sm<__nv_bfloat16, 1>()
                        : nt == 2 ? decode_ctas_per_sm<__nv_bfloat16, 2>()
                                  : decode_ctas_per_sm<__nv_bfloat16, 3>();
     const int target = device_info().sms * per_sm;
-    int64_t worst = 0;
     for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
       const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
       // staging may be on: count the staged partials too
       DecodePlanned pl = plan_decode(reqs, b0, b1, nt * 8, num_kv_heads, 1 << 20, target, INT64_MAX, true);
       worst = std::max(worst, pl.part_bytes);
     }
-    return worst;
   }
   const int rows = rows_for(max_q, group);
-  if (head_dim != 64 && head_dim != 128 && head_dim != 256) return -1;
   const int target = attn_target(head_dim, rows / 16);
-  int64_t worst = 0;
   for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
     const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
     Planned pl = plan_batch(reqs, b0, b1, rows, group, num_kv_heads, head_dim, target, INT64_MAX);

@@ -238,12 +238,15 @@ def merge_slab(output, lse, part, part_lse, start, ids) -> None:
                                          part_lse.data_ptr(), n, hq, d, int(start), _ptr(ids_t), _stream(dev)))
 
 
-_PATHS = {"auto": 0, "tile": 1, "decode": 2}
+_PATHS = {"auto": 0, "tile": 1, "decode": 2, "tensor": 3}
 
 
 def set_attention_path(path: str) -> None:
-    """Kernel family for slab_attention: "auto"/"decode" (decode kernel where
-    eligible) or "tile" (tile kernel only).  Both compute the same function."""
+    """Kernel family for slab_attention: "auto" (tensor-core decode kernel,
+    else the mma.sync decode kernel, else the tile kernel, whichever is
+    eligible first), "tensor" or "decode" (that decode kernel where eligible,
+    else the tile kernel) or "tile" (tile kernel only).  All compute the same
+    function."""
     check(_native.lib().oscar_set_attention_path(_PATHS[path]))
 
 

@@ -12,10 +12,11 @@ from oscar_b200.synthetic import make_case
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["auto", "tile"])
+@pytest.fixture(params=["auto", "decode", "tile"])
 def attn_path(request):
-    """Run a test under both attention kernel families (decode kernel where
-    eligible, and the general tile kernel)."""
+    """Run a test under every attention kernel family: "auto" (the tensor-core
+    decode kernel where eligible), the mma.sync decode kernel and the general
+    tile kernel."""
     from oscar_b200 import kernels
 
     need_gpu()
