@@ -5,32 +5,35 @@
 //   warp 8, lane 0: TMA producer and MMA issuer.  The split's INT2 history
 //     arrives in 128-token stages through a 2-slot ring: K slot bytes [0:96)
 //     and V slot bytes [0:64) of every token, one 2D tensor-map box per page.
-//   warpgroups 0 and 1 (warps 0-3, 4-7) take alternate stages (ping-pong), so
-//     one group's softmax overlaps the other's integer dequantisation; thread
-//     tok of a group owns token tok of its stage, all 256 dims.
+//   warps 0-7: thread (tok, half) = (tid % 128, tid / 128) handles dims
+//     [128 half, 128 half + 128) of token tok and query rows
+//     [16 half, 16 half + 16).  All eight warps work on the same stage (and run
+//     the same code), which keeps the instruction cache warm.
 //
 // Prologue: the split's staging owner tags are scanned into a bitmask of
 // staged positions (owner[(blk % rows) * bs + off] == blk, backend.py:172-176).
 // INT2 stages mask those positions; after them, "staged stages" attend the
 // staged positions (in position order, 128 per stage) from their fp32 rows.
 //
-// Per stage, in the group's own TMEM columns and shared tiles:
+// Per stage:
 //   K -> values T(fp16(code * scale + zero)) (streaming_attention.py:116-124)
 //     by PRMT look-up in the token's 4-entry table (staged: T(fp16(x))),
 //     written into tensor memory as the A operand (lanes = tokens, K-major).
-//   S^T = K Q^T: M = 128 tokens, N = 32 query rows, K = 256 dims; Q sits in
-//     shared memory (K-major, loaded once).
+//     A 17th k-step carries a per-token bias, 0 or -inf for masked tokens
+//     (whose K is zero), against a column of ones in Q: masking costs the
+//     softmax nothing.
+//   S^T = K Q^T: M = 128 tokens, N = 32 query rows, K = 256 dims (+16); Q sits
+//     in shared memory (K-major, loaded once).
 //   V -> fp16 values (the chain's values are fp16-exact) in a shared V^T tile
 //     (MN-major: dims contiguous per token).
-//   softmax: each thread loads its token's 32 scores from TMEM.  The group's
-//     running row maximum moves only when a score exceeds it by more than 15
-//     (log2 units): P = 2^(x - m) stays <= 2^15 in fp16, and O/l are rescaled
-//     on those stages only.  P^T goes to shared memory (MN-major).
+//   softmax: each thread loads its token's 16 scores from TMEM.  The running
+//     row maximum moves only when a score exceeds it by more than 15 (log2
+//     units): P = 2^(x - m) stays <= 2^15 in fp16, and O/l are rescaled on
+//     those stages only.  P^T goes to shared memory (MN-major).
 //   O^T += V^T P^T: two M = 128 dim halves, N = 32 rows, K = 16 tokens per
-//     instruction, accumulated in the group's TMEM across its stages.
-// Epilogue: the two groups' (m, l, O) are merged and the normalised partial
-// (O, LSE) goes to the workspace; decode_combine_kernel merges the splits with
-// the causal current chunk.
+//     instruction, accumulated in TMEM across the split.
+// The normalised partial (O, LSE) goes to the workspace;
+// decode_combine_kernel merges the splits with the causal current chunk.
 //
 // Dims inside each 16-dim group are permuted as [0,2,..,14,1,3,..,15] (the
 // order the look-up emits them); Q is loaded in the same order and the output
@@ -48,40 +51,36 @@ namespace oscar {
 
 constexpr int kTcStage = 128;
 constexpr int kTcThreads = 288;
-constexpr int kTcRows = 32;  // N of both MMAs: query rows (GQA group x MTP tokens)
-constexpr int kTcCols = 512;
-// TMEM columns of group w: A_K [256w, 256w+128) | S [256w+128, +32) | O [256w+160, +64)
-constexpr int kTcColA = 0, kTcColS = 128, kTcColO = 160;
+constexpr int kTcRows = 32;   // N of both MMAs: query rows (GQA group x MTP tokens)
+constexpr int kTcK = 272;     // QK reduction: 256 dims + the bias k-step
+constexpr int kTcCols = 256;  // TMEM columns: A_K [0,136) | S [160,192) | O [192,256)
+constexpr int kTcColA = 0, kTcColS = 160, kTcColO = 192;
 constexpr int kTcMaxStages = 64;  // INT2 stages per split (staged bitmask capacity)
 constexpr int kTcMaxWords = kTcMaxStages * kTcStage / 32;
 constexpr int kTcMaxPages = kTcMaxStages * kTcStage / 8 + 2;
-constexpr uint32_t kTcVtSbo = 2048;  // V^T / P^T: bytes between 8-element MN groups (16 token groups x 128 B)
-constexpr uint32_t kTcQSbo = 4096;   // Q: bytes between 8-row groups (32 k-groups x 128 B)
+constexpr uint32_t kTcVtSbo = 2048;          // V^T / P^T: bytes between 8-element MN groups (16 token groups x 128 B)
+constexpr uint32_t kTcQSbo = kTcK / 8 * 128;  // Q: bytes between 8-row groups (34 k-groups x 128 B)
 constexpr float kTcHeadroom = 15.0f;
 
 struct TcSmem {
   uint8_t k[2][kTcStage][96];
   uint8_t v[2][kTcStage][64];
-  uint8_t vt[2][256 * kTcStage * 2];      // V^T: address(tok, m) = (m/8)*2048 + (tok/8)*128 + (tok%8)*16 + (m%8)*2
-  uint8_t pt[2][kTcRows * kTcStage * 2];  // P^T: address(tok, n) = (n/8)*2048 + (tok/8)*128 + (tok%8)*16 + (n%8)*2
-  uint8_t qb[kTcRows * 256 * 2];          // Q:   address(n, k)   = (n/8)*4096 + (k/8)*128 + (n%8)*16 + (k%8)*2
+  uint8_t vt[256 * kTcStage * 2];      // V^T: address(tok, m) = (m/8)*2048 + (tok/8)*128 + (tok%8)*16 + (m%8)*2
+  uint8_t pt[kTcRows * kTcStage * 2];  // P^T: address(tok, n) = (n/8)*2048 + (tok/8)*128 + (tok%8)*16 + (n%8)*2
+  uint8_t qb[kTcRows * kTcK * 2];      // Q:   address(n, k)   = (n/8)*4352 + (k/8)*128 + (n%8)*16 + (k%8)*2
   int btab[kTcMaxPages];
   uint32_t smask[kTcMaxWords];  // staged positions of the split, bit (pos - lo)
   int spref[kTcMaxWords + 1];   // exclusive prefix counts of smask
   int lim[kTcRows];             // cache-only chunks: row r sees positions < lim[r]
-  int red[8][kTcRows];
-  alignas(16) float mrow[2][kTcRows];   // running row maxima of each group (log2 units), read as float4
-  alignas(16) float alpha[2][kTcRows];  // their rescale factors on the stage that moved them
-  alignas(16) float lfin[2][kTcRows];
-  unsigned long long bar_full[2], bar_empty[2], bar_k[2], bar_s[2], bar_p[2], bar_pv[2];
+  int red[8][16];
+  unsigned long long bar_full[2], bar_empty[2], bar_k, bar_s, bar_p, bar_pv;
   uint32_t tmem;
   int abort;
   int n_staged;
 };
-
-// vector accesses (uint4 / float4 / float2) and TMA / bulk destinations rely on these
+// vector accesses (uint4) and TMA destinations rely on these
 static_assert(offsetof(TcSmem, v) % 128 == 0 && offsetof(TcSmem, vt) % 16 == 0 && offsetof(TcSmem, pt) % 16 == 0 &&
-                  offsetof(TcSmem, qb) % 16 == 0 && offsetof(TcSmem, mrow) % 16 == 0 && sizeof(TcSmem) <= 227 * 1024,
+                  offsetof(TcSmem, qb) % 16 == 0 && sizeof(TcSmem) <= 227 * 1024,
               "TcSmem layout");
 
 // dim of the M/K index m (16-dim groups emitted as [0,2,..,14,1,3,..,15])
@@ -105,8 +104,16 @@ OSCAR_DEVINL void tc_lut_word(uint32_t w, uint32_t x, uint32_t y, uint32_t* r) {
 // 16 fp32 values of dims 16j..16j+15 -> 8 registers in the same permuted order,
 // through the chain T(fp16(x)) (K) or its fp16 bit pattern (V)
 template <typename T, bool kV>
-OSCAR_DEVINL void tc_pack_word(const float4& a, const float4& b, const float4& c, const float4& d, uint32_t* r) {
-  const float f[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+OSCAR_DEVINL void tc_pack_word(const float* src, bool live, uint32_t* r) {
+  float f[16];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 q = live ? *reinterpret_cast<const float4*>(src + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    f[4 * i] = q.x;
+    f[4 * i + 1] = q.y;
+    f[4 * i + 2] = q.z;
+    f[4 * i + 3] = q.w;
+  }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int d0 = (i < 4) ? 4 * i : 4 * (i - 4) + 1;  // dims (d0, d0 + 2)
@@ -122,21 +129,6 @@ OSCAR_DEVINL float tc_exp2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
   return y;
 }
-// x = S * scale (log2 units) for the 16 rows row0.. of this thread's token, masked
-OSCAR_DEVINL void tc_scores(uint32_t taddr, int row0, float scale, bool live, int R, bool need_lim, int pos,
-                            const int* lim, float (&x)[16]) {
-  uint32_t sraw[16];
-  tc::tmem_ld16(taddr, sraw);
-  tc::tmem_wait_ld();
-#pragma unroll
-  for (int r = 0; r < 16; ++r) {
-    const int row = row0 + r;
-    bool ok = live && row < R;
-    if (need_lim) ok = ok && pos < lim[row];
-    x[r] = ok ? __uint_as_float(sraw[r]) * scale : -INFINITY;
-  }
-}
-
 // order-preserving float <-> int map (for redux.sync max)
 OSCAR_DEVINL int tc_ord(float v) {
   const int k = __float_as_int(v);
@@ -204,28 +196,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int nwords = (hi > lo) ? (hi - lo + 31) >> 5 : 0;
 
   const uint32_t b_full = smem_u32(&sm.bar_full[0]), b_empty = smem_u32(&sm.bar_empty[0]);
-  const uint32_t b_k = smem_u32(&sm.bar_k[0]), b_s = smem_u32(&sm.bar_s[0]), b_p = smem_u32(&sm.bar_p[0]),
-                 b_pv = smem_u32(&sm.bar_pv[0]);
+  const uint32_t b_k = smem_u32(&sm.bar_k), b_s = smem_u32(&sm.bar_s), b_p = smem_u32(&sm.bar_p),
+                 b_pv = smem_u32(&sm.bar_pv);
   const TcWait wait{&sm.abort};
 
-  // ---------------- prologue: barriers, block-table slice, staged bitmask, Q operand, TMEM
+  // ---------------- prologue: barriers, block-table slice, Q operand, TMEM, staged bitmask
   if (tid == 0) {
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(b_full + 8 * i, 1);
-      tc::mbar_init(b_empty + 8 * i, 4);
-      tc::mbar_init(b_k + 8 * i, 4);
-      tc::mbar_init(b_s + 8 * i, 1);
-      tc::mbar_init(b_p + 8 * i, 4);
-      tc::mbar_init(b_pv + 8 * i, 1);
+      tc::mbar_init(b_empty + 8 * i, 8);
     }
+    tc::mbar_init(b_k, 8);
+    tc::mbar_init(b_s, 1);
+    tc::mbar_init(b_p, 8);
+    tc::mbar_init(b_pv, 1);
     sm.abort = 0;
     tc::mbar_fence_init();
   }
-  if (tid < kTcRows) {
-    sm.lim[tid] = tid < R ? seq - qlen + tid / G + 1 : INT_MIN;
-    sm.mrow[0][tid] = sm.mrow[1][tid] = -INFINITY;
-  }
+  if (tid < kTcRows) sm.lim[tid] = tid < R ? seq - qlen + tid / G + 1 : INT_MIN;
   for (int i = tid; i < npages; i += kTcThreads) {
     int blk = a.bt[(int64_t)req * a.bt_stride + page0 + i];
     if (blk < 0 || blk >= a.num_blocks) {
@@ -235,20 +224,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     sm.btab[i] = blk;
   }
   if (tid < 256) {
-    // Q rows n < R, 16-dim word j: k-group 2j holds dims 16j + {0,2,..,14}, 2j+1 dims 16j + {1,3,..,15}
-    for (int u = tid; u < kTcRows * 16; u += 256) {
-      const int n = u >> 4, j = u & 15;
-      uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0;
-      if (n < R) {
+    // Q rows n < R, 16-dim word j: k-group 2j holds dims 16j + {0,2,..,14}, 2j+1 dims 16j + {1,3,..,15};
+    // k-groups 32, 33 hold the bias column: 1 at k = 256, zeros after
+    for (int u = tid; u < kTcRows * 17; u += 256) {
+      const int n = u / 17, j = u - 17 * (u / 17);
+      uint4 ev = make_uint4(0, 0, 0, 0), od = ev;
+      if (j == 16) {
+        ev.x = (uint32_t)(std::is_same<T, __nv_bfloat16>::value ? 0x3F80u : 0x3C00u);  // 1.0 in T
+      } else if (n < R) {
         const T* qrow =
             reinterpret_cast<const T*>(a.q) + ((int64_t)(q_start + n / G) * a.hq + (int64_t)h * G + n % G) * D;
-        q0 = *reinterpret_cast<const uint4*>(qrow + 16 * j);
-        q1 = *reinterpret_cast<const uint4*>(qrow + 16 * j + 8);
+        const uint4 q0 = *reinterpret_cast<const uint4*>(qrow + 16 * j);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(qrow + 16 * j + 8);
+        ev = make_uint4(prmt(q0.x, q0.y, 0x5410u), prmt(q0.z, q0.w, 0x5410u), prmt(q1.x, q1.y, 0x5410u),
+                        prmt(q1.z, q1.w, 0x5410u));
+        od = make_uint4(prmt(q0.x, q0.y, 0x7632u), prmt(q0.z, q0.w, 0x7632u), prmt(q1.x, q1.y, 0x7632u),
+                        prmt(q1.z, q1.w, 0x7632u));
       }
-      const uint4 ev = make_uint4(prmt(q0.x, q0.y, 0x5410u), prmt(q0.z, q0.w, 0x5410u), prmt(q1.x, q1.y, 0x5410u),
-                                  prmt(q1.z, q1.w, 0x5410u));
-      const uint4 od = make_uint4(prmt(q0.x, q0.y, 0x7632u), prmt(q0.z, q0.w, 0x7632u), prmt(q1.x, q1.y, 0x7632u),
-                                  prmt(q1.z, q1.w, 0x7632u));
       uint8_t* dst = sm.qb + (n >> 3) * kTcQSbo + (2 * j) * 128 + (n & 7) * 16;
       *reinterpret_cast<uint4*>(dst) = ev;
       *reinterpret_cast<uint4*>(dst + 128) = od;
@@ -265,8 +257,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       bool hit = false;
       if (a.owner != nullptr && pos < hi) {
         const int blk = sm.btab[(pos >> bs_log2) - page0];
-        const int off = pos & (bs - 1);
-        hit = a.owner[(int64_t)(blk % (int)a.stage_rows) * bs + off] == (int64_t)blk;
+        hit = a.owner[(int64_t)(blk % (int)a.stage_rows) * bs + (pos & (bs - 1))] == (int64_t)blk;
       }
       const uint32_t bits = __ballot_sync(0xffffffffu, hit);
       if (lane == 0) sm.smask[(base - lo) >> 5] = bits;
@@ -303,134 +294,97 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 8) {
     // ============================ producer + MMA issuer
     if (lane == 0) {
-      const int rows_box = min(bs, kTcStage);
       constexpr uint32_t idesc_qk = tc::instr_desc(std::is_same<T, __nv_bfloat16>::value ? 1u : 0u, 0, 0, 128, kTcRows);
       constexpr uint32_t idesc_pv = tc::instr_desc(0u, 1, 1, 128, kTcRows);
       // descriptors of k-step 0; k-step j starts 256 * j bytes later (+16 * j in the start field)
       const uint64_t dq0 = tc::smem_desc(smem_u32(sm.qb), 128, kTcQSbo);
-      // group w's tiles sit sizeof(vt[0]) / sizeof(pt[0]) bytes further: the start field grows by that >> 4
-      const uint64_t dv0 = tc::smem_desc(smem_u32(sm.vt[0]), 128, kTcVtSbo);
-      const uint64_t dp0 = tc::smem_desc(smem_u32(sm.pt[0]), 128, kTcVtSbo);
-      for (int s = 0; s < min(2, n_int); ++s) tc_issue_stage(sm, s, lo, hi, bs_log2, page0, h, a.ksh, a.vsh, &tmk, &tmv, b_full);
-      int qk = 0, pv = 0;
-      uint32_t idle = 0;
-      while (pv < nst && !*reinterpret_cast<volatile int*>(&sm.abort)) {
-        bool progressed = false;
-        // QK of stage qk once its K operand is written (its S buffer was consumed by stage qk-2's softmax)
-        if (qk < nst && qk <= pv + 1 && tc::mbar_try(b_k + 8 * (qk & 1), (qk >> 1) & 1)) {
-          const int w = qk & 1;
-          tc::tc_fence_after();
-          const uint32_t d_s = tmem + 256 * w + kTcColS, a_k = tmem + 256 * w + kTcColA;
+      const uint64_t dva = tc::smem_desc(smem_u32(sm.vt), 128, kTcVtSbo);
+      const uint64_t dvb = tc::smem_desc(smem_u32(sm.vt) + 16 * kTcVtSbo, 128, kTcVtSbo);
+      const uint64_t dp0 = tc::smem_desc(smem_u32(sm.pt), 128, kTcVtSbo);
+      const uint32_t d_s = tmem + kTcColS, a_k = tmem + kTcColA, d_o = tmem + kTcColO;
+      for (int s = 0; s < min(2, n_int); ++s)
+        tc_issue_stage(sm, s, lo, hi, bs_log2, page0, h, a.ksh, a.vsh, &tmk, &tmv, b_full);
+      for (int st = 0; st < nst; ++st) {
+        wait(b_k, st & 1);
+        tc::tc_fence_after();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) tc::mma_ts(d_s, a_k + 8 * j, dq0 + 16 * j, idesc_qk, j > 0 ? 1u : 0u);
-          tc::mma_commit(b_s + 8 * w);
-          if (qk + 2 < n_int) {
-            wait(b_empty + 8 * w, (qk >> 1) & 1);
-            tc_issue_stage(sm, qk + 2, lo, hi, bs_log2, page0, h, a.ksh, a.vsh, &tmk, &tmv, b_full);
-          }
-          ++qk;
-          progressed = true;
+        for (int j = 0; j < kTcK / 16; ++j) tc::mma_ts(d_s, a_k + 8 * j, dq0 + 16 * j, idesc_qk, j > 0 ? 1u : 0u);
+        tc::mma_commit(b_s);
+        if (st + 2 < n_int) {
+          wait(b_empty + 8 * (st & 1), (st >> 1) & 1);
+          tc_issue_stage(sm, st + 2, lo, hi, bs_log2, page0, h, a.ksh, a.vsh, &tmk, &tmv, b_full);
         }
-        // PV of stage pv once its P^T and V^T are written
-        if (pv < qk && tc::mbar_try(b_p + 8 * (pv & 1), (pv >> 1) & 1)) {
-          const int w = pv & 1;
-          tc::tc_fence_after();
-          const uint32_t d_o = tmem + 256 * w + kTcColO;
-          const uint32_t acc0 = pv >= 2 ? 1u : 0u;
-          const uint64_t dva = dv0 + (uint64_t)(w * (sizeof(sm.vt[0]) >> 4));
-          const uint64_t dvb = dva + (16 * kTcVtSbo >> 4);
-          const uint64_t dpa = dp0 + (uint64_t)(w * (sizeof(sm.pt[0]) >> 4));
+        wait(b_p, st & 1);
+        tc::tc_fence_after();
+        const uint32_t acc0 = st > 0 ? 1u : 0u;
 #pragma unroll
-          for (int j = 0; j < kTcStage / 16; ++j) {
-            tc::mma_ss(d_o, dva + 16 * j, dpa + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
-            tc::mma_ss(d_o + 32, dvb + 16 * j, dpa + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
-          }
-          tc::mma_commit(b_pv + 8 * w);
-          ++pv;
-          progressed = true;
+        for (int j = 0; j < kTcStage / 16; ++j) {
+          tc::mma_ss(d_o, dva + 16 * j, dp0 + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
+          tc::mma_ss(d_o + 32, dvb + 16 * j, dp0 + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
         }
-        if (progressed) {
-          idle = 0;
-        } else if (++idle > tc::kSpinLimit) {
-          *reinterpret_cast<volatile int*>(&sm.abort) = 1;
-          flag_error(16u);
-        }
+        tc::mma_commit(b_pv);
       }
-      // drain: the last MMAs of both groups complete before TMEM is released
-      for (int s = max(0, nst - 2); s < nst; ++s)
-        if (!tc::mbar_wait(b_pv + 8 * (s & 1), (s >> 1) & 1)) flag_error(16u);
+      // drain: the last MMAs complete before TMEM is released
+      if (nst > 0 && !tc::mbar_wait(b_pv, (nst - 1) & 1)) flag_error(16u);
     }
   } else {
-    // ============================ dequant + softmax warpgroups
-    const int grp = warp >> 2, tok = tid & 127;
+    // ============================ dequant + softmax warps
+    const int half = warp >> 2, tok = tid & 127;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t t_a = tmem + lane_base + 256 * grp + kTcColA;
-    const uint32_t t_s = tmem + lane_base + 256 * grp + kTcColS;
-    const uint32_t t_o = tmem + lane_base + 256 * grp + kTcColO;
+    const uint32_t t_a = tmem + lane_base + kTcColA;
+    const uint32_t t_s = tmem + lane_base + kTcColS + 16 * half;
+    const uint32_t t_o = tmem + lane_base + kTcColO + 16 * half;
     const bool need_lim = hi > seq - qlen + 1;  // history reaches the causal window (cache-only chunks)
-    float lrow[kTcRows];
+    const float scale = a.scale_log2;
+    const uint32_t neg_inf = std::is_same<T, __nv_bfloat16>::value ? 0xFF80u : 0xFC00u;
+    float mrow[16], lrow[16];
 #pragma unroll
-    for (int r = 0; r < kTcRows; ++r) lrow[r] = 0.0f;
-    const float4* mrow4 = reinterpret_cast<const float4*>(sm.mrow[grp]);
-    uint8_t* vt_row = sm.vt[grp] + (tok >> 3) * 128 + (tok & 7) * 16;
-    uint8_t* pt_row = sm.pt[grp] + (tok >> 3) * 128 + (tok & 7) * 16;
-    int it = 0;
-    for (int st = grp; st < nst; st += 2, ++it) {
+    for (int r = 0; r < 16; ++r) {
+      mrow[r] = -INFINITY;
+      lrow[r] = 0.0f;
+    }
+    uint8_t* vt_row = sm.vt + (16 * half) * kTcVtSbo + (tok >> 3) * 128 + (tok & 7) * 16;
+    uint8_t* pt_row = sm.pt + (2 * half) * kTcVtSbo + (tok >> 3) * 128 + (tok & 7) * 16;
+
+    for (int st = 0; st < nst; ++st) {
       int pos;
       bool live;
-      if (st < n_int) {
+      uint4 vc0 = make_uint4(0, 0, 0, 0), vc1 = vc0;
+      uint2 vlut = make_uint2(0, 0);
+      const float* srow_v = nullptr;
+      const bool is_int = st < n_int;
+      if (is_int) {
         // ---------- INT2 stage: raw bytes -> registers, release the slot, K -> TMEM
         const int slot = st & 1;
         pos = lo + st * kTcStage + tok;
         wait(b_full + 8 * slot, (st >> 1) & 1);
         const uint32_t kmeta = *reinterpret_cast<const uint32_t*>(&sm.k[slot][tok][0]);
         const uint32_t vmeta = *reinterpret_cast<const uint32_t*>(&sm.k[slot][tok][4]);
-        uint4 kc[4], vc[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          kc[i] = *reinterpret_cast<const uint4*>(&sm.k[slot][tok][32 + 16 * i]);
-          vc[i] = *reinterpret_cast<const uint4*>(&sm.v[slot][tok][16 * i]);
-        }
+        const uint4 kc0 = *reinterpret_cast<const uint4*>(&sm.k[slot][tok][32 + 32 * half]);
+        const uint4 kc1 = *reinterpret_cast<const uint4*>(&sm.k[slot][tok][48 + 32 * half]);
+        vc0 = *reinterpret_cast<const uint4*>(&sm.v[slot][tok][32 * half]);
+        vc1 = *reinterpret_cast<const uint4*>(&sm.v[slot][tok][16 + 32 * half]);
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(b_empty + 8 * slot);
         live = pos < hi && !((sm.smask[(pos - lo) >> 5] >> ((pos - lo) & 31)) & 1u);
-        uint2 klut = make_uint2(0, 0), vlut = make_uint2(0, 0);
+        uint2 klut = make_uint2(0, 0);
         if (live) {
           klut = make_klut<T>(f16_bits_to_f32(kmeta & 0xffffu), f16_bits_to_f32(kmeta >> 16));
           vlut = make_vlut<T>(f16_bits_to_f32(vmeta & 0xffffu), f16_bits_to_f32(vmeta >> 16));
         }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tc_lut_word(kc[c].x, klut.x, klut.y, r);
-          tc_lut_word(kc[c].y, klut.x, klut.y, r + 8);
-          tc_lut_word(kc[c].z, klut.x, klut.y, r + 16);
-          tc_lut_word(kc[c].w, klut.x, klut.y, r + 24);
-          tc::tmem_st32(t_a + 32 * c, r);
-        }
-        tc::tmem_wait_st();
-        tc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(b_k + 8 * grp);
-        // PV of this group's previous stage done: V^T, P^T and O are free
-        if (it > 0) {
-          wait(b_pv + 8 * grp, (it - 1) & 1);
-          tc::tc_fence_after();
-        }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint32_t vw[4] = {vc[c].x, vc[c].y, vc[c].z, vc[c].w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t r[8];
-            tc_lut_word(vw[j], vlut.x, vlut.y, r);
-            const int m8 = 2 * (4 * c + j);  // M groups of dims 16(4c+j) + {0,2,..,14} and + {1,3,..,15}
-            *reinterpret_cast<uint4*>(vt_row + m8 * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
-            *reinterpret_cast<uint4*>(vt_row + (m8 + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
-          }
-        }
+        uint32_t r[32];
+        tc_lut_word(kc0.x, klut.x, klut.y, r);
+        tc_lut_word(kc0.y, klut.x, klut.y, r + 8);
+        tc_lut_word(kc0.z, klut.x, klut.y, r + 16);
+        tc_lut_word(kc0.w, klut.x, klut.y, r + 24);
+        tc::tmem_st32(t_a + 64 * half, r);
+        tc_lut_word(kc1.x, klut.x, klut.y, r);
+        tc_lut_word(kc1.y, klut.x, klut.y, r + 8);
+        tc_lut_word(kc1.z, klut.x, klut.y, r + 16);
+        tc_lut_word(kc1.w, klut.x, klut.y, r + 24);
+        tc::tmem_st32(t_a + 64 * half + 32, r);
       } else {
-        // ---------- staged stage: the (128 q + tok)-th staged position, fp32 rows -> K (TMEM), V^T
+        // ---------- staged stage: the (128 q + tok)-th staged position, fp32 rows -> K (TMEM)
         const int j = (st - n_int) * kTcStage + tok;
         live = j < n_staged;
         pos = hi;
@@ -447,192 +401,163 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int64_t seat = (int64_t)(blk % (int)a.stage_rows) * bs + (pos & (bs - 1));
           srow_k = a.stage_k + (seat * a.hk + h) * D;
         }
-#pragma unroll 4
-        for (int w16 = 0; w16 < 16; ++w16) {
-          float4 f[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            f[i] = live ? *reinterpret_cast<const float4*>(srow_k + 16 * w16 + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        srow_v = a.stage_v + (srow_k - a.stage_k) + 128 * half;
+        srow_k += 128 * half;
+#pragma unroll 2
+        for (int w = 0; w < 8; ++w) {
           uint32_t r[8];
-          tc_pack_word<T, false>(f[0], f[1], f[2], f[3], r);
-          tc::tmem_st8(t_a + 8 * w16, r);
+          tc_pack_word<T, false>(srow_k + 16 * w, live, r);
+          tc::tmem_st8(t_a + 64 * half + 8 * w, r);
         }
-        tc::tmem_wait_st();
-        tc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(b_k + 8 * grp);
-        if (it > 0) {
-          wait(b_pv + 8 * grp, (it - 1) & 1);
-          tc::tc_fence_after();
-        }
-        const float* srow_v = a.stage_v + (srow_k - a.stage_k);
-#pragma unroll 4
-        for (int w16 = 0; w16 < 16; ++w16) {
-          float4 f[4];
+      }
+      if (half == 0) {
+        // bias k-step (columns 128..135): element 256 = 0 for live tokens, -inf for masked ones
+        const uint32_t bias[8] = {live ? 0u : neg_inf, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+        tc::tmem_st8(t_a + 128, bias);
+      }
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(b_k);
+
+      // ---------- V -> V^T (after the previous stage's PV freed V^T, P^T and O)
+      if (st > 0) {
+        wait(b_pv, (st - 1) & 1);
+        tc::tc_fence_after();
+      }
+      if (is_int) {
+        const uint32_t vw[8] = {vc0.x, vc0.y, vc0.z, vc0.w, vc1.x, vc1.y, vc1.z, vc1.w};
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            f[i] = live ? *reinterpret_cast<const float4*>(srow_v + 16 * w16 + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < 8; ++j) {
           uint32_t r[8];
-          tc_pack_word<T, true>(f[0], f[1], f[2], f[3], r);
-          *reinterpret_cast<uint4*>(vt_row + (2 * w16) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
-          *reinterpret_cast<uint4*>(vt_row + (2 * w16 + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
+          tc_lut_word(vw[j], vlut.x, vlut.y, r);
+          *reinterpret_cast<uint4*>(vt_row + (2 * j) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
+          *reinterpret_cast<uint4*>(vt_row + (2 * j + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
+        }
+      } else {
+#pragma unroll 2
+        for (int j = 0; j < 8; ++j) {
+          uint32_t r[8];
+          tc_pack_word<T, true>(srow_v + 16 * j, live, r);
+          *reinterpret_cast<uint4*>(vt_row + (2 * j) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
+          *reinterpret_cast<uint4*>(vt_row + (2 * j + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
         }
       }
 
-      // ---------- scores of this token, x = S * scale (log2 units), masked; re-read
-      // from TMEM in each pass (16 rows at a time) to keep registers for the dequant
-      wait(b_s + 8 * grp, it & 1);
+      // ---------- scores of rows [16 half, +16): x = S * scale (log2 units)
+      wait(b_s, st & 1);
       tc::tc_fence_after();
-      const float scale = a.scale_log2;
+      float x[16];
+      {
+        uint32_t sraw[16];
+        tc::tmem_ld16(t_s, sraw);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int r = 0; r < 16; ++r) x[r] = __uint_as_float(sraw[r]) * scale;
+      }
+      if (need_lim) {
+#pragma unroll
+        for (int r = 0; r < 16; ++r)
+          if (pos >= sm.lim[16 * half + r]) x[r] = -INFINITY;
+      }
       bool need = false;
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float x[16];
-        tc_scores(t_s + 16 * hh, 16 * hh, scale, live, R, need_lim, pos, sm.lim, x);
+      for (int r = 0; r < 16; ++r) need = need || (x[r] > mrow[r] + kTcHeadroom);
+      if (tc::bar_or(1 + half, 128, need)) {
+        // new row maxima over the stage's 128 tokens; rescale l and (if they moved) O
 #pragma unroll
-        for (int r4 = 0; r4 < 4; ++r4) {
-          const float4 m4 = mrow4[4 * hh + r4];
-          need = need || (x[4 * r4] > m4.x + kTcHeadroom) || (x[4 * r4 + 1] > m4.y + kTcHeadroom) ||
-                 (x[4 * r4 + 2] > m4.z + kTcHeadroom) || (x[4 * r4 + 3] > m4.w + kTcHeadroom);
+        for (int r = 0; r < 16; ++r) {
+          const int v = __reduce_max_sync(0xffffffffu, tc_ord(x[r]));
+          if (lane == 0) sm.red[warp][r] = v;
         }
-      }
-      if (tc::bar_or(1 + grp, 128, need)) {
-        // new row maxima over the stage; rescale l and (if they moved) O
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float x[16];
-          tc_scores(t_s + 16 * hh, 16 * hh, scale, live, R, need_lim, pos, sm.lim, x);
-#pragma unroll
-          for (int r = 0; r < 16; ++r) {
-            const int v = __reduce_max_sync(0xffffffffu, tc_ord(x[r]));
-            if (lane == 0) sm.red[warp][16 * hh + r] = v;
-          }
-        }
-        tc::bar_sync(1 + grp, 128);
-        if (tok < kTcRows) {
-          const int r = tok;
-          const int k = max(max(sm.red[4 * grp][r], sm.red[4 * grp + 1][r]),
-                            max(sm.red[4 * grp + 2][r], sm.red[4 * grp + 3][r]));
-          const float mo = sm.mrow[grp][r];
-          const float mn = fmaxf(mo, tc_unord(k));
-          sm.alpha[grp][r] = (mo == -INFINITY) ? 0.0f : tc_exp2(mo - mn);
-          sm.mrow[grp][r] = mn;
-        }
-        tc::bar_sync(1 + grp, 128);
+        tc::bar_sync(1 + half, 128);
+        float alpha[16];
         bool moved = false;
 #pragma unroll
-        for (int r = 0; r < kTcRows; ++r) {
-          const float al = sm.alpha[grp][r];
-          moved = moved || al != 1.0f;
-          lrow[r] *= al;
+        for (int r = 0; r < 16; ++r) {
+          const int k = max(max(sm.red[4 * half][r], sm.red[4 * half + 1][r]),
+                            max(sm.red[4 * half + 2][r], sm.red[4 * half + 3][r]));
+          const float mn = fmaxf(mrow[r], tc_unord(k));
+          alpha[r] = (mrow[r] == -INFINITY) ? 0.0f : tc_exp2(mrow[r] - mn);
+          moved = moved || alpha[r] != 1.0f;
+          lrow[r] *= alpha[r];
+          mrow[r] = mn;
         }
-        if (it > 0 && moved) {
+        tc::bar_sync(1 + half, 128);
+        if (st > 0 && moved) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
+            uint32_t o[16];
+            tc::tmem_ld16(t_o + 32 * hh, o);
+            tc::tmem_wait_ld();
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              uint32_t o[16];
-              tc::tmem_ld16(t_o + 32 * hh + 16 * q, o);
-              tc::tmem_wait_ld();
-#pragma unroll
-              for (int r = 0; r < 16; ++r)
-                o[r] = __float_as_uint(__uint_as_float(o[r]) * sm.alpha[grp][16 * q + r]);
-              tc::tmem_st16(t_o + 32 * hh + 16 * q, o);
-            }
+            for (int r = 0; r < 16; ++r) o[r] = __float_as_uint(__uint_as_float(o[r]) * alpha[r]);
+            tc::tmem_st16(t_o + 32 * hh, o);
           }
           tc::tmem_wait_st();
         }
       }
-      // ---------- P^T (fp16) for this token, l
+      // ---------- P^T (fp16) and l
+      uint32_t pk[8];
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float x[16];
-        tc_scores(t_s + 16 * hh, 16 * hh, scale, live, R, need_lim, pos, sm.lim, x);
-        uint32_t pk[8];
-#pragma unroll
-        for (int r = 0; r < 16; r += 2) {
-          const float2 mm = reinterpret_cast<const float2*>(sm.mrow[grp])[(16 * hh + r) >> 1];
-          const float m0 = (mm.x == -INFINITY) ? 0.0f : mm.x;
-          const float m1 = (mm.y == -INFINITY) ? 0.0f : mm.y;
-          const float p0 = tc_exp2(x[r] - m0), p1 = tc_exp2(x[r + 1] - m1);
-          lrow[16 * hh + r] += p0;
-          lrow[16 * hh + r + 1] += p1;
-          const __half2 ph = __floats2half2_rn(p0, p1);
-          pk[r >> 1] = *reinterpret_cast<const uint32_t*>(&ph);
-        }
-        *reinterpret_cast<uint4*>(pt_row + (2 * hh) * kTcVtSbo) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(pt_row + (2 * hh + 1) * kTcVtSbo) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      for (int r = 0; r < 16; r += 2) {
+        const float m0 = (mrow[r] == -INFINITY) ? 0.0f : mrow[r];
+        const float m1 = (mrow[r + 1] == -INFINITY) ? 0.0f : mrow[r + 1];
+        const float p0 = tc_exp2(x[r] - m0), p1 = tc_exp2(x[r + 1] - m1);
+        lrow[r] += p0;
+        lrow[r + 1] += p1;
+        const __half2 ph = __floats2half2_rn(p0, p1);
+        pk[r >> 1] = *reinterpret_cast<const uint32_t*>(&ph);
       }
+      *reinterpret_cast<uint4*>(pt_row) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      *reinterpret_cast<uint4*>(pt_row + kTcVtSbo) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       tc::fence_async_smem();
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(b_p + 8 * grp);
+      if (lane == 0) tc::mbar_arrive(b_p);
     }
 
-    // ---------------- epilogue: merge the two groups' (m, l, O) and write the partial
-    if (it > 0) {
-      wait(b_pv + 8 * grp, (it - 1) & 1);
+    // ---------------- epilogue: l over the 128 tokens, normalised partial O and LSE
+    if (nst > 0) {
+      wait(b_pv, (nst - 1) & 1);
       tc::tc_fence_after();
     }
 #pragma unroll
-    for (int r = 0; r < kTcRows; ++r) {
+    for (int r = 0; r < 16; ++r) {
       float v = lrow[r];
 #pragma unroll
       for (int o2 = 16; o2 > 0; o2 >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o2);
       if (lane == 0) sm.red[warp][r] = __float_as_int(v);
     }
-    tc::bar_sync(1 + grp, 128);
-    if (tok < kTcRows) {
-      const int r = tok;
-      sm.lfin[grp][r] = (__int_as_float(sm.red[4 * grp][r]) + __int_as_float(sm.red[4 * grp + 1][r])) +
-                        (__int_as_float(sm.red[4 * grp + 2][r]) + __int_as_float(sm.red[4 * grp + 3][r]));
-      if (it == 0) sm.mrow[grp][r] = -INFINITY;
-    }
-    tc::tc_fence_before();
-    tc::bar_sync(3, 256);
-    tc::tc_fence_after();
-    // thread (tok, grp): dim tc_dim(128 grp + tok) of both groups' accumulators
-    const bool has0 = nst > 0, has1 = nst > 1;
+    tc::bar_sync(1 + half, 128);
+    float L[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+      L[r] = (__int_as_float(sm.red[4 * half][r]) + __int_as_float(sm.red[4 * half + 1][r])) +
+             (__int_as_float(sm.red[4 * half + 2][r]) + __int_as_float(sm.red[4 * half + 3][r]));
     const int64_t pslot = p.part_begin[ri] + sp;
-    const int64_t prow0 = (pslot * a.hk + h) * kTcRows;
-    const int dim = tc_dim(128 * grp + tok);
+    const int64_t prow0 = (pslot * a.hk + h) * kTcRows + 16 * half;
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      uint32_t o0[16], o1[16];
+    for (int hh = 0; hh < 2; ++hh) {
+      uint32_t o[16];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) o0[r] = o1[r] = 0u;
-      if (has0) {
-        tc::tmem_ld16(tmem + lane_base + kTcColO + 32 * grp + 16 * q, o0);
+      for (int r = 0; r < 16; ++r) o[r] = 0u;
+      if (nst > 0) {
+        tc::tmem_ld16(t_o + 32 * hh, o);
         tc::tmem_wait_ld();
       }
-      if (has1) {
-        tc::tmem_ld16(tmem + lane_base + 256 + kTcColO + 32 * grp + 16 * q, o1);
-        tc::tmem_wait_ld();
-      }
+      const int dim = tc_dim(128 * hh + tok);
 #pragma unroll
       for (int r = 0; r < 16; ++r) {
-        const int row = 16 * q + r;
-        if (row >= R) continue;
-        const float m0 = sm.mrow[0][row], m1 = sm.mrow[1][row];
-        const float M = fmaxf(m0, m1);
-        const float w0 = (has0 && m0 != -INFINITY) ? tc_exp2(m0 - M) : 0.0f;
-        const float w1 = (has1 && m1 != -INFINITY) ? tc_exp2(m1 - M) : 0.0f;
-        const float L = sm.lfin[0][row] * w0 + sm.lfin[1][row] * w1;
-        if (!(L > 0.0f) && L == L) continue;
-        const float ov = (w0 != 0.0f ? __uint_as_float(o0[r]) * w0 : 0.0f) +
-                         (w1 != 0.0f ? __uint_as_float(o1[r]) * w1 : 0.0f);
-        a.part_o[(prow0 + row) * D + dim] = ov / L;
+        const bool keep = (16 * half + r < R) && (L[r] > 0.0f || L[r] != L[r]);
+        if (keep) a.part_o[(prow0 + r) * D + dim] = __uint_as_float(o[r]) / L[r];
       }
     }
-    if (tid < R) {
-      const int row = tid;
-      const float m0 = sm.mrow[0][row], m1 = sm.mrow[1][row];
-      const float M = fmaxf(m0, m1);
-      const float w0 = (has0 && m0 != -INFINITY) ? tc_exp2(m0 - M) : 0.0f;
-      const float w1 = (has1 && m1 != -INFINITY) ? tc_exp2(m1 - M) : 0.0f;
-      const float L = sm.lfin[0][row] * w0 + sm.lfin[1][row] * w1;
-      a.part_lse[prow0 + row] = (L > 0.0f || L != L) ? (M + log2f(L)) * 0.69314718055994531f : -INFINITY;
-    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+      if (tok == r && 16 * half + r < R)
+        a.part_lse[prow0 + r] =
+            (L[r] > 0.0f || L[r] != L[r]) ? (mrow[r] + log2f(L[r])) * 0.69314718055994531f : -INFINITY;
   }
 
   // ---------------- teardown
