@@ -1,14 +1,16 @@
 // Decode / MTP attention over paged INT2 history on the 5th-generation tensor
 // cores: the tcgen05 + TMEM + TMA kernel.
 //
-// One CTA per SM = one (request, kv head, history split); 288 threads.
-//   warp 8, lane 0: TMA producer and MMA issuer.  The split's INT2 history
-//     arrives in 128-token stages through a 2-slot ring: K slot bytes [0:96)
-//     and V slot bytes [0:64) of every token, one 2D tensor-map box per page.
-//   warps 0-7: thread (tok, half) = (tid % 128, tid / 128) handles dims
-//     [128 half, 128 half + 128) of token tok and query rows
-//     [16 half, 16 half + 16).  All eight warps work on the same stage (and run
-//     the same code), which keeps the instruction cache warm.
+// One CTA per SM = one (request, kv head, history split); 544 threads.
+//   warp 16, lane 0: TMA producer and MMA issuer.  The split's INT2 history
+//     arrives in 128-token stages through a 2-slot ring: K slot bytes [0:48)
+//     and [48:96), V slot bytes [0:48) and [16:64) of every token, four 2D
+//     tensor-map boxes per page whose 48-byte rows put the 8 tokens of a
+//     shared-memory wavefront on 8 distinct bank groups.
+//   warps 0-15: thread (tok, q) = (tid % 128, tid / 128) handles dims
+//     [64 q, 64 q + 64) of token tok and query rows [8 q, 8 q + 8).  All
+//     sixteen warps work on the same stage (and run the same code, which keeps
+//     the instruction cache warm); four per scheduler hide each other's latency.
 //
 // Prologue: the split's staging owner tags are scanned into a bitmask of
 // staged positions (owner[(blk % rows) * bs + off] == blk, backend.py:172-176).
@@ -26,7 +28,7 @@
 //     in shared memory (K-major, loaded once).
 //   V -> fp16 values (the chain's values are fp16-exact) in a shared V^T tile
 //     (MN-major: dims contiguous per token).
-//   softmax: each thread loads its token's 16 scores from TMEM.  The running
+//   softmax: each thread loads its token's 8 scores from TMEM.  The running
 //     row maximum moves only when a score exceeds it by more than 15 (log2
 //     units): P = 2^(x - m) stays <= 2^15 in fp16, and O/l are rescaled on
 //     those stages only.  P^T goes to shared memory (MN-major).
@@ -50,11 +52,12 @@
 namespace oscar {
 
 constexpr int kTcStage = 128;
-constexpr int kTcThreads = 288;
+constexpr int kTcThreads = 544;  // 16 dequant/softmax warps + the producer warp
+constexpr int kTcCompute = 512;
 constexpr int kTcRows = 32;   // N of both MMAs: query rows (GQA group x MTP tokens)
 constexpr int kTcK = 272;     // QK reduction: 256 dims + the bias k-step
-constexpr int kTcCols = 256;  // TMEM columns: A_K [0,136) | S [160,192) | O [192,256)
-constexpr int kTcColA = 0, kTcColS = 160, kTcColO = 192;
+constexpr int kTcCols = 512;  // TMEM columns: A_K[0] [0,136) | S[0] [160,192) | S[1] [192,224) | O [224,288) | A_K[1] [288,424)
+constexpr int kTcColA0 = 0, kTcColA1 = 288, kTcColS = 160, kTcColO = 224;
 constexpr int kTcMaxStages = 64;  // INT2 stages per split (staged bitmask capacity)
 constexpr int kTcMaxWords = kTcMaxStages * kTcStage / 32;
 constexpr int kTcMaxPages = kTcMaxStages * kTcStage / 8 + 2;
@@ -62,24 +65,31 @@ constexpr uint32_t kTcVtSbo = 2048;          // V^T / P^T: bytes between 8-eleme
 constexpr uint32_t kTcQSbo = kTcK / 8 * 128;  // Q: bytes between 8-row groups (34 k-groups x 128 B)
 constexpr float kTcHeadroom = 15.0f;
 
+constexpr int kTcRow = 48;  // bytes per token row of each raw box
+
 struct TcSmem {
-  uint8_t k[2][kTcStage][96];
-  uint8_t v[2][kTcStage][64];
-  uint8_t vt[256 * kTcStage * 2];      // V^T: address(tok, m) = (m/8)*2048 + (tok/8)*128 + (tok%8)*16 + (m%8)*2
-  uint8_t pt[kTcRows * kTcStage * 2];  // P^T: address(tok, n) = (n/8)*2048 + (tok/8)*128 + (tok%8)*16 + (n%8)*2
+  uint8_t ka[2][kTcStage][kTcRow];  // K slot bytes [0, 48): K/V scale+zero, pad, codes of dims 0..63
+  uint8_t kb[2][kTcStage][kTcRow];  // K slot bytes [48, 96): codes of dims 64..255
+  uint8_t va[2][kTcStage][kTcRow];  // V slot bytes [0, 48)
+  uint8_t vb[2][kTcStage][kTcRow];  // V slot bytes [16, 64)
+  uint8_t vt[2][256 * kTcStage * 2];      // V^T: address(tok, m) = (m/8)*2048 + (tok/8)*128 + (tok%8)*16 + (m%8)*2
+  uint8_t pt[2][kTcRows * kTcStage * 2];  // P^T: address(tok, n) = (n/8)*2048 + (tok/8)*128 + (tok%8)*16 + (n%8)*2
   uint8_t qb[kTcRows * kTcK * 2];      // Q:   address(n, k)   = (n/8)*4352 + (k/8)*128 + (n%8)*16 + (k%8)*2
   int btab[kTcMaxPages];
   uint32_t smask[kTcMaxWords];  // staged positions of the split, bit (pos - lo)
   int spref[kTcMaxWords + 1];   // exclusive prefix counts of smask
   int lim[kTcRows];             // cache-only chunks: row r sees positions < lim[r]
-  int red[8][16];
-  unsigned long long bar_full[2], bar_empty[2], bar_k, bar_s, bar_p, bar_pv;
+  alignas(16) int red[2][16][8];  // slow-path row maxima, double-buffered
+  float lsum[16][8];
+  uint2 klut[kTcStage], vlut[kTcStage];  // value tables of the stage's tokens (built by half 0 / half 1)
+  unsigned long long bar_full[2], bar_empty[2], bar_k[2], bar_s[2], bar_p, bar_pv;  // k, s per TMEM buffer
   uint32_t tmem;
   int abort;
   int n_staged;
 };
 // vector accesses (uint4) and TMA destinations rely on these
-static_assert(offsetof(TcSmem, v) % 128 == 0 && offsetof(TcSmem, vt) % 16 == 0 && offsetof(TcSmem, pt) % 16 == 0 &&
+static_assert(offsetof(TcSmem, kb) % 128 == 0 && offsetof(TcSmem, va) % 128 == 0 &&
+                  offsetof(TcSmem, vb) % 128 == 0 && offsetof(TcSmem, vt) % 16 == 0 && offsetof(TcSmem, pt) % 16 == 0 &&
                   offsetof(TcSmem, qb) % 16 == 0 && sizeof(TcSmem) <= 227 * 1024,
               "TcSmem layout");
 
@@ -124,6 +134,40 @@ OSCAR_DEVINL void tc_pack_word(const float* src, bool live, uint32_t* r) {
   }
 }
 
+// 4-entry value tables from a token's fp16 (scale, zero) pair, built with
+// packed conversions: K holds T(fp16(c * s + z)) (c * s + z computed as one fma:
+// c * s is exact), V the fp16 bit patterns of the same values clamped to the
+// fp16 range (make_klut / make_vlut semantics)
+template <typename T>
+OSCAR_DEVINL uint2 tc_klut(uint32_t meta) {
+  const float sc = f16_bits_to_f32(meta & 0xffffu), zr = f16_bits_to_f32(meta >> 16);
+  __half2 h01 = __floats2half2_rn(zr, fmaf(1.0f, sc, zr)), h23 = __floats2half2_rn(fmaf(2.0f, sc, zr), fmaf(3.0f, sc, zr));
+  uint32_t p01, p23;
+  if (std::is_same<T, __nv_bfloat16>::value) {
+    const float2 g01 = __half22float2(h01), g23 = __half22float2(h23);
+    const __nv_bfloat162 b01 = __floats2bfloat162_rn(g01.x, g01.y), b23 = __floats2bfloat162_rn(g23.x, g23.y);
+    p01 = *reinterpret_cast<const uint32_t*>(&b01);
+    p23 = *reinterpret_cast<const uint32_t*>(&b23);
+  } else {
+    p01 = *reinterpret_cast<const uint32_t*>(&h01);
+    p23 = *reinterpret_cast<const uint32_t*>(&h23);
+  }
+  return lut_from(p01, p23);
+}
+template <typename T>
+OSCAR_DEVINL uint2 tc_vlut(uint32_t meta) {
+  const float sc = f16_bits_to_f32(meta & 0xffffu), zr = f16_bits_to_f32(meta >> 16);
+  const __half2 h01 = __floats2half2_rn(zr, fmaf(1.0f, sc, zr)), h23 = __floats2half2_rn(fmaf(2.0f, sc, zr), fmaf(3.0f, sc, zr));
+  float2 g01 = __half22float2(h01), g23 = __half22float2(h23);
+  if (std::is_same<T, __nv_bfloat16>::value) {
+    g01 = __bfloat1622float2(__floats2bfloat162_rn(g01.x, g01.y));
+    g23 = __bfloat1622float2(__floats2bfloat162_rn(g23.x, g23.y));
+  }
+  const __half2 c01 = __floats2half2_rn(fminf(fmaxf(g01.x, -65504.0f), 65504.0f), fminf(fmaxf(g01.y, -65504.0f), 65504.0f));
+  const __half2 c23 = __floats2half2_rn(fminf(fmaxf(g23.x, -65504.0f), 65504.0f), fminf(fmaxf(g23.y, -65504.0f), 65504.0f));
+  return lut_from(*reinterpret_cast<const uint32_t*>(&c01), *reinterpret_cast<const uint32_t*>(&c23));
+}
+
 OSCAR_DEVINL float tc_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
@@ -136,8 +180,8 @@ OSCAR_DEVINL int tc_ord(float v) {
 }
 OSCAR_DEVINL float tc_unord(int k) { return __int_as_float(k >= 0 ? k : k ^ 0x7fffffff); }
 
-// TMA of INT2 stage s into ring slot s & 1: one K box (96 B x rows) and one V
-// box (64 B x rows) per page of the stage
+// TMA of INT2 stage s into ring slot s & 1: four 48-byte boxes (K [0,48),
+// K [48,96), V [0,48), V [16,64)) of `rows` tokens per page of the stage
 OSCAR_DEVINL void tc_issue_stage(TcSmem& sm, int s, int lo, int hi, int bs_log2, int page0, int h, int64_t ksh,
                                  int64_t vsh, const CUtensorMap* tmk, const CUtensorMap* tmv, uint32_t b_full) {
   const int bs = 1 << bs_log2;
@@ -147,14 +191,17 @@ OSCAR_DEVINL void tc_issue_stage(TcSmem& sm, int s, int lo, int hi, int bs_log2,
   const int end = min(base + kTcStage, hi);
   const int pg_first = base >> bs_log2, pg_last = (end - 1) >> bs_log2;
   const uint32_t bar = b_full + 8 * slot;
-  tc::mbar_expect_tx(bar, (uint32_t)((pg_last - pg_first + 1) * rows_box * (96 + 64)));
+  tc::mbar_expect_tx(bar, (uint32_t)((pg_last - pg_first + 1) * rows_box * 4 * kTcRow));
   for (int pg = pg_first; pg <= pg_last; ++pg) {
     const int blk = sm.btab[pg - page0];
     const int off0 = (bs > kTcStage) ? base - (pg << bs_log2) : 0;
     const int row = (pg << bs_log2) + off0 - base;
     const int y = (blk << bs_log2) + off0;
-    tc::tma_load_2d(smem_u32(&sm.k[slot][row][0]), tmk, (int)(h * ksh), y, bar);
-    tc::tma_load_2d(smem_u32(&sm.v[slot][row][0]), tmv, (int)(h * vsh), y, bar);
+    const int xk = (int)(h * ksh), xv = (int)(h * vsh);
+    tc::tma_load_2d(smem_u32(&sm.ka[slot][row][0]), tmk, xk, y, bar);
+    tc::tma_load_2d(smem_u32(&sm.kb[slot][row][0]), tmk, xk + 48, y, bar);
+    tc::tma_load_2d(smem_u32(&sm.va[slot][row][0]), tmv, xv, y, bar);
+    tc::tma_load_2d(smem_u32(&sm.vb[slot][row][0]), tmv, xv + 16, y, bar);
   }
 }
 
@@ -163,6 +210,7 @@ struct TcWait {
   // bounded wait; after a timeout (or once the CTA gave up) every wait returns
   // at once, so control flow stays uniform and the kernel drains and exits
   OSCAR_DEVINL void operator()(uint32_t bar, uint32_t parity) const {
+    if (tc::mbar_try(bar, parity)) return;
     if (*reinterpret_cast<volatile int*>(abort)) return;
     if (!tc::mbar_wait(bar, parity)) {
       *reinterpret_cast<volatile int*>(abort) = 1;
@@ -172,7 +220,7 @@ struct TcWait {
 };
 
 template <typename T>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __maxnreg__(96)
     decode_tc_kernel(const AttnArgs a, const __grid_constant__ AttnPlan p, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv) {
   constexpr int D = 256;
@@ -194,9 +242,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int page0 = lo >> bs_log2;
   const int npages = (hi > lo) ? ((hi - 1) >> bs_log2) - page0 + 1 : 0;
   const int nwords = (hi > lo) ? (hi - lo + 31) >> 5 : 0;
+  constexpr int kWarps = kTcCompute / 32;
 
   const uint32_t b_full = smem_u32(&sm.bar_full[0]), b_empty = smem_u32(&sm.bar_empty[0]);
-  const uint32_t b_k = smem_u32(&sm.bar_k), b_s = smem_u32(&sm.bar_s), b_p = smem_u32(&sm.bar_p),
+  const uint32_t b_k = smem_u32(&sm.bar_k[0]), b_s = smem_u32(&sm.bar_s[0]), b_p = smem_u32(&sm.bar_p),
                  b_pv = smem_u32(&sm.bar_pv);
   const TcWait wait{&sm.abort};
 
@@ -205,11 +254,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(b_full + 8 * i, 1);
-      tc::mbar_init(b_empty + 8 * i, 8);
+      tc::mbar_init(b_empty + 8 * i, kWarps);
     }
-    tc::mbar_init(b_k, 8);
+    tc::mbar_init(b_k, kWarps);
+    tc::mbar_init(b_k + 8, kWarps);
     tc::mbar_init(b_s, 1);
-    tc::mbar_init(b_p, 8);
+    tc::mbar_init(b_s + 8, 1);
+    tc::mbar_init(b_p, kWarps);
     tc::mbar_init(b_pv, 1);
     sm.abort = 0;
     tc::mbar_fence_init();
@@ -223,10 +274,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     sm.btab[i] = blk;
   }
-  if (tid < 256) {
+  if (tid < kTcCompute) {
     // Q rows n < R, 16-dim word j: k-group 2j holds dims 16j + {0,2,..,14}, 2j+1 dims 16j + {1,3,..,15};
     // k-groups 32, 33 hold the bias column: 1 at k = 256, zeros after
-    for (int u = tid; u < kTcRows * 17; u += 256) {
+    for (int u = tid; u < kTcRows * 17; u += kTcCompute) {
       const int n = u / 17, j = u - 17 * (u / 17);
       uint4 ev = make_uint4(0, 0, 0, 0), od = ev;
       if (j == 16) {
@@ -246,13 +297,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       *reinterpret_cast<uint4*>(dst + 128) = od;
     }
   }
-  if (warp == 8) {
+  if (warp == kWarps) {
     tc::tmem_alloc(smem_u32(&sm.tmem), kTcCols);
     tc::tmem_relinquish();
   }
   __syncthreads();  // btab ready
-  if (tid < 256) {
-    for (int base = lo + (tid & ~31); base < hi; base += 256) {
+  if (tid < kTcCompute) {
+    for (int base = lo + (tid & ~31); base < hi; base += kTcCompute) {
       const int pos = base + lane;
       bool hit = false;
       if (a.owner != nullptr && pos < hi) {
@@ -291,230 +342,374 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int n_staged = sm.n_staged;
   const int nst = n_int + (n_staged + kTcStage - 1) / kTcStage;
 
-  if (warp == 8) {
+  if (warp == kWarps) {
     // ============================ producer + MMA issuer
+    // order: QK(0); then per stage st: QK(st + 1), PV(st) -- the dequant warps
+    // write stage st + 1's operands before stage st's probabilities.  The K and
+    // S barriers exist per TMEM buffer: with two stages in flight a single
+    // barrier could complete twice before its waiter looks, and a parity wait
+    // cannot tell that apart from no completion.
     if (lane == 0) {
       constexpr uint32_t idesc_qk = tc::instr_desc(std::is_same<T, __nv_bfloat16>::value ? 1u : 0u, 0, 0, 128, kTcRows);
       constexpr uint32_t idesc_pv = tc::instr_desc(0u, 1, 1, 128, kTcRows);
-      // descriptors of k-step 0; k-step j starts 256 * j bytes later (+16 * j in the start field)
+      // descriptors of k-step 0; k-step j starts 256 * j bytes later (+16 * j in the start field);
+      // buffer 1 of V^T / P^T sits sizeof(vt[0]) / sizeof(pt[0]) bytes after buffer 0
       const uint64_t dq0 = tc::smem_desc(smem_u32(sm.qb), 128, kTcQSbo);
-      const uint64_t dva = tc::smem_desc(smem_u32(sm.vt), 128, kTcVtSbo);
-      const uint64_t dvb = tc::smem_desc(smem_u32(sm.vt) + 16 * kTcVtSbo, 128, kTcVtSbo);
-      const uint64_t dp0 = tc::smem_desc(smem_u32(sm.pt), 128, kTcVtSbo);
-      const uint32_t d_s = tmem + kTcColS, a_k = tmem + kTcColA, d_o = tmem + kTcColO;
+      const uint64_t dv0 = tc::smem_desc(smem_u32(sm.vt[0]), 128, kTcVtSbo);
+      const uint64_t dp0 = tc::smem_desc(smem_u32(sm.pt[0]), 128, kTcVtSbo);
       for (int s = 0; s < min(2, n_int); ++s)
         tc_issue_stage(sm, s, lo, hi, bs_log2, page0, h, a.ksh, a.vsh, &tmk, &tmv, b_full);
-      for (int st = 0; st < nst; ++st) {
-        wait(b_k, st & 1);
-        tc::tc_fence_after();
+      for (int qs = 0, ps = 0; ps < nst; ) {
+        if (qs < nst && qs <= ps + 1) {
+          // QK of stage qs into S[qs & 1] from A_K[qs & 1]
+          wait(b_k + 8 * (qs & 1), (qs >> 1) & 1);
+          tc::tc_fence_after();
+          const uint32_t d_s = tmem + kTcColS + 32 * (qs & 1), a_k = tmem + ((qs & 1) ? kTcColA1 : kTcColA0);
 #pragma unroll
-        for (int j = 0; j < kTcK / 16; ++j) tc::mma_ts(d_s, a_k + 8 * j, dq0 + 16 * j, idesc_qk, j > 0 ? 1u : 0u);
-        tc::mma_commit(b_s);
-        if (st + 2 < n_int) {
-          wait(b_empty + 8 * (st & 1), (st >> 1) & 1);
-          tc_issue_stage(sm, st + 2, lo, hi, bs_log2, page0, h, a.ksh, a.vsh, &tmk, &tmv, b_full);
-        }
-        wait(b_p, st & 1);
-        tc::tc_fence_after();
-        const uint32_t acc0 = st > 0 ? 1u : 0u;
+          for (int j = 0; j < kTcK / 16; ++j) tc::mma_ts(d_s, a_k + 8 * j, dq0 + 16 * j, idesc_qk, j > 0 ? 1u : 0u);
+          tc::mma_commit(b_s + 8 * (qs & 1));
+          if (qs + 2 < n_int) {
+            wait(b_empty + 8 * (qs & 1), (qs >> 1) & 1);
+            tc_issue_stage(sm, qs + 2, lo, hi, bs_log2, page0, h, a.ksh, a.vsh, &tmk, &tmv, b_full);
+          }
+          ++qs;
+        } else {
+          // PV of stage ps from V^T[ps & 1], P^T[ps & 1]
+          wait(b_p, ps & 1);
+          tc::tc_fence_after();
+          const uint64_t dva = dv0 + (uint64_t)((ps & 1) * (sizeof(sm.vt[0]) >> 4));
+          const uint64_t dvb = dva + (16 * kTcVtSbo >> 4);
+          const uint64_t dpa = dp0 + (uint64_t)((ps & 1) * (sizeof(sm.pt[0]) >> 4));
+          const uint32_t d_o = tmem + kTcColO;
+          const uint32_t acc0 = ps > 0 ? 1u : 0u;
 #pragma unroll
-        for (int j = 0; j < kTcStage / 16; ++j) {
-          tc::mma_ss(d_o, dva + 16 * j, dp0 + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
-          tc::mma_ss(d_o + 32, dvb + 16 * j, dp0 + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
+          for (int j = 0; j < kTcStage / 16; ++j) {
+            tc::mma_ss(d_o, dva + 16 * j, dpa + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
+            tc::mma_ss(d_o + 32, dvb + 16 * j, dpa + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
+          }
+          tc::mma_commit(b_pv);
+          ++ps;
         }
-        tc::mma_commit(b_pv);
       }
       // drain: the last MMAs complete before TMEM is released
       if (nst > 0 && !tc::mbar_wait(b_pv, (nst - 1) & 1)) flag_error(16u);
     }
   } else {
-    // ============================ dequant + softmax warps
-    const int half = warp >> 2, tok = tid & 127;
+    // ============================ dequant + softmax warps: thread (tok, quarter q) owns
+    // dims [64 q, 64 q + 64) of token tok and query rows [8 q, 8 q + 8).
+    // Iteration it: operands of stage it (K -> TMEM, V -> V^T[it & 1]), then the
+    // softmax of stage it - 1, whose QK ran meanwhile.
+    const int q = warp >> 2, tok = tid & 127;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t t_a = tmem + lane_base + kTcColA;
-    const uint32_t t_s = tmem + lane_base + kTcColS + 16 * half;
-    const uint32_t t_o = tmem + lane_base + kTcColO + 16 * half;
     const bool need_lim = hi > seq - qlen + 1;  // history reaches the causal window (cache-only chunks)
     const float scale = a.scale_log2;
     const uint32_t neg_inf = std::is_same<T, __nv_bfloat16>::value ? 0xFF80u : 0xFC00u;
-    float mrow[16], lrow[16];
+    // this thread's slot bytes: K codes [32 + 16 q, +16), V codes [16 q, +16)
+    const int koff = (q == 0) ? 32 : 16 * (q - 1);  // in ka for q == 0, else in kb
+    const int voff = (q < 3) ? 16 * q : 32;         // in va for q < 3, else in vb (which starts at byte 16)
+    float mrow[8], muse[8], lrow[8];  // running maxima, the same with -inf -> 0, sums
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
+    for (int r = 0; r < 8; ++r) {
       mrow[r] = -INFINITY;
+      muse[r] = 0.0f;
       lrow[r] = 0.0f;
     }
-    uint8_t* vt_row = sm.vt + (16 * half) * kTcVtSbo + (tok >> 3) * 128 + (tok & 7) * 16;
-    uint8_t* pt_row = sm.pt + (2 * half) * kTcVtSbo + (tok >> 3) * 128 + (tok & 7) * 16;
+    int nslow = 0;
+    int pos_prev = hi;  // position of this thread's token in the stage whose softmax runs next
+    const int vt_off = (8 * q) * kTcVtSbo + (tok >> 3) * 128 + (tok & 7) * 16;
+    const int pt_off = q * kTcVtSbo + (tok >> 3) * 128 + (tok & 7) * 16;
 
-    for (int st = 0; st < nst; ++st) {
-      int pos;
-      bool live;
-      uint4 vc0 = make_uint4(0, 0, 0, 0), vc1 = vc0;
-      uint2 vlut = make_uint2(0, 0);
-      const float* srow_v = nullptr;
-      const bool is_int = st < n_int;
-      if (is_int) {
-        // ---------- INT2 stage: raw bytes -> registers, release the slot, K -> TMEM
-        const int slot = st & 1;
-        pos = lo + st * kTcStage + tok;
-        wait(b_full + 8 * slot, (st >> 1) & 1);
-        const uint32_t kmeta = *reinterpret_cast<const uint32_t*>(&sm.k[slot][tok][0]);
-        const uint32_t vmeta = *reinterpret_cast<const uint32_t*>(&sm.k[slot][tok][4]);
-        const uint4 kc0 = *reinterpret_cast<const uint4*>(&sm.k[slot][tok][32 + 32 * half]);
-        const uint4 kc1 = *reinterpret_cast<const uint4*>(&sm.k[slot][tok][48 + 32 * half]);
-        vc0 = *reinterpret_cast<const uint4*>(&sm.v[slot][tok][32 * half]);
-        vc1 = *reinterpret_cast<const uint4*>(&sm.v[slot][tok][16 + 32 * half]);
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(b_empty + 8 * slot);
-        live = pos < hi && !((sm.smask[(pos - lo) >> 5] >> ((pos - lo) & 31)) & 1u);
-        uint2 klut = make_uint2(0, 0);
-        if (live) {
-          klut = make_klut<T>(f16_bits_to_f32(kmeta & 0xffffu), f16_bits_to_f32(kmeta >> 16));
-          vlut = make_vlut<T>(f16_bits_to_f32(vmeta & 0xffffu), f16_bits_to_f32(vmeta >> 16));
-        }
-        uint32_t r[32];
-        tc_lut_word(kc0.x, klut.x, klut.y, r);
-        tc_lut_word(kc0.y, klut.x, klut.y, r + 8);
-        tc_lut_word(kc0.z, klut.x, klut.y, r + 16);
-        tc_lut_word(kc0.w, klut.x, klut.y, r + 24);
-        tc::tmem_st32(t_a + 64 * half, r);
-        tc_lut_word(kc1.x, klut.x, klut.y, r);
-        tc_lut_word(kc1.y, klut.x, klut.y, r + 8);
-        tc_lut_word(kc1.z, klut.x, klut.y, r + 16);
-        tc_lut_word(kc1.w, klut.x, klut.y, r + 24);
-        tc::tmem_st32(t_a + 64 * half + 32, r);
-      } else {
-        // ---------- staged stage: the (128 q + tok)-th staged position, fp32 rows -> K (TMEM)
-        const int j = (st - n_int) * kTcStage + tok;
-        live = j < n_staged;
-        pos = hi;
-        const float* srow_k = a.stage_k;
-        if (live) {
-          int lo_w = 0, hi_w = nwords - 1;  // last word whose prefix count is <= j
-          while (lo_w < hi_w) {
-            const int mid = (lo_w + hi_w + 1) >> 1;
-            if (sm.spref[mid] <= j) lo_w = mid; else hi_w = mid - 1;
+    for (int it = 0; it <= nst; ++it) {
+      if (it < nst) {
+        // ======== operands of stage it
+        const int b = it & 1;
+        const uint32_t t_a = tmem + lane_base + (b ? kTcColA1 : kTcColA0);
+        int pos;
+        bool live;
+        uint4 vc = make_uint4(0, 0, 0, 0);
+        uint2 vlut = make_uint2(0, 0);
+        const float* srow_v = nullptr;
+        const bool is_int = it < n_int;
+        if (is_int) {
+          const int slot = it & 1;
+          pos = lo + it * kTcStage + tok;
+          wait(b_full + 8 * slot, (it >> 1) & 1);
+          const uint2 meta = *reinterpret_cast<const uint2*>(&sm.ka[slot][tok][0]);
+          const uint4 kc = *reinterpret_cast<const uint4*>((q == 0 ? sm.ka[slot][tok] : sm.kb[slot][tok]) + koff);
+          vc = *reinterpret_cast<const uint4*>((q < 3 ? sm.va[slot][tok] : sm.vb[slot][tok]) + voff);
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(b_empty + 8 * slot);
+          live = pos < hi && !((sm.smask[(pos - lo) >> 5] >> ((pos - lo) & 31)) & 1u);
+          // quarter 0 builds the token's K table, quarter 1 its V table; all read both
+          if (q < 2) {
+            uint2 lut = make_uint2(0, 0);
+            if (live) lut = q ? tc_vlut<T>(meta.y) : tc_klut<T>(meta.x);
+            (q ? sm.vlut : sm.klut)[tok] = lut;
           }
-          const int bit = (int)__fns(sm.smask[lo_w], 0u, j - sm.spref[lo_w] + 1);
-          pos = lo + 32 * lo_w + bit;
-          const int blk = sm.btab[(pos >> bs_log2) - page0];
-          const int64_t seat = (int64_t)(blk % (int)a.stage_rows) * bs + (pos & (bs - 1));
-          srow_k = a.stage_k + (seat * a.hk + h) * D;
+          tc::bar_sync(5, kTcCompute);
+          const uint2 klut = sm.klut[tok];
+          vlut = sm.vlut[tok];
+          uint32_t r[32];
+          tc_lut_word(kc.x, klut.x, klut.y, r);
+          tc_lut_word(kc.y, klut.x, klut.y, r + 8);
+          tc_lut_word(kc.z, klut.x, klut.y, r + 16);
+          tc_lut_word(kc.w, klut.x, klut.y, r + 24);
+          tc::tmem_st32(t_a + 32 * q, r);
+        } else {
+          // staged stage: the (128 (it - n_int) + tok)-th staged position, fp32 rows
+          const int j = (it - n_int) * kTcStage + tok;
+          live = j < n_staged;
+          pos = hi;
+          const float* srow_k = a.stage_k;
+          if (live) {
+            int lo_w = 0, hi_w = nwords - 1;  // last word whose prefix count is <= j
+            while (lo_w < hi_w) {
+              const int mid = (lo_w + hi_w + 1) >> 1;
+              if (sm.spref[mid] <= j) lo_w = mid; else hi_w = mid - 1;
+            }
+            const int bit = (int)__fns(sm.smask[lo_w], 0u, j - sm.spref[lo_w] + 1);
+            pos = lo + 32 * lo_w + bit;
+            const int blk = sm.btab[(pos >> bs_log2) - page0];
+            const int64_t seat = (int64_t)(blk % (int)a.stage_rows) * bs + (pos & (bs - 1));
+            srow_k = a.stage_k + (seat * a.hk + h) * D;
+          }
+          srow_v = a.stage_v + (srow_k - a.stage_k) + 64 * q;
+          srow_k += 64 * q;
+#pragma unroll 1
+          for (int w = 0; w < 4; ++w) {
+            uint32_t r[8];
+            tc_pack_word<T, false>(srow_k + 16 * w, live, r);
+            tc::tmem_st8(t_a + 32 * q + 8 * w, r);
+          }
         }
-        srow_v = a.stage_v + (srow_k - a.stage_k) + 128 * half;
-        srow_k += 128 * half;
-#pragma unroll 2
-        for (int w = 0; w < 8; ++w) {
-          uint32_t r[8];
-          tc_pack_word<T, false>(srow_k + 16 * w, live, r);
-          tc::tmem_st8(t_a + 64 * half + 8 * w, r);
+        if (q == 0) {
+          // bias k-step (columns 128..135): element 256 = 0 for live tokens, -inf for masked ones
+          const uint32_t bias[8] = {live ? 0u : neg_inf, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+          tc::tmem_st8(t_a + 128, bias);
         }
-      }
-      if (half == 0) {
-        // bias k-step (columns 128..135): element 256 = 0 for live tokens, -inf for masked ones
-        const uint32_t bias[8] = {live ? 0u : neg_inf, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-        tc::tmem_st8(t_a + 128, bias);
-      }
-      tc::tmem_wait_st();
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(b_k);
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(b_k + 8 * b);
 
-      // ---------- V -> V^T (after the previous stage's PV freed V^T, P^T and O)
-      if (st > 0) {
-        wait(b_pv, (st - 1) & 1);
-        tc::tc_fence_after();
-      }
-      if (is_int) {
-        const uint32_t vw[8] = {vc0.x, vc0.y, vc0.z, vc0.w, vc1.x, vc1.y, vc1.z, vc1.w};
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          uint32_t r[8];
-          tc_lut_word(vw[j], vlut.x, vlut.y, r);
-          *reinterpret_cast<uint4*>(vt_row + (2 * j) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
-          *reinterpret_cast<uint4*>(vt_row + (2 * j + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
+        // V -> V^T[b], once the PV of stage it - 2 (the last reader of V^T[b]) is done
+        if (it >= 2) {
+          wait(b_pv, (it - 2) & 1);
+          tc::tc_fence_after();
         }
-      } else {
-#pragma unroll 2
-        for (int j = 0; j < 8; ++j) {
-          uint32_t r[8];
-          tc_pack_word<T, true>(srow_v + 16 * j, live, r);
-          *reinterpret_cast<uint4*>(vt_row + (2 * j) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
-          *reinterpret_cast<uint4*>(vt_row + (2 * j + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
+        uint8_t* vt_row = sm.vt[b] + vt_off;
+        if (is_int) {
+          const uint32_t vw[4] = {vc.x, vc.y, vc.z, vc.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t r[8];
+            tc_lut_word(vw[j], vlut.x, vlut.y, r);
+            *reinterpret_cast<uint4*>(vt_row + (2 * j) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
+            *reinterpret_cast<uint4*>(vt_row + (2 * j + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
+          }
+        } else {
+#pragma unroll 1
+          for (int j = 0; j < 4; ++j) {
+            uint32_t r[8];
+            tc_pack_word<T, true>(srow_v + 16 * j, live, r);
+            *reinterpret_cast<uint4*>(vt_row + (2 * j) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
+            *reinterpret_cast<uint4*>(vt_row + (2 * j + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
+          }
         }
-      }
-
-      // ---------- scores of rows [16 half, +16): x = S * scale (log2 units)
-      wait(b_s, st & 1);
-      tc::tc_fence_after();
-      float x[16];
-      {
-        uint32_t sraw[16];
-        tc::tmem_ld16(t_s, sraw);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int r = 0; r < 16; ++r) x[r] = __uint_as_float(sraw[r]) * scale;
-      }
-      if (need_lim) {
-#pragma unroll
-        for (int r = 0; r < 16; ++r)
-          if (pos >= sm.lim[16 * half + r]) x[r] = -INFINITY;
-      }
-      bool need = false;
-#pragma unroll
-      for (int r = 0; r < 16; ++r) need = need || (x[r] > mrow[r] + kTcHeadroom);
-      if (tc::bar_or(1 + half, 128, need)) {
-        // new row maxima over the stage's 128 tokens; rescale l and (if they moved) O
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-          const int v = __reduce_max_sync(0xffffffffu, tc_ord(x[r]));
-          if (lane == 0) sm.red[warp][r] = v;
+        tc::fence_async_smem();
+        if (it == 0) {
+          pos_prev = pos;
+          continue;  // no softmax yet
         }
-        tc::bar_sync(1 + half, 128);
-        float alpha[16];
-        bool moved = false;
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-          const int k = max(max(sm.red[4 * half][r], sm.red[4 * half + 1][r]),
-                            max(sm.red[4 * half + 2][r], sm.red[4 * half + 3][r]));
-          const float mn = fmaxf(mrow[r], tc_unord(k));
-          alpha[r] = (mrow[r] == -INFINITY) ? 0.0f : tc_exp2(mrow[r] - mn);
-          moved = moved || alpha[r] != 1.0f;
-          lrow[r] *= alpha[r];
-          mrow[r] = mn;
-        }
-        tc::bar_sync(1 + half, 128);
-        if (st > 0 && moved) {
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            uint32_t o[16];
-            tc::tmem_ld16(t_o + 32 * hh, o);
+        const int pos_it = pos;
+        // fall through to the softmax of stage it - 1 with pos_prev, then carry pos_it
+        {
+          const int st = it - 1;
+          // ======== softmax of stage st
+          wait(b_s + 8 * (st & 1), (st >> 1) & 1);
+          tc::tc_fence_after();
+          const uint32_t t_s = tmem + lane_base + kTcColS + 32 * (st & 1) + 8 * q;
+          const uint32_t t_o = tmem + lane_base + kTcColO + 8 * q;
+          float x[8];
+          {
+            uint32_t sraw[8];
+            tc::tmem_ld8(t_s, sraw);
             tc::tmem_wait_ld();
 #pragma unroll
-            for (int r = 0; r < 16; ++r) o[r] = __float_as_uint(__uint_as_float(o[r]) * alpha[r]);
-            tc::tmem_st16(t_o + 32 * hh, o);
+            for (int r = 0; r < 8; ++r) x[r] = __uint_as_float(sraw[r]) * scale;
           }
-          tc::tmem_wait_st();
-        }
-      }
-      // ---------- P^T (fp16) and l
-      uint32_t pk[8];
+          if (need_lim) {
 #pragma unroll
-      for (int r = 0; r < 16; r += 2) {
-        const float m0 = (mrow[r] == -INFINITY) ? 0.0f : mrow[r];
-        const float m1 = (mrow[r + 1] == -INFINITY) ? 0.0f : mrow[r + 1];
-        const float p0 = tc_exp2(x[r] - m0), p1 = tc_exp2(x[r + 1] - m1);
-        lrow[r] += p0;
-        lrow[r + 1] += p1;
-        const __half2 ph = __floats2half2_rn(p0, p1);
-        pk[r >> 1] = *reinterpret_cast<const uint32_t*>(&ph);
+            for (int r = 0; r < 8; ++r)
+              if (pos_prev >= sm.lim[8 * q + r]) x[r] = -INFINITY;
+          }
+          bool need = false;
+#pragma unroll
+          for (int r = 0; r < 8; ++r) need = need || (x[r] > mrow[r] + kTcHeadroom);
+          if (tc::bar_or(1 + q, 128, need)) {
+            // new row maxima over the stage's 128 tokens; rescale l and (if they moved) O.
+            // (the reduction buffer alternates: the vote barrier of any later stage
+            // orders these reads before the buffer's next writes)
+            int(*red)[8] = sm.red[nslow & 1];
+            ++nslow;
+            int rm[8];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) rm[r] = __reduce_max_sync(0xffffffffu, tc_ord(x[r]));
+            if (lane == 0) {
+              *reinterpret_cast<int4*>(&red[warp][0]) = make_int4(rm[0], rm[1], rm[2], rm[3]);
+              *reinterpret_cast<int4*>(&red[warp][4]) = make_int4(rm[4], rm[5], rm[6], rm[7]);
+            }
+            tc::bar_sync(1 + q, 128);
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              if (w == (warp & 3)) continue;  // own warp's maxima are already in rm
+              const int4 a4 = *reinterpret_cast<const int4*>(&red[4 * q + w][0]);
+              const int4 b4 = *reinterpret_cast<const int4*>(&red[4 * q + w][4]);
+              rm[0] = max(rm[0], a4.x);
+              rm[1] = max(rm[1], a4.y);
+              rm[2] = max(rm[2], a4.z);
+              rm[3] = max(rm[3], a4.w);
+              rm[4] = max(rm[4], b4.x);
+              rm[5] = max(rm[5], b4.y);
+              rm[6] = max(rm[6], b4.z);
+              rm[7] = max(rm[7], b4.w);
+            }
+            float alpha[8];
+            bool moved = false;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+              const float mn = fmaxf(mrow[r], tc_unord(rm[r]));
+              alpha[r] = (mrow[r] == -INFINITY) ? 0.0f : tc_exp2(mrow[r] - mn);
+              moved = moved || alpha[r] != 1.0f;
+              lrow[r] *= alpha[r];
+              mrow[r] = mn;
+              muse[r] = (mn == -INFINITY) ? 0.0f : mn;
+            }
+            if (st > 0 && moved) {
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                uint32_t o[8];
+                tc::tmem_ld8(t_o + 32 * hh, o);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int r = 0; r < 8; ++r) o[r] = __float_as_uint(__uint_as_float(o[r]) * alpha[r]);
+                tc::tmem_st8(t_o + 32 * hh, o);
+              }
+              tc::tmem_wait_st();
+            }
+          }
+          // P^T[st & 1] (fp16) and l
+          uint32_t pk[4];
+#pragma unroll
+          for (int r = 0; r < 8; r += 2) {
+            const float p0 = tc_exp2(x[r] - muse[r]), p1 = tc_exp2(x[r + 1] - muse[r + 1]);
+            lrow[r] += p0;
+            lrow[r + 1] += p1;
+            const __half2 ph = __floats2half2_rn(p0, p1);
+            pk[r >> 1] = *reinterpret_cast<const uint32_t*>(&ph);
+          }
+          *reinterpret_cast<uint4*>(sm.pt[st & 1] + pt_off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          tc::fence_async_smem();
+          tc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(b_p);
+        }
+        pos_prev = pos_it;
+      } else if (it >= 1) {
+        // ======== last softmax (stage nst - 1); O must hold every earlier stage before a rescale
+        const int st = it - 1;
+        if (st >= 1) {
+          wait(b_pv, (st - 1) & 1);
+          tc::tc_fence_after();
+        }
+        wait(b_s + 8 * (st & 1), (st >> 1) & 1);
+        tc::tc_fence_after();
+        const uint32_t t_s = tmem + lane_base + kTcColS + 32 * (st & 1) + 8 * q;
+        const uint32_t t_o = tmem + lane_base + kTcColO + 8 * q;
+        float x[8];
+        {
+          uint32_t sraw[8];
+          tc::tmem_ld8(t_s, sraw);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int r = 0; r < 8; ++r) x[r] = __uint_as_float(sraw[r]) * scale;
+        }
+        if (need_lim) {
+#pragma unroll
+          for (int r = 0; r < 8; ++r)
+            if (pos_prev >= sm.lim[8 * q + r]) x[r] = -INFINITY;
+        }
+        bool need = false;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) need = need || (x[r] > mrow[r] + kTcHeadroom);
+        if (tc::bar_or(1 + q, 128, need)) {
+          // new row maxima over the stage's 128 tokens; rescale l and (if they moved) O.
+          // (the reduction buffer alternates: the vote barrier of any later stage
+          // orders these reads before the buffer's next writes)
+          int(*red)[8] = sm.red[nslow & 1];
+          ++nslow;
+          int rm[8];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) rm[r] = __reduce_max_sync(0xffffffffu, tc_ord(x[r]));
+          if (lane == 0) {
+            *reinterpret_cast<int4*>(&red[warp][0]) = make_int4(rm[0], rm[1], rm[2], rm[3]);
+            *reinterpret_cast<int4*>(&red[warp][4]) = make_int4(rm[4], rm[5], rm[6], rm[7]);
+          }
+          tc::bar_sync(1 + q, 128);
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            if (w == (warp & 3)) continue;  // own warp's maxima are already in rm
+            const int4 a4 = *reinterpret_cast<const int4*>(&red[4 * q + w][0]);
+            const int4 b4 = *reinterpret_cast<const int4*>(&red[4 * q + w][4]);
+            rm[0] = max(rm[0], a4.x);
+            rm[1] = max(rm[1], a4.y);
+            rm[2] = max(rm[2], a4.z);
+            rm[3] = max(rm[3], a4.w);
+            rm[4] = max(rm[4], b4.x);
+            rm[5] = max(rm[5], b4.y);
+            rm[6] = max(rm[6], b4.z);
+            rm[7] = max(rm[7], b4.w);
+          }
+          float alpha[8];
+          bool moved = false;
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            const float mn = fmaxf(mrow[r], tc_unord(rm[r]));
+            alpha[r] = (mrow[r] == -INFINITY) ? 0.0f : tc_exp2(mrow[r] - mn);
+            moved = moved || alpha[r] != 1.0f;
+            lrow[r] *= alpha[r];
+            mrow[r] = mn;
+            muse[r] = (mn == -INFINITY) ? 0.0f : mn;
+          }
+          if (st > 0 && moved) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              uint32_t o[8];
+              tc::tmem_ld8(t_o + 32 * hh, o);
+              tc::tmem_wait_ld();
+#pragma unroll
+              for (int r = 0; r < 8; ++r) o[r] = __float_as_uint(__uint_as_float(o[r]) * alpha[r]);
+              tc::tmem_st8(t_o + 32 * hh, o);
+            }
+            tc::tmem_wait_st();
+          }
+        }
+        // P^T[st & 1] (fp16) and l
+        uint32_t pk[4];
+#pragma unroll
+        for (int r = 0; r < 8; r += 2) {
+          const float p0 = tc_exp2(x[r] - muse[r]), p1 = tc_exp2(x[r + 1] - muse[r + 1]);
+          lrow[r] += p0;
+          lrow[r + 1] += p1;
+          const __half2 ph = __floats2half2_rn(p0, p1);
+          pk[r >> 1] = *reinterpret_cast<const uint32_t*>(&ph);
+        }
+        *reinterpret_cast<uint4*>(sm.pt[st & 1] + pt_off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(b_p);
       }
-      *reinterpret_cast<uint4*>(pt_row) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      *reinterpret_cast<uint4*>(pt_row + kTcVtSbo) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-      tc::fence_async_smem();
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(b_p);
     }
 
     // ---------------- epilogue: l over the 128 tokens, normalised partial O and LSE
@@ -523,39 +718,39 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::tc_fence_after();
     }
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
+    for (int r = 0; r < 8; ++r) {
       float v = lrow[r];
 #pragma unroll
       for (int o2 = 16; o2 > 0; o2 >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o2);
-      if (lane == 0) sm.red[warp][r] = __float_as_int(v);
+      if (lane == 0) sm.lsum[warp][r] = v;
     }
-    tc::bar_sync(1 + half, 128);
-    float L[16];
+    tc::bar_sync(1 + q, 128);
+    float L[8];
 #pragma unroll
-    for (int r = 0; r < 16; ++r)
-      L[r] = (__int_as_float(sm.red[4 * half][r]) + __int_as_float(sm.red[4 * half + 1][r])) +
-             (__int_as_float(sm.red[4 * half + 2][r]) + __int_as_float(sm.red[4 * half + 3][r]));
+    for (int r = 0; r < 8; ++r)
+      L[r] = (sm.lsum[4 * q][r] + sm.lsum[4 * q + 1][r]) + (sm.lsum[4 * q + 2][r] + sm.lsum[4 * q + 3][r]);
     const int64_t pslot = p.part_begin[ri] + sp;
-    const int64_t prow0 = (pslot * a.hk + h) * kTcRows + 16 * half;
+    const int64_t prow0 = (pslot * a.hk + h) * kTcRows + 8 * q;
+    const uint32_t t_o = tmem + lane_base + kTcColO + 8 * q;
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
-      uint32_t o[16];
+      uint32_t o[8];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) o[r] = 0u;
+      for (int r = 0; r < 8; ++r) o[r] = 0u;
       if (nst > 0) {
-        tc::tmem_ld16(t_o + 32 * hh, o);
+        tc::tmem_ld8(t_o + 32 * hh, o);
         tc::tmem_wait_ld();
       }
       const int dim = tc_dim(128 * hh + tok);
 #pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        const bool keep = (16 * half + r < R) && (L[r] > 0.0f || L[r] != L[r]);
+      for (int r = 0; r < 8; ++r) {
+        const bool keep = (8 * q + r < R) && (L[r] > 0.0f || L[r] != L[r]);
         if (keep) a.part_o[(prow0 + r) * D + dim] = __uint_as_float(o[r]) / L[r];
       }
     }
 #pragma unroll
-    for (int r = 0; r < 16; ++r)
-      if (tok == r && 16 * half + r < R)
+    for (int r = 0; r < 8; ++r)
+      if (tok == r && 8 * q + r < R)
         a.part_lse[prow0 + r] =
             (L[r] > 0.0f || L[r] != L[r]) ? (mrow[r] + log2f(L[r])) * 0.69314718055994531f : -INFINITY;
   }
@@ -564,7 +759,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
-  if (warp == 8) tc::tmem_dealloc(tmem, kTcCols);
+  if (warp == kWarps) tc::tmem_dealloc(tmem, kTcCols);
 }
 
 }  // namespace oscar

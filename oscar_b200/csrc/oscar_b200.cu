@@ -508,8 +508,8 @@ int run_decode_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs,
   }
   CUtensorMap tmk, tmv;
   const int box_y = std::min(base.bs, oscar::kTcStage);
-  if (!make_cache_map(&tmk, base.kc, base.num_blocks, base.bs, base.kst, 96, box_y) ||
-      !make_cache_map(&tmv, base.vc, base.num_blocks, base.bs, base.vst, 64, box_y))
+  if (!make_cache_map(&tmk, base.kc, base.num_blocks, base.bs, base.kst, oscar::kTcRow, box_y) ||
+      !make_cache_map(&tmv, base.vc, base.num_blocks, base.bs, base.vst, oscar::kTcRow, box_y))
     return kDecodeNoFit;
   for (const DecodePlanned& pl : plans) {
     oscar::AttnArgs a = base;
