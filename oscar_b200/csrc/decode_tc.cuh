@@ -420,6 +420,7 @@ __global__ void __maxnreg__(96)
     const int pt_off = q * kTcVtSbo + (tok >> 3) * 128 + (tok & 7) * 16;
 
     for (int it = 0; it <= nst; ++it) {
+      int pos_it = hi;
       if (it < nst) {
         // ======== operands of stage it
         const int b = it & 1;
@@ -517,111 +518,15 @@ __global__ void __maxnreg__(96)
           }
         }
         tc::fence_async_smem();
-        if (it == 0) {
-          pos_prev = pos;
-          continue;  // no softmax yet
-        }
-        const int pos_it = pos;
-        // fall through to the softmax of stage it - 1 with pos_prev, then carry pos_it
-        {
-          const int st = it - 1;
-          // ======== softmax of stage st
-          wait(b_s + 8 * (st & 1), (st >> 1) & 1);
-          tc::tc_fence_after();
-          const uint32_t t_s = tmem + lane_base + kTcColS + 32 * (st & 1) + 8 * q;
-          const uint32_t t_o = tmem + lane_base + kTcColO + 8 * q;
-          float x[8];
-          {
-            uint32_t sraw[8];
-            tc::tmem_ld8(t_s, sraw);
-            tc::tmem_wait_ld();
-#pragma unroll
-            for (int r = 0; r < 8; ++r) x[r] = __uint_as_float(sraw[r]) * scale;
-          }
-          if (need_lim) {
-#pragma unroll
-            for (int r = 0; r < 8; ++r)
-              if (pos_prev >= sm.lim[8 * q + r]) x[r] = -INFINITY;
-          }
-          bool need = false;
-#pragma unroll
-          for (int r = 0; r < 8; ++r) need = need || (x[r] > mrow[r] + kTcHeadroom);
-          if (tc::bar_or(1 + q, 128, need)) {
-            // new row maxima over the stage's 128 tokens; rescale l and (if they moved) O.
-            // (the reduction buffer alternates: the vote barrier of any later stage
-            // orders these reads before the buffer's next writes)
-            int(*red)[8] = sm.red[nslow & 1];
-            ++nslow;
-            int rm[8];
-#pragma unroll
-            for (int r = 0; r < 8; ++r) rm[r] = __reduce_max_sync(0xffffffffu, tc_ord(x[r]));
-            if (lane == 0) {
-              *reinterpret_cast<int4*>(&red[warp][0]) = make_int4(rm[0], rm[1], rm[2], rm[3]);
-              *reinterpret_cast<int4*>(&red[warp][4]) = make_int4(rm[4], rm[5], rm[6], rm[7]);
-            }
-            tc::bar_sync(1 + q, 128);
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-              if (w == (warp & 3)) continue;  // own warp's maxima are already in rm
-              const int4 a4 = *reinterpret_cast<const int4*>(&red[4 * q + w][0]);
-              const int4 b4 = *reinterpret_cast<const int4*>(&red[4 * q + w][4]);
-              rm[0] = max(rm[0], a4.x);
-              rm[1] = max(rm[1], a4.y);
-              rm[2] = max(rm[2], a4.z);
-              rm[3] = max(rm[3], a4.w);
-              rm[4] = max(rm[4], b4.x);
-              rm[5] = max(rm[5], b4.y);
-              rm[6] = max(rm[6], b4.z);
-              rm[7] = max(rm[7], b4.w);
-            }
-            float alpha[8];
-            bool moved = false;
-#pragma unroll
-            for (int r = 0; r < 8; ++r) {
-              const float mn = fmaxf(mrow[r], tc_unord(rm[r]));
-              alpha[r] = (mrow[r] == -INFINITY) ? 0.0f : tc_exp2(mrow[r] - mn);
-              moved = moved || alpha[r] != 1.0f;
-              lrow[r] *= alpha[r];
-              mrow[r] = mn;
-              muse[r] = (mn == -INFINITY) ? 0.0f : mn;
-            }
-            if (st > 0 && moved) {
-#pragma unroll
-              for (int hh = 0; hh < 2; ++hh) {
-                uint32_t o[8];
-                tc::tmem_ld8(t_o + 32 * hh, o);
-                tc::tmem_wait_ld();
-#pragma unroll
-                for (int r = 0; r < 8; ++r) o[r] = __float_as_uint(__uint_as_float(o[r]) * alpha[r]);
-                tc::tmem_st8(t_o + 32 * hh, o);
-              }
-              tc::tmem_wait_st();
-            }
-          }
-          // P^T[st & 1] (fp16) and l
-          uint32_t pk[4];
-#pragma unroll
-          for (int r = 0; r < 8; r += 2) {
-            const float p0 = tc_exp2(x[r] - muse[r]), p1 = tc_exp2(x[r + 1] - muse[r + 1]);
-            lrow[r] += p0;
-            lrow[r + 1] += p1;
-            const __half2 ph = __floats2half2_rn(p0, p1);
-            pk[r >> 1] = *reinterpret_cast<const uint32_t*>(&ph);
-          }
-          *reinterpret_cast<uint4*>(sm.pt[st & 1] + pt_off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          tc::fence_async_smem();
-          tc::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(b_p);
-        }
-        pos_prev = pos_it;
-      } else if (it >= 1) {
-        // ======== last softmax (stage nst - 1); O must hold every earlier stage before a rescale
+        pos_it = pos;
+      } else if (it >= 2) {
+        // last softmax: O must hold every earlier stage before a rescale
+        wait(b_pv, (it - 2) & 1);
+        tc::tc_fence_after();
+      }
+      if (it >= 1) {
+        // ======== softmax of stage st = it - 1 (its QK ran meanwhile)
         const int st = it - 1;
-        if (st >= 1) {
-          wait(b_pv, (st - 1) & 1);
-          tc::tc_fence_after();
-        }
         wait(b_s + 8 * (st & 1), (st >> 1) & 1);
         tc::tc_fence_after();
         const uint32_t t_s = tmem + lane_base + kTcColS + 32 * (st & 1) + 8 * q;
@@ -710,6 +615,7 @@ __global__ void __maxnreg__(96)
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(b_p);
       }
+      pos_prev = pos_it;
     }
 
     // ---------------- epilogue: l over the 128 tokens, normalised partial O and LSE
