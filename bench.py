@@ -38,6 +38,7 @@ METRIC = "INT2-KV attn query-tok/s & HBM GB/s vs peak; 8x24K MTP step latency"
 UNIT = "query_tokens/s"
 WORKLOAD = "cfg3_mtp_8x24k"
 BYTES_PER_TOKEN_HEAD = 136  # 64 B K codes + 64 B V codes + 8 B scale/zero
+BYTES_PER_STAGED = 2 * 256 * 4  # fp32 K and V staging rows of a staged (sink/recent) token
 
 
 def parse():
@@ -64,6 +65,20 @@ def workload_config(layers):
 
 # ---------------------------------------------------------------------------
 # GPU arm
+def count_staged(torch, lay):
+    """History positions whose staging seat is owned by their block (read from
+    the fp32 staging rows instead of the INT2 codes)."""
+    case = lay.case
+    owner = lay.layer._oscar_slot_owner.reshape(-1)
+    rows = owner.numel() // 128
+    n = 0
+    for r, (seq, ql) in enumerate(zip(case.seqs, np.diff(case.qsl))):
+        pos = torch.arange(int(seq) - int(ql), device=owner.device)
+        blk = case.bt[r, pos // 128].long()
+        n += int((owner[(blk % rows) * 128 + pos % 128] == blk).sum())
+    return n
+
+
 def build_layers(torch, dev, n_layers):
     from oscar_b200 import synthetic
     from oscar_b200.backend import OscarAttentionBackendImpl
@@ -269,7 +284,8 @@ def run_gpu(args):
     n_attn = max(args.steps, 2 * L)
     ms_attn = timed(torch, dev, attn, n_attn, dist) / n_attn
     hist = sum(layers[0].case.seqs) - layers[0].q.shape[0]
-    alg_bytes = BYTES_PER_TOKEN_HEAD * hist * 1
+    staged = count_staged(torch, layers[0])
+    alg_bytes = BYTES_PER_TOKEN_HEAD * hist + BYTES_PER_STAGED * staged
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = float(peaks.get("hbm_gbs", 6650.0))
     achieved = alg_bytes / (ms_attn * 1e-3) / 1e9
@@ -317,8 +333,8 @@ def run_gpu(args):
                 "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e / args.steps},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "kernel": "slab attention pass (decode_attn_kernel with its staged items + decode_combine_kernel)",
-                     "launch_us": ms_attn * 1e3, "algorithmic_bytes": alg_bytes,
+                     "traffic": traffic, "kernel": "slab attention pass (decode_tc_kernel + decode_combine_kernel)",
+                     "launch_us": ms_attn * 1e3, "algorithmic_bytes": alg_bytes, "staged_tokens": staged,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6650 GB/s"},
         "clocks": clk,
     }

@@ -186,6 +186,21 @@ int oscar_merge_slab(float* out, float* lse, int64_t out_rows, /* [out_rows, num
                      int64_t query_start, const int32_t* query_ids,
                      void* stream);
 
+/* Per-layer rotation of head vectors: out = x @ R (transpose = 0) or
+ * x @ R^T (transpose = 1), fp32 products and sums.  No counterpart in the
+ * reference's kernel API: backend.py:238-246 (and the k/q/v/output rotations
+ * of backend.py:151-198, 334-393) run it as fp32 library GEMMs.  x holds
+ * `rows` vectors of head_dim (64, 128 or 256) elements of x_dtype, x_stride
+ * elements apart (a multiple of 8; x 16-byte aligned); rot is
+ * [head_dim, head_dim] fp32 row-major, 16-byte aligned.
+ * Either output may be null: out (out_dtype, out_stride elements between rows)
+ * and out_f32 (fp32, out_f32_stride).  Asynchronous on `stream`. */
+int oscar_rotate_rows(const void* x, int32_t x_dtype, int64_t rows, int64_t x_stride, int32_t head_dim,
+                      const float* rot, int32_t transpose,
+                      void* out, int32_t out_dtype, int64_t out_stride,
+                      float* out_f32, int64_t out_f32_stride,
+                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif

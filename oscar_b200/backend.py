@@ -133,10 +133,9 @@ class OscarAttentionImplMixin:
             layer._oscar_rots = (rk, rv)
         return rk, rv
 
-    def _rotate(self, x: torch.Tensor, rot: torch.Tensor) -> torch.Tensor:
-        """x @ R in fp32 (plain library GEMM), [N, H, D] -> fp32 [N, H, D]."""
-        n, h, d = x.shape
-        return torch.matmul(x.reshape(n * h, d).float(), rot).view(n, h, d)
+    def _rotate(self, x: torch.Tensor, rot: torch.Tensor, out_dtype=torch.float32) -> torch.Tensor:
+        """x @ R in fp32, [N, H, D] -> [N, H, D] of out_dtype (rotate_rows)."""
+        return kernels.rotate_rows(x, rot, out_dtype=out_dtype)[0]
 
     # ------------------------------------------------------------------ write path
     def _store(self, layer, key, value, slot_mapping, *, invalidate: bool):
@@ -147,12 +146,18 @@ class OscarAttentionImplMixin:
         if invalidate and getattr(layer, "_oscar_stage_ready", False):
             kernels.staging_invalidate(slot_mapping, layer._oscar_slot_owner, self.stage_block)
         rk, rv = self._layer_rots(layer, k.device)
-        k_rot, v_rot = self._rotate(k, rk), self._rotate(v, rv)
+        # one pass per tensor: fp32 rows for the store / staging window and the
+        # model-dtype rows the attention reads (x @ R then .to(dtype), backend.py:360-366)
+        k_rot, v_rot = (torch.empty(n, hk, d, dtype=torch.float32, device=k.device) for _ in range(2))
+        k_lo = torch.empty((n, hk, d), dtype=k.dtype, device=k.device)
+        v_lo = torch.empty((n, hk, d), dtype=v.dtype, device=v.device)
+        kernels.rotate_rows(k, rk, out=k_lo, out_f32=k_rot)
+        kernels.rotate_rows(v, rv, out=v_lo, out_f32=v_rot)
         kernels.oscar_store(k_rot, v_rot, self.key_cache, self.value_cache, slot_mapping,
                             self._oscar.k_clip_ratio, self._oscar.v_clip_ratio)
         self._oscar_stats["writes"] += 1
         self._oscar_stats["kv_bytes_written"] += n * hk * 160
-        return k_rot, v_rot
+        return k_rot, v_rot, k_lo, v_lo
 
     def do_kv_cache_update(self, layer, key, value, kv_cache, slot_mapping) -> None:
         """backend.py:151-198: owner invalidation -> rotate -> clip/INT2 store."""
@@ -230,12 +235,16 @@ class OscarAttentionImplMixin:
                 rotated = self._store(layer, key, value, slots, invalidate=not self._oscar.window_enabled)
             if self._oscar.window_enabled:
                 self._ensure_staging(layer, kv_cache)
-                self._staging_write(layer, key, value, attn_metadata, rotated=rotated)
+                self._staging_write(layer, key, value, attn_metadata, rotated=None if rotated is None else rotated[:2])
+            return self._streaming_attention(layer, query, key, value, kv_cache, attn_metadata, output,
+                                             rotated_lo=None if rotated is None else rotated[2:])
         return self._streaming_attention(layer, query, key, value, kv_cache, attn_metadata, output)
 
-    def _streaming_attention(self, layer, query, key, value, kv_cache, metadata, output):
+    def _streaming_attention(self, layer, query, key, value, kv_cache, metadata, output, rotated_lo=None):
         """backend.py:334-393: prefix-free requests attend their own chunk in
-        the model's domain; cached requests go through the rotated INT2 path."""
+        the model's domain; cached requests go through the rotated INT2 path.
+        ``rotated_lo`` holds the store path's (x @ R).to(dtype) rows of key and
+        value, reused instead of rotating them again."""
         if (key is None) != (value is None):
             raise ValueError("Both new K and V must be supplied together")
         actual = min(query.shape[0], metadata.num_actual_tokens)
@@ -279,9 +288,14 @@ class OscarAttentionImplMixin:
                 v_in = None if v_all is None else v_all[ids]
             if rotate:
                 rk, rv = self._layer_rots(layer, query.device)
-                q_in = self._rotate(q_in, rk).to(query.dtype)
-                k_in = None if k_in is None else self._rotate(k_in, rk).to(query.dtype)
-                v_in = None if v_in is None else self._rotate(v_in, rv).to(query.dtype)
+                q_in = self._rotate(q_in, rk, query.dtype)
+                if k_in is not None and rotated_lo is not None and rotated_lo[0].shape[0] >= covered:
+                    k_lo, v_lo = rotated_lo
+                    k_in = k_lo[:covered] if ids is None else k_lo[ids]
+                    v_in = v_lo[:covered] if ids is None else v_lo[ids]
+                else:
+                    k_in = None if k_in is None else self._rotate(k_in, rk, query.dtype)
+                    v_in = None if v_in is None else self._rotate(v_in, rv, query.dtype)
                 stage = self._stage(layer)
             else:
                 stage = None
@@ -290,7 +304,11 @@ class OscarAttentionImplMixin:
                                             workspace_bytes=self._oscar.stream_workspace_bytes)
             if rotate:
                 m = out.shape[0]
-                out = torch.matmul(out.view(m * hq, d), rv.t()).view(m, hq, d)
+                if ids is None and out_rows.is_contiguous():
+                    # o @ R_v^T straight into the output rows, in the output dtype
+                    kernels.rotate_rows(out, rv, transpose=True, out=out_rows[:m].view(m, hq, d))
+                    continue
+                out = kernels.rotate_rows(out, rv, transpose=True, out_dtype=output.dtype)[0]
             result = out.to(output.dtype).view(out.shape[0], hq * d)
             if ids is None:
                 out_rows[: result.shape[0]].copy_(result)

@@ -14,6 +14,7 @@
 #include "attention.cuh"
 #include "decode.cuh"
 #include "decode_tc.cuh"
+#include "rotate.cuh"
 #include "store.cuh"
 
 namespace {
@@ -815,3 +816,67 @@ int oscar_staging_write_noalloc(const float* k_rot, const float* v_rot, int64_t 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// per-layer rotation of head vectors (backend.py:238-246 applies it with
+// library GEMMs); no counterpart entry point in the reference's kernel API
+namespace {
+
+template <typename InT, typename OutT, int D>
+int launch_rotate_d(const void* x, int64_t rows, int64_t xs, const float* rot, int tr, void* out, int64_t os,
+                    float* of, int64_t ofs, cudaStream_t s) {
+  constexpr size_t smem = (size_t)(D * oscar::kRotCols + oscar::kRotRows * D) * sizeof(float);
+  static thread_local int cfg_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cfg_dev != dev) {
+    cudaFuncSetAttribute(oscar::rotate_rows_kernel<InT, OutT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    cfg_dev = dev;
+  }
+  dim3 grid((unsigned)((rows + oscar::kRotRows - 1) / oscar::kRotRows), (unsigned)(D / oscar::kRotCols));
+  oscar::rotate_rows_kernel<InT, OutT, D><<<grid, 256, smem, s>>>(
+      reinterpret_cast<const InT*>(x), xs, rows, rot, tr, reinterpret_cast<OutT*>(out), os, of, ofs);
+  return cuda_status("rotate_rows_kernel");
+}
+
+template <typename InT, typename OutT>
+int launch_rotate(const void* x, int64_t rows, int64_t xs, int d, const float* rot, int tr, void* out, int64_t os,
+                  float* of, int64_t ofs, cudaStream_t s) {
+  if (d == 256) return launch_rotate_d<InT, OutT, 256>(x, rows, xs, rot, tr, out, os, of, ofs, s);
+  if (d == 128) return launch_rotate_d<InT, OutT, 128>(x, rows, xs, rot, tr, out, os, of, ofs, s);
+  return launch_rotate_d<InT, OutT, 64>(x, rows, xs, rot, tr, out, os, of, ofs, s);
+}
+
+template <typename InT>
+int rotate_out(int out_dtype, const void* x, int64_t rows, int64_t xs, int d, const float* rot, int tr, void* out,
+               int64_t os, float* of, int64_t ofs, cudaStream_t s) {
+  if (out == nullptr || out_dtype == OSCAR_DTYPE_F32)
+    return launch_rotate<InT, float>(x, rows, xs, d, rot, tr, out, os, of, ofs, s);
+  if (out_dtype == OSCAR_DTYPE_BF16) return launch_rotate<InT, __nv_bfloat16>(x, rows, xs, d, rot, tr, out, os, of, ofs, s);
+  return launch_rotate<InT, __half>(x, rows, xs, d, rot, tr, out, os, of, ofs, s);
+}
+
+}  // namespace
+
+extern "C" int oscar_rotate_rows(const void* x, int32_t x_dtype, int64_t rows, int64_t x_stride, int32_t head_dim,
+                                 const float* rot, int32_t transpose, void* out, int32_t out_dtype, int64_t out_stride,
+                                 float* out_f32, int64_t out_f32_stride, void* stream) {
+  if (rows < 0 || (head_dim != 64 && head_dim != 128 && head_dim != 256))
+    return fail(OSCAR_ERR_INVALID, "rotate: D=%d must be 64, 128 or 256", head_dim);
+  if (x_dtype < 0 || x_dtype > 2 || out_dtype < 0 || out_dtype > 2) return fail(OSCAR_ERR_INVALID, "rotate: bad dtype");
+  if (rows == 0 || (out == nullptr && out_f32 == nullptr)) return OSCAR_OK;
+  if (x == nullptr || rot == nullptr) return fail(OSCAR_ERR_INVALID, "rotate: null pointer");
+  if ((reinterpret_cast<uintptr_t>(rot) | reinterpret_cast<uintptr_t>(x)) & 15 || (rows > 1 && x_stride % 8))
+    return fail(OSCAR_ERR_INVALID, "rotate: x and the rotation must be 16-byte aligned, x rows a multiple of 8 apart");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (x_dtype == OSCAR_DTYPE_F32)
+    return rotate_out<float>(out_dtype, x, rows, x_stride, head_dim, rot, transpose, out, out_stride, out_f32,
+                             out_f32_stride, s);
+  if (x_dtype == OSCAR_DTYPE_BF16)
+    return rotate_out<__nv_bfloat16>(out_dtype, x, rows, x_stride, head_dim, rot, transpose, out, out_stride, out_f32,
+                                     out_f32_stride, s);
+  return rotate_out<__half>(out_dtype, x, rows, x_stride, head_dim, rot, transpose, out, out_stride, out_f32,
+                            out_f32_stride, s);
+}
+

@@ -241,6 +241,35 @@ def merge_slab(output, lse, part, part_lse, start, ids) -> None:
 _PATHS = {"auto": 0, "tile": 1, "decode": 2, "tensor": 3}
 
 
+def rotate_rows(x: torch.Tensor, rot: torch.Tensor, *, transpose: bool = False, out: torch.Tensor | None = None,
+                out_f32: torch.Tensor | None = None, out_dtype: torch.dtype | None = None):
+    """y = x @ R (or x @ R^T) over the last dim of x in fp32 (the per-layer
+    rotations of backend.py:238-246).  x: [..., D] (fp32/bf16/fp16, rows with a
+    uniform stride); writes `out` (given, or new of `out_dtype`) and/or
+    `out_f32`, both [..., D] views with uniform row strides.  Returns (out, out_f32)."""
+    d = x.shape[-1]
+    if rot.shape != (d, d) or rot.dtype != torch.float32:
+        raise ValueError(f"rotation must be fp32 [{d}, {d}], got {tuple(rot.shape)} {rot.dtype}")
+    rot = rot.contiguous()
+    x2 = x.reshape(-1, d)
+    if x2.stride(-1) != 1 or (x2.shape[0] > 1 and x2.stride(0) % 8) or x2.data_ptr() % 16:
+        x2 = x2.clone(memory_format=torch.contiguous_format)
+    rows = x2.shape[0]
+    if out is None and out_f32 is None:
+        out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    o2 = None if out is None else out.view(-1, d)
+    f2 = None if out_f32 is None else out_f32.view(-1, d)
+    for t in (x2, o2, f2):
+        if t is not None and rows > 1 and t.stride(-1) != 1:
+            raise ValueError("rotate_rows: rows must be contiguous in the last dim")
+    dev = _require_cuda(x, rot)
+    check(_native.lib().oscar_rotate_rows(
+        _ptr(x2), _DTYPES[x2.dtype], rows, x2.stride(0), d, _ptr(rot), 1 if transpose else 0,
+        _ptr(o2), _DTYPES[o2.dtype] if o2 is not None else 0, o2.stride(0) if o2 is not None else 0,
+        _ptr(f2), f2.stride(0) if f2 is not None else 0, _stream(dev)))
+    return out, out_f32
+
+
 def set_attention_path(path: str) -> None:
     """Kernel family for slab_attention: "auto" (tensor-core decode kernel,
     else the mma.sync decode kernel, else the tile kernel, whichever is

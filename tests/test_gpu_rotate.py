@@ -1,0 +1,42 @@
+"""The per-layer rotation kernel (x @ R and x @ R^T in fp32) against torch's
+fp64 product, for every dtype pair the backend uses and strided outputs."""
+import pytest
+import torch
+
+from gpu_helpers import need_gpu
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("d", [64, 128, 256])
+@pytest.mark.parametrize("xdt,odt", [(torch.bfloat16, torch.float32), (torch.bfloat16, torch.bfloat16),
+                                     (torch.float16, torch.float16), (torch.float32, torch.bfloat16)])
+@pytest.mark.parametrize("transpose", [False, True])
+def test_rotate_rows_matches_fp64_product(d, xdt, odt, transpose):
+    from oscar_b200 import kernels
+
+    dev = need_gpu()
+    g = torch.Generator(device="cpu").manual_seed(d + (7 if transpose else 0))
+    rot = torch.linalg.qr(torch.randn(d, d, generator=g, dtype=torch.float64)).Q.float().to(dev)
+    x = torch.randn(37, 3, d, generator=g).to(dev, xdt)  # 111 rows: not a multiple of the 16-row tile
+    out, f32 = kernels.rotate_rows(x, rot, transpose=transpose, out=torch.empty(37, 3, d, dtype=odt, device=dev),
+                                   out_f32=torch.empty(37, 3, d, dtype=torch.float32, device=dev))
+    r = rot.double().t() if transpose else rot.double()
+    want = (x.double().reshape(-1, d) @ r).reshape(37, 3, d)
+    torch.testing.assert_close(f32.double(), want, atol=2e-5, rtol=2e-5)
+    # both outputs come from the same fp32 accumulator: out is its round-to-nearest cast
+    torch.testing.assert_close(out, f32.to(odt), atol=0, rtol=0)
+
+
+def test_rotate_rows_into_strided_rows_of_a_wider_output():
+    from oscar_b200 import kernels
+
+    dev = need_gpu()
+    d = 256
+    rot = torch.linalg.qr(torch.randn(d, d, dtype=torch.float64)).Q.float().to(dev)
+    x = torch.randn(10, 6, d, device=dev)
+    wide = torch.zeros(12, 6 * d, dtype=torch.bfloat16, device=dev)
+    kernels.rotate_rows(x, rot, transpose=True, out=wide[:10].view(10, 6, d))
+    want = (x.reshape(-1, d) @ rot.t()).reshape(10, 6 * d).bfloat16()
+    torch.testing.assert_close(wide[:10].float(), want.float(), atol=1e-2, rtol=1e-2)
+    assert torch.count_nonzero(wide[10:]) == 0
