@@ -349,7 +349,10 @@ __global__ void __maxnreg__(96)
     // S barriers exist per TMEM buffer: with two stages in flight a single
     // barrier could complete twice before its waiter looks, and a parity wait
     // cannot tell that apart from no completion.
-    if (lane == 0) {
+    // The whole warp runs the schedule and waits (warp-uniform control flow
+    // keeps the MMA operands in uniform registers); one elected lane issues
+    // each batch of MMAs with its commit, and each stage's TMA.
+    {
       constexpr uint32_t idesc_qk = tc::instr_desc(std::is_same<T, __nv_bfloat16>::value ? 1u : 0u, 0, 0, 128, kTcRows);
       constexpr uint32_t idesc_pv = tc::instr_desc(0u, 1, 1, 128, kTcRows);
       // descriptors of k-step 0; k-step j starts 256 * j bytes later (+16 * j in the start field);
@@ -357,20 +360,27 @@ __global__ void __maxnreg__(96)
       const uint64_t dq0 = tc::smem_desc(smem_u32(sm.qb), 128, kTcQSbo);
       const uint64_t dv0 = tc::smem_desc(smem_u32(sm.vt[0]), 128, kTcVtSbo);
       const uint64_t dp0 = tc::smem_desc(smem_u32(sm.pt[0]), 128, kTcVtSbo);
-      for (int s = 0; s < min(2, n_int); ++s)
-        tc_issue_stage(sm, s, lo, hi, bs_log2, page0, h, a.ksh, a.vsh, &tmk, &tmv, b_full);
+      if (tc::elect_one()) {
+        for (int s = 0; s < min(2, n_int); ++s)
+          tc_issue_stage(sm, s, lo, hi, bs_log2, page0, h, a.ksh, a.vsh, &tmk, &tmv, b_full);
+      }
+      __syncwarp();
       for (int qs = 0, ps = 0; ps < nst; ) {
         if (qs < nst && qs <= ps + 1) {
           // QK of stage qs into S[qs & 1] from A_K[qs & 1]
           wait(b_k + 8 * (qs & 1), (qs >> 1) & 1);
           tc::tc_fence_after();
           const uint32_t d_s = tmem + kTcColS + 32 * (qs & 1), a_k = tmem + ((qs & 1) ? kTcColA1 : kTcColA0);
+          if (tc::elect_one()) {
 #pragma unroll
-          for (int j = 0; j < kTcK / 16; ++j) tc::mma_ts(d_s, a_k + 8 * j, dq0 + 16 * j, idesc_qk, j > 0 ? 1u : 0u);
-          tc::mma_commit(b_s + 8 * (qs & 1));
+            for (int j = 0; j < kTcK / 16; ++j) tc::mma_ts(d_s, a_k + 8 * j, dq0 + 16 * j, idesc_qk, j > 0 ? 1u : 0u);
+            tc::mma_commit(b_s + 8 * (qs & 1));
+          }
+          __syncwarp();
           if (qs + 2 < n_int) {
             wait(b_empty + 8 * (qs & 1), (qs >> 1) & 1);
-            tc_issue_stage(sm, qs + 2, lo, hi, bs_log2, page0, h, a.ksh, a.vsh, &tmk, &tmv, b_full);
+            if (tc::elect_one()) tc_issue_stage(sm, qs + 2, lo, hi, bs_log2, page0, h, a.ksh, a.vsh, &tmk, &tmv, b_full);
+            __syncwarp();
           }
           ++qs;
         } else {
@@ -382,12 +392,15 @@ __global__ void __maxnreg__(96)
           const uint64_t dpa = dp0 + (uint64_t)((ps & 1) * (sizeof(sm.pt[0]) >> 4));
           const uint32_t d_o = tmem + kTcColO;
           const uint32_t acc0 = ps > 0 ? 1u : 0u;
+          if (tc::elect_one()) {
 #pragma unroll
-          for (int j = 0; j < kTcStage / 16; ++j) {
-            tc::mma_ss(d_o, dva + 16 * j, dpa + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
-            tc::mma_ss(d_o + 32, dvb + 16 * j, dpa + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
+            for (int j = 0; j < kTcStage / 16; ++j) {
+              tc::mma_ss(d_o, dva + 16 * j, dpa + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
+              tc::mma_ss(d_o + 32, dvb + 16 * j, dpa + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
+            }
+            tc::mma_commit(b_pv);
           }
-          tc::mma_commit(b_pv);
+          __syncwarp();
           ++ps;
         }
       }

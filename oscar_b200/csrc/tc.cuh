@@ -41,6 +41,13 @@ OSCAR_DEVINL bool mbar_wait(uint32_t bar, uint32_t parity) {
   return false;
 }
 
+// one lane of a converged warp (the lowest active one) gets true
+OSCAR_DEVINL bool elect_one() {
+  uint32_t pred;
+  asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n" : "=r"(pred));
+  return pred != 0;
+}
+
 // ---------------------------------------------------------------- copies
 OSCAR_DEVINL void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
