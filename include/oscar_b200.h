@@ -201,6 +201,27 @@ int oscar_rotate_rows(const void* x, int32_t x_dtype, int64_t rows, int64_t x_st
                       float* out_f32, int64_t out_f32_stride,
                       void* stream);
 
+/* One segment of oscar_rotate_rows_batch: the arguments of
+ * oscar_rotate_rows for one tensor. */
+typedef struct oscar_rotate_seg {
+  const void* x;
+  int64_t rows;
+  int64_t x_stride;
+  const float* rot;
+  int32_t transpose;
+  void* out;
+  int64_t out_stride;
+  float* out_f32;
+  int64_t out_f32_stride;
+} oscar_rotate_seg;
+
+/* Up to 4 rotations in one launch (e.g. the step's queries with R_k and its
+ * keys / values with R_k / R_v); every segment shares x_dtype, head_dim and
+ * out_dtype, and follows the rules of oscar_rotate_rows.  No counterpart in
+ * the reference's kernel API. */
+int oscar_rotate_rows_batch(const oscar_rotate_seg* segs, int32_t n_segs, int32_t x_dtype, int32_t head_dim,
+                            int32_t out_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,6 +21,14 @@ _I64 = ctypes.c_int64
 _U32 = ctypes.c_uint32
 _F32 = ctypes.c_float
 
+
+
+class RotateSeg(ctypes.Structure):
+    """struct oscar_rotate_seg of include/oscar_b200.h."""
+    _fields_ = [("x", _P), ("rows", _I64), ("x_stride", _I64), ("rot", _P), ("transpose", _I32),
+                ("out", _P), ("out_stride", _I64), ("out_f32", _P), ("out_f32_stride", _I64)]
+
+
 # name -> (restype, argtypes), exactly the prototypes of include/oscar_b200.h
 SIGNATURES = {
     "oscar_abi_version": (ctypes.c_int, []),
@@ -41,6 +49,7 @@ SIGNATURES = {
     "oscar_slab_attention_workspace": (ctypes.c_int64, [_P, _P, _I32, _I32, _I32, _I32, _I32]),
     "oscar_merge_slab": (ctypes.c_int, [_P, _P, _I64, _P, _I32, _P, _I64, _I32, _I32, _I64, _P, _P]),
     "oscar_rotate_rows": (ctypes.c_int, [_P, _I32, _I64, _I64, _I32, _P, _I32, _P, _I32, _I64, _P, _I64, _P]),
+    "oscar_rotate_rows_batch": (ctypes.c_int, [ctypes.POINTER(RotateSeg), _I32, _I32, _I32, _I32, _P]),
 }
 
 ABI_VERSION = 1

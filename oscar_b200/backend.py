@@ -131,14 +131,29 @@ class OscarAttentionImplMixin:
         if rk.device != device:
             rk, rv = rk.to(device), rv.to(device)
             layer._oscar_rots = (rk, rv)
+            layer._oscar_rvt = None
         return rk, rv
+
+    def _layer_rvt(self, layer, device):
+        """R_v^T (contiguous), cached per layer: o @ R_v^T reads it row-major."""
+        rvt = getattr(layer, "_oscar_rvt", None)
+        _, rv = self._layer_rots(layer, device)
+        if rvt is None or rvt.device != device:
+            rvt = rv.t().contiguous()
+            layer._oscar_rvt = rvt
+        return rvt
 
     def _rotate(self, x: torch.Tensor, rot: torch.Tensor, out_dtype=torch.float32) -> torch.Tensor:
         """x @ R in fp32, [N, H, D] -> [N, H, D] of out_dtype (rotate_rows)."""
         return kernels.rotate_rows(x, rot, out_dtype=out_dtype)[0]
 
     # ------------------------------------------------------------------ write path
-    def _store(self, layer, key, value, slot_mapping, *, invalidate: bool):
+    def _store(self, layer, key, value, slot_mapping, *, invalidate: bool, query_rows=None):
+        """Rotate, clip/INT2-store; returns (k_rot, v_rot, k_lo, v_lo, q_lo):
+        fp32 rows for the store / staging window, the model-dtype rows the
+        attention reads (x @ R then .to(dtype), backend.py:360-366) and, when
+        ``query_rows`` is given, the rotated queries (q @ R_k, query dtype),
+        all from one rotation launch."""
         n = slot_mapping.shape[0]
         hk, d = self.num_kv_heads, self.head_size
         k = key[:n].reshape(n, hk, d)
@@ -146,18 +161,24 @@ class OscarAttentionImplMixin:
         if invalidate and getattr(layer, "_oscar_stage_ready", False):
             kernels.staging_invalidate(slot_mapping, layer._oscar_slot_owner, self.stage_block)
         rk, rv = self._layer_rots(layer, k.device)
-        # one pass per tensor: fp32 rows for the store / staging window and the
-        # model-dtype rows the attention reads (x @ R then .to(dtype), backend.py:360-366)
         k_rot, v_rot = (torch.empty(n, hk, d, dtype=torch.float32, device=k.device) for _ in range(2))
         k_lo = torch.empty((n, hk, d), dtype=k.dtype, device=k.device)
         v_lo = torch.empty((n, hk, d), dtype=v.dtype, device=v.device)
-        kernels.rotate_rows(k, rk, out=k_lo, out_f32=k_rot)
-        kernels.rotate_rows(v, rv, out=v_lo, out_f32=v_rot)
+        jobs = [(k, rk, k_lo, k_rot), (v, rv, v_lo, v_rot)]
+        q_lo = None
+        if query_rows is not None and query_rows.dtype == k.dtype == v.dtype:
+            q_lo = torch.empty(query_rows.shape, dtype=query_rows.dtype, device=k.device)
+            jobs.append((query_rows, rk, q_lo, None))
+        if k.dtype == v.dtype:
+            kernels.rotate_rows_many(jobs)
+        else:
+            kernels.rotate_rows(k, rk, out=k_lo, out_f32=k_rot)
+            kernels.rotate_rows(v, rv, out=v_lo, out_f32=v_rot)
         kernels.oscar_store(k_rot, v_rot, self.key_cache, self.value_cache, slot_mapping,
                             self._oscar.k_clip_ratio, self._oscar.v_clip_ratio)
         self._oscar_stats["writes"] += 1
         self._oscar_stats["kv_bytes_written"] += n * hk * 160
-        return k_rot, v_rot, k_lo, v_lo
+        return k_rot, v_rot, k_lo, v_lo, q_lo
 
     def do_kv_cache_update(self, layer, key, value, kv_cache, slot_mapping) -> None:
         """backend.py:151-198: owner invalidation -> rotate -> clip/INT2 store."""
@@ -232,7 +253,9 @@ class OscarAttentionImplMixin:
             slots = attn_metadata.slot_mapping[:n].to(device=key.device, dtype=torch.int64)
             rotated = None
             if slots.shape[0] > 0:
-                rotated = self._store(layer, key, value, slots, invalidate=not self._oscar.window_enabled)
+                q_rows = self._whole_batch_rotated_queries(query, key, attn_metadata)
+                rotated = self._store(layer, key, value, slots, invalidate=not self._oscar.window_enabled,
+                                      query_rows=q_rows)
             if self._oscar.window_enabled:
                 self._ensure_staging(layer, kv_cache)
                 self._staging_write(layer, key, value, attn_metadata, rotated=None if rotated is None else rotated[:2])
@@ -240,11 +263,25 @@ class OscarAttentionImplMixin:
                                              rotated_lo=None if rotated is None else rotated[2:])
         return self._streaming_attention(layer, query, key, value, kv_cache, attn_metadata, output)
 
+    def _whole_batch_rotated_queries(self, query, key, metadata):
+        """The query rows [covered, Hq, D] when every active request takes the
+        rotated (cached-history) path of _streaming_attention, else None."""
+        actual = min(query.shape[0], metadata.num_actual_tokens)
+        if actual == 0:
+            return None
+        starts, seqs = metadata_batch_lists(metadata)
+        starts = [min(x, actual) for x in starts]
+        active = [i for i, (a, b) in enumerate(pairwise(starts)) if b > a]
+        if not active or any(seqs[i] == starts[i + 1] - starts[i] for i in active):
+            return None
+        return query[:starts[-1]].view(starts[-1], self.num_heads, self.head_size)
+
     def _streaming_attention(self, layer, query, key, value, kv_cache, metadata, output, rotated_lo=None):
         """backend.py:334-393: prefix-free requests attend their own chunk in
         the model's domain; cached requests go through the rotated INT2 path.
         ``rotated_lo`` holds the store path's (x @ R).to(dtype) rows of key and
-        value, reused instead of rotating them again."""
+        value (and of the queries, or None), reused instead of rotating them
+        again."""
         if (key is None) != (value is None):
             raise ValueError("Both new K and V must be supplied together")
         actual = min(query.shape[0], metadata.num_actual_tokens)
@@ -288,9 +325,13 @@ class OscarAttentionImplMixin:
                 v_in = None if v_all is None else v_all[ids]
             if rotate:
                 rk, rv = self._layer_rots(layer, query.device)
-                q_in = self._rotate(q_in, rk, query.dtype)
+                q_lo = None if rotated_lo is None else rotated_lo[2]
+                if ids is None and q_lo is not None and q_lo.shape[0] == covered:
+                    q_in = q_lo
+                else:
+                    q_in = self._rotate(q_in, rk, query.dtype)
                 if k_in is not None and rotated_lo is not None and rotated_lo[0].shape[0] >= covered:
-                    k_lo, v_lo = rotated_lo
+                    k_lo, v_lo = rotated_lo[:2]
                     k_in = k_lo[:covered] if ids is None else k_lo[ids]
                     v_in = v_lo[:covered] if ids is None else v_lo[ids]
                 else:
@@ -304,11 +345,12 @@ class OscarAttentionImplMixin:
                                             workspace_bytes=self._oscar.stream_workspace_bytes)
             if rotate:
                 m = out.shape[0]
+                rvt = self._layer_rvt(layer, query.device)
                 if ids is None and out_rows.is_contiguous():
                     # o @ R_v^T straight into the output rows, in the output dtype
-                    kernels.rotate_rows(out, rv, transpose=True, out=out_rows[:m].view(m, hq, d))
+                    kernels.rotate_rows(out, rvt, out=out_rows[:m].view(m, hq, d))
                     continue
-                out = kernels.rotate_rows(out, rv, transpose=True, out_dtype=output.dtype)[0]
+                out = kernels.rotate_rows(out, rvt, out_dtype=output.dtype)[0]
             result = out.to(output.dtype).view(out.shape[0], hq * d)
             if ids is None:
                 out_rows[: result.shape[0]].copy_(result)

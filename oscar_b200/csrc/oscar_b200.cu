@@ -3,6 +3,7 @@
 // included headers.
 #include <algorithm>
 #include <atomic>
+#include <climits>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -113,14 +114,15 @@ int oscar_store_int2(const float* k_rot, const float* v_rot, int64_t n_tokens, i
                      v_stride_block, v_stride_token, v_stride_head};
   const int kidx = clip_index(k_clip_ratio, head_dim), vidx = clip_index(v_clip_ratio, head_dim);
   const int64_t vecs = n_tokens * num_kv_heads;
-  const int64_t blocks = std::min<int64_t>((vecs + 7) / 8, (int64_t)device_info().sms * 32);
+  // one warp per vector, four per CTA (one per scheduler): the kernel is latency-bound at decode sizes
+  const int64_t blocks = std::min<int64_t>((vecs + 3) / 4, (int64_t)device_info().sms * 64);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int grid = (int)std::max<int64_t>(blocks, 1);
   if (head_dim > 128)
-    oscar::store_int2_kernel<2><<<grid, 256, 0, s>>>(k_rot, v_rot, n_tokens, num_kv_heads, head_dim, kidx, vidx, g,
+    oscar::store_int2_kernel<2><<<grid, 128, 0, s>>>(k_rot, v_rot, n_tokens, num_kv_heads, head_dim, kidx, vidx, g,
                                                       slot_mapping);
   else
-    oscar::store_int2_kernel<1><<<grid, 256, 0, s>>>(k_rot, v_rot, n_tokens, num_kv_heads, head_dim, kidx, vidx, g,
+    oscar::store_int2_kernel<1><<<grid, 128, 0, s>>>(k_rot, v_rot, n_tokens, num_kv_heads, head_dim, kidx, vidx, g,
                                                       slot_mapping);
   return cuda_status("store_int2_kernel");
 }
@@ -823,9 +825,8 @@ int oscar_staging_write_noalloc(const float* k_rot, const float* v_rot, int64_t 
 namespace {
 
 template <typename InT, typename OutT, int D>
-int launch_rotate_d(const void* x, int64_t rows, int64_t xs, const float* rot, int tr, void* out, int64_t os,
-                    float* of, int64_t ofs, cudaStream_t s) {
-  constexpr size_t smem = (size_t)(D * oscar::kRotCols + oscar::kRotRows * D) * sizeof(float);
+int launch_rotate_d(const oscar::RotBatch& b, cudaStream_t s) {
+  constexpr size_t smem = oscar::rotate_smem_bytes<D>();
   static thread_local int cfg_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -834,49 +835,70 @@ int launch_rotate_d(const void* x, int64_t rows, int64_t xs, const float* rot, i
                          (int)smem);
     cfg_dev = dev;
   }
-  dim3 grid((unsigned)((rows + oscar::kRotRows - 1) / oscar::kRotRows), (unsigned)(D / oscar::kRotCols));
-  oscar::rotate_rows_kernel<InT, OutT, D><<<grid, 256, smem, s>>>(
-      reinterpret_cast<const InT*>(x), xs, rows, rot, tr, reinterpret_cast<OutT*>(out), os, of, ofs);
+  dim3 grid((unsigned)b.tile_begin[b.n], (unsigned)(D / oscar::kRotCols));
+  oscar::rotate_rows_kernel<InT, OutT, D><<<grid, 256, smem, s>>>(b);
   return cuda_status("rotate_rows_kernel");
 }
 
 template <typename InT, typename OutT>
-int launch_rotate(const void* x, int64_t rows, int64_t xs, int d, const float* rot, int tr, void* out, int64_t os,
-                  float* of, int64_t ofs, cudaStream_t s) {
-  if (d == 256) return launch_rotate_d<InT, OutT, 256>(x, rows, xs, rot, tr, out, os, of, ofs, s);
-  if (d == 128) return launch_rotate_d<InT, OutT, 128>(x, rows, xs, rot, tr, out, os, of, ofs, s);
-  return launch_rotate_d<InT, OutT, 64>(x, rows, xs, rot, tr, out, os, of, ofs, s);
+int launch_rotate(const oscar::RotBatch& b, int d, cudaStream_t s) {
+  if (d == 256) return launch_rotate_d<InT, OutT, 256>(b, s);
+  if (d == 128) return launch_rotate_d<InT, OutT, 128>(b, s);
+  return launch_rotate_d<InT, OutT, 64>(b, s);
 }
 
 template <typename InT>
-int rotate_out(int out_dtype, const void* x, int64_t rows, int64_t xs, int d, const float* rot, int tr, void* out,
-               int64_t os, float* of, int64_t ofs, cudaStream_t s) {
-  if (out == nullptr || out_dtype == OSCAR_DTYPE_F32)
-    return launch_rotate<InT, float>(x, rows, xs, d, rot, tr, out, os, of, ofs, s);
-  if (out_dtype == OSCAR_DTYPE_BF16) return launch_rotate<InT, __nv_bfloat16>(x, rows, xs, d, rot, tr, out, os, of, ofs, s);
-  return launch_rotate<InT, __half>(x, rows, xs, d, rot, tr, out, os, of, ofs, s);
+int rotate_out(int out_dtype, const oscar::RotBatch& b, int d, cudaStream_t s) {
+  if (out_dtype == OSCAR_DTYPE_F32) return launch_rotate<InT, float>(b, d, s);
+  if (out_dtype == OSCAR_DTYPE_BF16) return launch_rotate<InT, __nv_bfloat16>(b, d, s);
+  return launch_rotate<InT, __half>(b, d, s);
 }
 
 }  // namespace
 
+extern "C" int oscar_rotate_rows_batch(const oscar_rotate_seg* segs, int32_t n_segs, int32_t x_dtype,
+                                       int32_t head_dim, int32_t out_dtype, void* stream) {
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+    return fail(OSCAR_ERR_INVALID, "rotate: D=%d must be 64, 128 or 256", head_dim);
+  if (x_dtype < 0 || x_dtype > 2 || out_dtype < 0 || out_dtype > 2) return fail(OSCAR_ERR_INVALID, "rotate: bad dtype");
+  if (n_segs < 0 || n_segs > oscar::kRotMaxSegs || (n_segs > 0 && segs == nullptr))
+    return fail(OSCAR_ERR_INVALID, "rotate: 0 to %d segments", oscar::kRotMaxSegs);
+  oscar::RotBatch b{};
+  int64_t tiles = 0;
+  for (int i = 0; i < n_segs; ++i) {
+    const oscar_rotate_seg& g = segs[i];
+    if (g.rows < 0) return fail(OSCAR_ERR_INVALID, "rotate: segment %d has %lld rows", i, (long long)g.rows);
+    if (g.rows == 0 || (g.out == nullptr && g.out_f32 == nullptr)) continue;
+    if (g.x == nullptr || g.rot == nullptr) return fail(OSCAR_ERR_INVALID, "rotate: null pointer in segment %d", i);
+    if ((reinterpret_cast<uintptr_t>(g.rot) | reinterpret_cast<uintptr_t>(g.x)) & 15 || (g.rows > 1 && g.x_stride % 8))
+      return fail(OSCAR_ERR_INVALID,
+                  "rotate: x and the rotation must be 16-byte aligned, x rows a multiple of 8 elements apart");
+    oscar::RotSeg& d = b.seg[b.n];
+    d.x = g.x;
+    d.rows = g.rows;
+    d.x_stride = g.x_stride;
+    d.rot = g.rot;
+    d.transpose = g.transpose ? 1 : 0;
+    d.out = g.out;
+    d.out_stride = g.out_stride;
+    d.out_f32 = g.out_f32;
+    d.out_f32_stride = g.out_f32_stride;
+    b.tile_begin[b.n] = (int)tiles;
+    tiles += (g.rows + oscar::kRotRows - 1) / oscar::kRotRows;
+    if (tiles > INT_MAX / 2) return fail(OSCAR_ERR_INVALID, "rotate: too many rows");
+    ++b.n;
+  }
+  if (b.n == 0) return OSCAR_OK;
+  b.tile_begin[b.n] = (int)tiles;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (x_dtype == OSCAR_DTYPE_F32) return rotate_out<float>(out_dtype, b, head_dim, s);
+  if (x_dtype == OSCAR_DTYPE_BF16) return rotate_out<__nv_bfloat16>(out_dtype, b, head_dim, s);
+  return rotate_out<__half>(out_dtype, b, head_dim, s);
+}
+
 extern "C" int oscar_rotate_rows(const void* x, int32_t x_dtype, int64_t rows, int64_t x_stride, int32_t head_dim,
                                  const float* rot, int32_t transpose, void* out, int32_t out_dtype, int64_t out_stride,
                                  float* out_f32, int64_t out_f32_stride, void* stream) {
-  if (rows < 0 || (head_dim != 64 && head_dim != 128 && head_dim != 256))
-    return fail(OSCAR_ERR_INVALID, "rotate: D=%d must be 64, 128 or 256", head_dim);
-  if (x_dtype < 0 || x_dtype > 2 || out_dtype < 0 || out_dtype > 2) return fail(OSCAR_ERR_INVALID, "rotate: bad dtype");
-  if (rows == 0 || (out == nullptr && out_f32 == nullptr)) return OSCAR_OK;
-  if (x == nullptr || rot == nullptr) return fail(OSCAR_ERR_INVALID, "rotate: null pointer");
-  if ((reinterpret_cast<uintptr_t>(rot) | reinterpret_cast<uintptr_t>(x)) & 15 || (rows > 1 && x_stride % 8))
-    return fail(OSCAR_ERR_INVALID, "rotate: x and the rotation must be 16-byte aligned, x rows a multiple of 8 apart");
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (x_dtype == OSCAR_DTYPE_F32)
-    return rotate_out<float>(out_dtype, x, rows, x_stride, head_dim, rot, transpose, out, out_stride, out_f32,
-                             out_f32_stride, s);
-  if (x_dtype == OSCAR_DTYPE_BF16)
-    return rotate_out<__nv_bfloat16>(out_dtype, x, rows, x_stride, head_dim, rot, transpose, out, out_stride, out_f32,
-                                     out_f32_stride, s);
-  return rotate_out<__half>(out_dtype, x, rows, x_stride, head_dim, rot, transpose, out, out_stride, out_f32,
-                            out_f32_stride, s);
+  oscar_rotate_seg g{x, rows, x_stride, rot, transpose, out, out_stride, out_f32, out_f32_stride};
+  return oscar_rotate_rows_batch(&g, 1, x_dtype, head_dim, out == nullptr ? OSCAR_DTYPE_F32 : out_dtype, stream);
 }
-

@@ -4,13 +4,16 @@
 // GEMMs on [tokens * heads, D] x [D, D]; here one kernel reads x in its own
 // dtype, accumulates in fp32 FMAs over the D products and writes fp32 and/or
 // the query dtype straight into strided destination rows, which also fuses
-// the casts and copies around the GEMM.
+// the casts and copies around the GEMM.  One launch serves up to four
+// segments (e.g. the step's queries, keys and values) that share the dtypes.
 //
-// CTA = 16 rows x 32 output columns, 256 threads; the [D, 32] column block of
-// R and the [16, D] row tile of x are staged in shared memory with 16-byte
-// loads (48 KB at D = 256); thread t computes row t / 16 and columns
-// 2 (t % 16), +1, each as two partial sums (even / odd k) to halve the
-// dependent FMA chain.
+// CTA = 16 rows x 32 output columns of one segment, 256 threads.  The [D, 32]
+// column block of R and the [16, D] row tile of x (transposed to [D, 16]) are
+// staged in shared memory (48 KB at D = 256).  The reduction over k is split
+// across the 8 warps (D / 8 products each); inside a warp, lane (rg, cg)
+// accumulates a 4 x 4 register tile (rows 4 rg.., columns 4 cg..) from one
+// 16-byte x load and one 16-byte R load per k, both single-wavefront.  The
+// eight partial tiles are summed through shared memory in warp order.
 #pragma once
 
 #include "common.cuh"
@@ -19,6 +22,31 @@ namespace oscar {
 
 constexpr int kRotRows = 16;
 constexpr int kRotCols = 32;
+constexpr int kRotMaxSegs = 4;
+
+struct RotSeg {
+  const void* x;
+  int64_t rows, x_stride;
+  const float* rot;
+  int transpose;
+  void* out;
+  int64_t out_stride;
+  float* out_f32;
+  int64_t out_f32_stride;
+};
+
+struct RotBatch {
+  RotSeg seg[kRotMaxSegs];
+  int tile_begin[kRotMaxSegs + 1];  // first row tile of each segment; tile_begin[n] = all tiles
+  int n;
+};
+
+template <int D>
+constexpr size_t rotate_smem_bytes() {
+  return (size_t)(D * kRotCols + D * kRotRows) * sizeof(float) > (size_t)8 * kRotRows * kRotCols * sizeof(float)
+             ? (size_t)(D * kRotCols + D * kRotRows) * sizeof(float)
+             : (size_t)8 * kRotRows * kRotCols * sizeof(float);
+}
 
 template <typename T>
 OSCAR_DEVINL void rot_store(T* p, float v) {
@@ -29,47 +57,80 @@ OSCAR_DEVINL void rot_store<float>(float* p, float v) {
   *p = v;
 }
 
-// 8 elements of x (16 bytes for 16-bit types, two 16-byte loads for fp32) -> fp32
+// 16 bytes of x -> fp32 (8 elements for 16-bit types, 4 for fp32)
 template <typename T>
-OSCAR_DEVINL void rot_load8(const T* p, float* f) {
-  const uint4 u = *reinterpret_cast<const uint4*>(p);
-  const T* e = reinterpret_cast<const T*>(&u);
+struct RotIn {
+  static constexpr int kPer16 = 8;
+  static OSCAR_DEVINL void convert(const uint4& u, float* f) {
+    const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) f[i] = Elem<T>::to_f32(e[i]);
-}
+    for (int i = 0; i < 8; ++i) f[i] = Elem<T>::to_f32(e[i]);
+  }
+};
 template <>
-OSCAR_DEVINL void rot_load8<float>(const float* p, float* f) {
-  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
-  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-}
+struct RotIn<float> {
+  static constexpr int kPer16 = 4;
+  static OSCAR_DEVINL void convert(const uint4& u, float* f) {
+    f[0] = __uint_as_float(u.x);
+    f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z);
+    f[3] = __uint_as_float(u.w);
+  }
+};
 
 template <typename InT, typename OutT, int D>
-__global__ void __launch_bounds__(256) rotate_rows_kernel(const InT* __restrict__ x, int64_t x_stride, int64_t rows,
-                                                          const float* __restrict__ rot, int transpose,
-                                                          OutT* __restrict__ out, int64_t out_stride,
-                                                          float* __restrict__ out_f32, int64_t out_f32_stride) {
+__global__ void __launch_bounds__(256) rotate_rows_kernel(const __grid_constant__ RotBatch b) {
   extern __shared__ __align__(16) float rsm[];
-  float* rblk = rsm;                    // [D][32]: R[k][c0 + j] (R^T: R[c0 + j][k])
-  float* xt = rsm + D * kRotCols;       // [16][D]
-  const int tid = threadIdx.x;
-  const int64_t r0 = (int64_t)blockIdx.x * kRotRows;
+  float* rblk = rsm;                 // [D][32]: R[k][c0 + j] (R^T: R[c0 + j][k])
+  float* xt = rsm + D * kRotCols;    // [D][16]: x[r0 + r][k] at k * 16 + r
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int si = 0;
+  while (si + 1 < b.n && (int)blockIdx.x >= b.tile_begin[si + 1]) ++si;
+  const RotSeg& sg = b.seg[si];
+  const int64_t r0 = (int64_t)((int)blockIdx.x - b.tile_begin[si]) * kRotRows;
   const int c0 = blockIdx.y * kRotCols;
-  if (!transpose) {
-    // float4 (k, 4 c4 .. 4 c4 + 3): 8 per k row
+  const InT* x = static_cast<const InT*>(sg.x);
+  const float* rot = sg.rot;
+  // every global load of the CTA is issued before the first shared-memory
+  // store: one round trip instead of one per unrolled batch
+  constexpr int kRLoads = D * kRotCols / 4 / 256;  // float4 of R per thread
+  constexpr int kP = RotIn<InT>::kPer16;
+  constexpr int kXChunks = kRotRows * D / kP;      // 16-byte chunks of the x tile
+  constexpr int kXLoads = (kXChunks + 255) / 256;
+  float4 rbuf[kRLoads];
 #pragma unroll
-    for (int i = tid; i < D * kRotCols / 4; i += 256) {
+  for (int u = 0; u < kRLoads; ++u) {
+    const int i = tid + 256 * u;
+    if (!sg.transpose) {
+      // (k, 4 c4 .. 4 c4 + 3): a warp reads 4 rows x 128 B
       const int k = i >> 3, c4 = i & 7;
-      *reinterpret_cast<float4*>(rblk + k * kRotCols + 4 * c4) =
-          *reinterpret_cast<const float4*>(rot + (int64_t)k * D + c0 + 4 * c4);
+      rbuf[u] = *reinterpret_cast<const float4*>(rot + (int64_t)k * D + c0 + 4 * c4);
+    } else {
+      // R^T[k][c] = R[c][k]: a warp reads 8 rows c x 64 B along k
+      const int rest = i >> 5;
+      const int j = ((rest & 3) << 3) | (i & 7), k4 = ((rest >> 2) << 2) | ((i >> 3) & 3);
+      rbuf[u] = *reinterpret_cast<const float4*>(rot + (int64_t)(c0 + j) * D + 4 * k4);
     }
-  } else {
-    // R^T[k][c] = R[c][k]: float4 along k of row c0 + j, scattered into column j
-    // (consecutive threads take consecutive columns: conflict-free stores)
+  }
+  uint4 xbuf[kXLoads];
 #pragma unroll
-    for (int i = tid; i < D * kRotCols / 4; i += 256) {
-      const int j = i & (kRotCols - 1), k4 = i / kRotCols;
-      const float4 v = *reinterpret_cast<const float4*>(rot + (int64_t)(c0 + j) * D + 4 * k4);
+  for (int u = 0; u < kXLoads; ++u) {
+    const int i = tid + 256 * u;
+    const int r = i & (kRotRows - 1), kc = i >> 4;
+    xbuf[u] = make_uint4(0u, 0u, 0u, 0u);
+    if (i < kXChunks && r0 + r < sg.rows)
+      xbuf[u] = *reinterpret_cast<const uint4*>(x + (r0 + r) * sg.x_stride + kP * kc);
+  }
+#pragma unroll
+  for (int u = 0; u < kRLoads; ++u) {
+    const int i = tid + 256 * u;
+    const float4 v = rbuf[u];
+    if (!sg.transpose) {
+      const int k = i >> 3, c4 = i & 7;
+      *reinterpret_cast<float4*>(rblk + k * kRotCols + 4 * c4) = v;
+    } else {
+      const int rest = i >> 5;
+      const int j = ((rest & 3) << 3) | (i & 7), k4 = ((rest >> 2) << 2) | ((i >> 3) & 3);
       rblk[(4 * k4) * kRotCols + j] = v.x;
       rblk[(4 * k4 + 1) * kRotCols + j] = v.y;
       rblk[(4 * k4 + 2) * kRotCols + j] = v.z;
@@ -77,38 +138,59 @@ __global__ void __launch_bounds__(256) rotate_rows_kernel(const InT* __restrict_
     }
   }
 #pragma unroll
-  for (int i = tid; i < kRotRows * D / 8; i += 256) {
-    const int r = i / (D / 8), k8 = i - r * (D / 8);
-    float f[8];
-    if (r0 + r < rows) {
-      rot_load8<InT>(x + (r0 + r) * x_stride + 8 * k8, f);
-    } else {
+  for (int u = 0; u < kXLoads; ++u) {
+    const int i = tid + 256 * u;
+    if (i < kXChunks) {
+      const int r = i & (kRotRows - 1), kc = i >> 4;
+      float f[kP];
+      RotIn<InT>::convert(xbuf[u], f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] = 0.0f;
+      for (int e = 0; e < kP; ++e) xt[(kP * kc + e) * kRotRows + r] = f[e];
     }
-    *reinterpret_cast<float4*>(xt + r * D + 8 * k8) = make_float4(f[0], f[1], f[2], f[3]);
-    *reinterpret_cast<float4*>(xt + r * D + 8 * k8 + 4) = make_float4(f[4], f[5], f[6], f[7]);
   }
   __syncthreads();
-  const int r = tid >> 4, cq = 2 * (tid & 15);
-  const float* xr = xt + r * D;
-  float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [even / odd k][column]
+
+  constexpr int kSlice = D / 8;  // products per warp
+  const int rg = lane >> 3, cg = lane & 7;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+  const float* xp = xt + warp * kSlice * kRotRows + 4 * rg;
+  const float* rp = rblk + warp * kSlice * kRotCols + 4 * cg;
 #pragma unroll 8
-  for (int k = 0; k < D; k += 2) {
-    const float2 xv = *reinterpret_cast<const float2*>(xr + k);
-    const float2 ra = *reinterpret_cast<const float2*>(rblk + k * kRotCols + cq);
-    const float2 rb = *reinterpret_cast<const float2*>(rblk + (k + 1) * kRotCols + cq);
-    acc[0][0] = fmaf(xv.x, ra.x, acc[0][0]);
-    acc[0][1] = fmaf(xv.x, ra.y, acc[0][1]);
-    acc[1][0] = fmaf(xv.y, rb.x, acc[1][0]);
-    acc[1][1] = fmaf(xv.y, rb.y, acc[1][1]);
+  for (int kk = 0; kk < kSlice; ++kk) {
+    const float4 xv = *reinterpret_cast<const float4*>(xp + kk * kRotRows);
+    const float4 rv = *reinterpret_cast<const float4*>(rp + kk * kRotCols);
+    const float xa[4] = {xv.x, xv.y, xv.z, xv.w}, ra[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], ra[j], acc[i][j]);
   }
-  if (r0 + r < rows) {
+  __syncthreads();  // every warp is done with rblk / xt
+  float* red = rsm;  // [8 warps][16 rows][32 cols]
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    *reinterpret_cast<float4*>(red + warp * kRotRows * kRotCols + (4 * rg + i) * kRotCols + 4 * cg) =
+        make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+  __syncthreads();
+  const int r = tid >> 4, cq = 2 * (tid & 15);
+  float2 s = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const float2 p = *reinterpret_cast<const float2*>(red + w * kRotRows * kRotCols + r * kRotCols + cq);
+    s.x += p.x;
+    s.y += p.y;
+  }
+  if (r0 + r < sg.rows) {
+    const float v[2] = {s.x, s.y};
+    OutT* out = static_cast<OutT*>(sg.out);
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const float v = acc[0][j] + acc[1][j];
-      if (out != nullptr) rot_store<OutT>(out + (r0 + r) * out_stride + c0 + cq + j, v);
-      if (out_f32 != nullptr) out_f32[(r0 + r) * out_f32_stride + c0 + cq + j] = v;
+      if (out != nullptr) rot_store<OutT>(out + (r0 + r) * sg.out_stride + c0 + cq + j, v[j]);
+      if (sg.out_f32 != nullptr) sg.out_f32[(r0 + r) * sg.out_f32_stride + c0 + cq + j] = v[j];
     }
   }
 }

@@ -9,6 +9,8 @@
 // codes and fp16 scale/zero bytes bit-identical to the torch CPU reference.
 #pragma once
 
+#include <climits>
+
 #include "common.cuh"
 
 namespace oscar {
@@ -78,13 +80,22 @@ OSCAR_DEVINL uint32_t quantize_vec(float (&x)[BPL][4], const bool (&act)[BPL], i
   const __half sh = __float2half_rn(scale);
   const __half zh = __float2half_rn(mn);
   const float s = __half2float(sh), z = __half2float(zh);
+  // q = floor(fl(fl((x - z) / s) + 0.5)) clamped to [0, 3].  The quotient
+  // through the rounded reciprocal r = RN(1 / s) differs from the rounded
+  // quotient by less than 2^-20 for |f| < 8, so the code only needs the
+  // correctly rounded division when f lies within 2^-16 of a boundary 1, 2, 3
+  // (or is not finite): that rare case takes the exact IEEE path.
+  const float r = __frcp_rn(s);
 #pragma unroll
   for (int j = 0; j < BPL; ++j) {
     uint32_t byte = 0;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      float q = floorf(__fadd_rn(__fdiv_rn(__fsub_rn(x[j][e], z), s), 0.5f));
-      q = fminf(fmaxf(q, 0.0f), 3.0f);
+      const float dx = __fsub_rn(x[j][e], z);
+      float f = __fadd_rn(__fmul_rn(dx, r), 0.5f);
+      const bool near = fabsf(__fsub_rn(f, rintf(f))) <= 1.0f / 65536.0f && f > 0.5f && f < 3.5f;
+      if (near || !(fabsf(f) < 8.0f)) f = __fadd_rn(__fdiv_rn(dx, s), 0.5f);
+      const float q = fminf(fmaxf(floorf(f), 0.0f), 3.0f);
       byte |= ((uint32_t)(int)q & 3u) << (2 * e);
     }
     code[j] = (uint8_t)byte;
@@ -93,7 +104,7 @@ OSCAR_DEVINL uint32_t quantize_vec(float (&x)[BPL][4], const bool (&act)[BPL], i
 }
 
 template <int BPL>
-__global__ void __launch_bounds__(256) store_int2_kernel(const float* __restrict__ k_rot,
+__global__ void __launch_bounds__(128) store_int2_kernel(const float* __restrict__ k_rot,
                                                          const float* __restrict__ v_rot, int64_t n, int hk, int D,
                                                          int k_clip_idx, int v_clip_idx, StoreGeom g,
                                                          const int64_t* __restrict__ slots) {
@@ -101,12 +112,30 @@ __global__ void __launch_bounds__(256) store_int2_kernel(const float* __restrict
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int bs_log2 = (g.block_size & (g.block_size - 1)) == 0 ? __ffs(g.block_size) - 1 : -1;
   for (int64_t vec = warp; vec < n * hk; vec += nwarps) {
-    const int64_t tok = vec / hk;
-    const int h = (int)(vec - tok * hk);
+    int64_t tok;
+    int h;
+    if (hk == 1) {
+      tok = vec;
+      h = 0;
+    } else if (vec < INT_MAX) {
+      tok = (int)vec / hk;
+      h = (int)vec - (int)tok * hk;
+    } else {
+      tok = vec / hk;
+      h = (int)(vec - tok * hk);
+    }
     const int64_t slot = slots[tok];
     if (slot < 0) continue;
-    const int64_t blk = slot / g.block_size, off = slot - blk * g.block_size;
+    int64_t blk, off;
+    if (bs_log2 >= 0) {
+      blk = slot >> bs_log2;
+      off = slot & (g.block_size - 1);
+    } else {
+      blk = slot / g.block_size;
+      off = slot - blk * g.block_size;
+    }
     if (blk >= g.num_blocks) {
       if (lane == 0) flag_error(1u);
       continue;

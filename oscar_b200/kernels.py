@@ -270,6 +270,43 @@ def rotate_rows(x: torch.Tensor, rot: torch.Tensor, *, transpose: bool = False, 
     return out, out_f32
 
 
+def rotate_rows_many(jobs) -> None:
+    """Several rotate_rows calls in one launch.  ``jobs``: up to four
+    ``(x, rot, out, out_f32)`` tuples (x @ R, no transpose) whose x share one
+    dtype and D and whose ``out`` tensors share one dtype; each output is
+    preallocated ([..., D] rows with uniform strides) or None."""
+    if not jobs:
+        return
+    if len(jobs) > 4:
+        raise ValueError("rotate_rows_many: at most 4 jobs per launch")
+    dev = _require_cuda(*[t for job in jobs for t in job])
+    d = jobs[0][0].shape[-1]
+    x_dt = jobs[0][0].dtype
+    out_dt = next((o.dtype for _, _, o, _ in jobs if o is not None), torch.float32)
+    segs = (_native.RotateSeg * len(jobs))()
+    keep = []
+    for i, (x, rot, out, out_f32) in enumerate(jobs):
+        if x.shape[-1] != d or x.dtype != x_dt or (out is not None and out.dtype != out_dt):
+            raise ValueError("rotate_rows_many: jobs must share x dtype, D and out dtype")
+        if rot.shape != (d, d) or rot.dtype != torch.float32:
+            raise ValueError(f"rotation must be fp32 [{d}, {d}], got {tuple(rot.shape)} {rot.dtype}")
+        rot = rot.contiguous()
+        keep.append(rot)
+        x2 = x.reshape(-1, d)
+        if x2.stride(-1) != 1 or (x2.shape[0] > 1 and x2.stride(0) % 8) or x2.data_ptr() % 16:
+            x2 = x2.clone(memory_format=torch.contiguous_format)
+        o2 = None if out is None else out.view(-1, d)
+        f2 = None if out_f32 is None else out_f32.view(-1, d)
+        for t in (o2, f2):
+            if t is not None and t.shape[0] > 1 and t.stride(-1) != 1:
+                raise ValueError("rotate_rows_many: rows must be contiguous in the last dim")
+        keep.append(x2)
+        segs[i] = _native.RotateSeg(_ptr(x2), x2.shape[0], x2.stride(0), _ptr(rot), 0,
+                                    _ptr(o2), o2.stride(0) if o2 is not None else 0,
+                                    _ptr(f2), f2.stride(0) if f2 is not None else 0)
+    check(_native.lib().oscar_rotate_rows_batch(segs, len(jobs), _DTYPES[x_dt], d, _DTYPES[out_dt], _stream(dev)))
+
+
 def set_attention_path(path: str) -> None:
     """Kernel family for slab_attention: "auto" (tensor-core decode kernel,
     else the mma.sync decode kernel, else the tile kernel, whichever is

@@ -40,3 +40,25 @@ def test_rotate_rows_into_strided_rows_of_a_wider_output():
     want = (x.reshape(-1, d) @ rot.t()).reshape(10, 6 * d).bfloat16()
     torch.testing.assert_close(wide[:10].float(), want.float(), atol=1e-2, rtol=1e-2)
     assert torch.count_nonzero(wide[10:]) == 0
+
+
+@pytest.mark.parametrize("d", [64, 256])
+def test_rotate_rows_many_one_launch_matches_separate_products(d):
+    from oscar_b200 import kernels
+
+    dev = need_gpu()
+    g = torch.Generator(device="cpu").manual_seed(d)
+    rk = torch.linalg.qr(torch.randn(d, d, generator=g, dtype=torch.float64)).Q.float().to(dev)
+    rv = torch.linalg.qr(torch.randn(d, d, generator=g, dtype=torch.float64)).Q.float().to(dev)
+    q = torch.randn(5, 6, d, generator=g).to(dev, torch.bfloat16)
+    k = torch.randn(5, 1, d, generator=g).to(dev, torch.bfloat16)
+    v = torch.randn(5, 1, d, generator=g).to(dev, torch.bfloat16)
+    q_lo, k_lo, v_lo = (torch.empty_like(t) for t in (q, k, v))
+    k32, v32 = (torch.empty(t.shape, dtype=torch.float32, device=dev) for t in (k, v))
+    kernels.rotate_rows_many([(k, rk, k_lo, k32), (v, rv, v_lo, v32), (q, rk, q_lo, None)])
+    for x, r, lo, f32 in ((k, rk, k_lo, k32), (v, rv, v_lo, v32), (q, rk, q_lo, None)):
+        want = (x.double().reshape(-1, d) @ r.double()).reshape(x.shape)
+        if f32 is not None:
+            torch.testing.assert_close(f32.double(), want, atol=2e-5, rtol=2e-5)
+            torch.testing.assert_close(lo, f32.to(lo.dtype), atol=0, rtol=0)
+        torch.testing.assert_close(lo.double(), want.to(lo.dtype).double(), atol=1e-2, rtol=1e-2)

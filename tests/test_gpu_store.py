@@ -187,3 +187,44 @@ def test_staging_collisions_at_scale_match_oracle():
         assert np.array_equal(owner.cpu().numpy(), st.owner), step
         assert np.array_equal(sk.cpu().numpy(), st.stage_k), step
         assert np.array_equal(sv.cpu().numpy(), st.stage_v), step
+
+
+def test_store_rounding_boundaries_bit_exact():
+    """Values placed on and a few ulps around every rounding boundary
+    (x - zero) / scale = k + 0.5 of their vector: the codes must follow the
+    reference's correctly rounded fp32 division exactly."""
+    from oscar_b200 import kernels
+
+    dev = need_gpu()
+    rng = np.random.default_rng(11)
+    n, d, bs = 512, 256, 16
+    x = np.zeros((n, 1, d), np.float32)
+    for i in range(n):
+        lo = np.float32(rng.normal() * 10 ** rng.uniform(-3, 3))
+        hi = np.float32(lo + abs(rng.normal()) * 10 ** rng.uniform(-3, 3) + 1e-3)
+        row = np.full(d, lo, np.float32)
+        row[1] = hi
+        scale, zero = orc.vector_scales(row[None])
+        s, z = np.float32(scale[0, 0]), np.float32(zero[0, 0])
+        vals = []
+        for k in range(3):
+            c = np.float32(np.float64(z) + np.float64(s) * (k + 0.5))
+            for step in range(-4, 5):
+                v = c
+                for _ in range(abs(step)):
+                    v = np.nextafter(v, np.float32(np.inf) if step > 0 else np.float32(-np.inf))
+                vals.append(v)
+        vals = np.clip(np.array(vals, np.float32), lo, hi)
+        row[2:2 + len(vals)] = vals
+        x[i, 0] = row
+    nb = n // bs + 1
+    slots = np.arange(n)
+    ek = np.zeros((nb, bs, 1, d), np.uint8)
+    ev = np.zeros_like(ek)
+    orc.store(x, x, ek, ev, slots)
+    kc = torch.zeros(nb, bs, 1, d, dtype=torch.int8, device=dev)
+    vc = torch.zeros_like(kc)
+    t = torch.from_numpy(x).to(dev)
+    kernels.oscar_store(t, t, kc, vc, torch.from_numpy(slots).to(dev))
+    assert np.array_equal(cache_bytes(kc), ek)
+    assert np.array_equal(cache_bytes(vc), ev)
