@@ -7,10 +7,11 @@
 //     and [48:96), V slot bytes [0:48) and [16:64) of every token, four 2D
 //     tensor-map boxes per page whose 48-byte rows put the 8 tokens of a
 //     shared-memory wavefront on 8 distinct bank groups.
-//   warps 0-15: thread (tok, q) = (tid % 128, tid / 128) handles dims
-//     [64 q, 64 q + 64) of token tok and query rows [8 q, 8 q + 8).  All
-//     sixteen warps work on the same stage (and run the same code, which keeps
-//     the instruction cache warm); four per scheduler hide each other's latency.
+//   warps 0-15: warp w serves tokens 32 (w % 4) .. + 31 (its TMEM lane
+//     quarter) in role q = w / 4: K dims [0, 128), K dims [128, 256), V dims
+//     [0, 128) or V dims [128, 256) of those tokens, and query rows
+//     [8 q, 8 q + 8) of their softmax.  The four roles of a scheduler wait on
+//     different buffers and overlap; no barrier spans the CTA inside a stage.
 //
 // Prologue: the split's staging owner tags are scanned into a bitmask of
 // staged positions (owner[(blk % rows) * bs + off] == blk, backend.py:172-176).
@@ -81,7 +82,6 @@ struct TcSmem {
   int lim[kTcRows];             // cache-only chunks: row r sees positions < lim[r]
   alignas(16) int red[2][16][8];  // slow-path row maxima, double-buffered
   float lsum[16][8];
-  uint2 klut[kTcStage], vlut[kTcStage];  // value tables of the stage's tokens (built by half 0 / half 1)
   unsigned long long bar_full[2], bar_empty[2], bar_k[2], bar_s[2], bar_p, bar_pv;  // k, s per TMEM buffer
   uint32_t tmem;
   int abort;
@@ -408,18 +408,31 @@ __global__ void __maxnreg__(96)
       if (nst > 0 && !tc::mbar_wait(b_pv, (nst - 1) & 1)) flag_error(16u);
     }
   } else {
-    // ============================ dequant + softmax warps: thread (tok, quarter q) owns
-    // dims [64 q, 64 q + 64) of token tok and query rows [8 q, 8 q + 8).
-    // Iteration it: operands of stage it (K -> TMEM, V -> V^T[it & 1]), then the
-    // softmax of stage it - 1, whose QK ran meanwhile.
+    // ============================ dequant + softmax warps.  Warp w serves the 32
+    // tokens of TMEM lane quarter w % 4 (tok = 32 (w % 4) + lane) in role
+    // q = w / 4: K dims [0, 128) (q = 0), K dims [128, 256) (1), V dims
+    // [0, 128) (2), V dims [128, 256) (3); in the softmax, thread (tok, q) owns
+    // query rows [8 q, 8 q + 8).  Each role waits only on the buffers it
+    // touches (no CTA-wide barrier per stage), so the four roles that share a
+    // scheduler overlap.  Iteration it: operands of stage it (K -> TMEM,
+    // V -> V^T[it & 1]), then the softmax of stage it - 1, whose QK ran meanwhile.
     const int q = warp >> 2, tok = tid & 127;
+    const bool is_k = q < 2;
+    const int half = q & 1;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const bool need_lim = hi > seq - qlen + 1;  // history reaches the causal window (cache-only chunks)
     const float scale = a.scale_log2;
     const uint32_t neg_inf = std::is_same<T, __nv_bfloat16>::value ? 0xFF80u : 0xFC00u;
-    // this thread's slot bytes: K codes [32 + 16 q, +16), V codes [16 q, +16)
-    const int koff = (q == 0) ? 32 : 16 * (q - 1);  // in ka for q == 0, else in kb
-    const int voff = (q < 3) ? 16 * q : 32;         // in va for q < 3, else in vb (which starts at byte 16)
+    // this thread's 32 code bytes as two 16-byte pieces of the raw rows (offsets
+    // from ka[slot][tok]; kb / va / vb follow ka at fixed distances):
+    //   K half 0: K bytes [32, 64) = ka[32, 48) + kb[0, 16);  K half 1: K bytes [64, 96) = kb[16, 48)
+    //   V half 0: V bytes [0, 32)  = va[0, 32);              V half 1: V bytes [32, 64) = vb[16, 48)
+    constexpr int kKb = (int)(offsetof(TcSmem, kb) - offsetof(TcSmem, ka));
+    constexpr int kVa = (int)(offsetof(TcSmem, va) - offsetof(TcSmem, ka));
+    constexpr int kVb = (int)(offsetof(TcSmem, vb) - offsetof(TcSmem, ka));
+    const int off0 = (q == 0) ? 32 : (q == 1) ? kKb + 16 : (q == 2) ? kVa : kVb + 16;
+    const int off1 = (q == 0) ? kKb : (q == 1) ? kKb + 32 : (q == 2) ? kVa + 16 : kVb + 32;
+    const int meta_off = is_k ? 0 : 4;  // K (scale, zero) at slot bytes [0, 4), V at [4, 8)
     float mrow[8], muse[8], lrow[8];  // running maxima, the same with -inf -> 0, sums
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
@@ -429,52 +442,70 @@ __global__ void __maxnreg__(96)
     }
     int nslow = 0;
     int pos_prev = hi;  // position of this thread's token in the stage whose softmax runs next
-    const int vt_off = (8 * q) * kTcVtSbo + (tok >> 3) * 128 + (tok & 7) * 16;
+    const int vt_off = (16 * half) * kTcVtSbo + (tok >> 3) * 128 + (tok & 7) * 16;
     const int pt_off = q * kTcVtSbo + (tok >> 3) * 128 + (tok & 7) * 16;
 
     for (int it = 0; it <= nst; ++it) {
       int pos_it = hi;
+      bool pv_done = false;  // this warp has waited for the PV of stage it - 2
       if (it < nst) {
         // ======== operands of stage it
         const int b = it & 1;
-        const uint32_t t_a = tmem + lane_base + (b ? kTcColA1 : kTcColA0);
+        const uint32_t t_a = tmem + lane_base + (b ? kTcColA1 : kTcColA0) + 64 * half;
+        if (!is_k) {
+          // V warps count in the K barrier too: their arrival releases S[b], which
+          // they last read in the softmax of stage it - 2, to the QK of stage it
+          tc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(b_k + 8 * b);
+        }
         int pos;
         bool live;
-        uint4 vc = make_uint4(0, 0, 0, 0);
-        uint2 vlut = make_uint2(0, 0);
-        const float* srow_v = nullptr;
         const bool is_int = it < n_int;
         if (is_int) {
           const int slot = it & 1;
           pos = lo + it * kTcStage + tok;
           wait(b_full + 8 * slot, (it >> 1) & 1);
-          const uint2 meta = *reinterpret_cast<const uint2*>(&sm.ka[slot][tok][0]);
-          const uint4 kc = *reinterpret_cast<const uint4*>((q == 0 ? sm.ka[slot][tok] : sm.kb[slot][tok]) + koff);
-          vc = *reinterpret_cast<const uint4*>((q < 3 ? sm.va[slot][tok] : sm.vb[slot][tok]) + voff);
+          const uint8_t* raw = &sm.ka[slot][tok][0];
+          const uint32_t meta = *reinterpret_cast<const uint32_t*>(raw + meta_off);
+          const uint4 c0 = *reinterpret_cast<const uint4*>(raw + off0);
+          const uint4 c1 = *reinterpret_cast<const uint4*>(raw + off1);
           __syncwarp();
           if (lane == 0) tc::mbar_arrive(b_empty + 8 * slot);
           live = pos < hi && !((sm.smask[(pos - lo) >> 5] >> ((pos - lo) & 31)) & 1u);
-          // quarter 0 builds the token's K table, quarter 1 its V table; all read both
-          if (q < 2) {
-            uint2 lut = make_uint2(0, 0);
-            if (live) lut = q ? tc_vlut<T>(meta.y) : tc_klut<T>(meta.x);
-            (q ? sm.vlut : sm.klut)[tok] = lut;
+          uint2 lut = make_uint2(0, 0);
+          if (live) lut = is_k ? tc_klut<T>(meta) : tc_vlut<T>(meta);
+          const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          if (is_k) {
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+              uint32_t r[32];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) tc_lut_word(cw[4 * g + j], lut.x, lut.y, r + 8 * j);
+              tc::tmem_st32(t_a + 32 * g, r);
+            }
+          } else {
+            if (it >= 2) {
+              // V^T[b] was last read by the PV of stage it - 2
+              wait(b_pv, (it - 2) & 1);
+              tc::tc_fence_after();
+              pv_done = true;
+            }
+            uint8_t* vt_row = sm.vt[b] + vt_off;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              uint32_t r[8];
+              tc_lut_word(cw[j], lut.x, lut.y, r);
+              *reinterpret_cast<uint4*>(vt_row + (2 * j) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
+              *reinterpret_cast<uint4*>(vt_row + (2 * j + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
+            }
           }
-          tc::bar_sync(5, kTcCompute);
-          const uint2 klut = sm.klut[tok];
-          vlut = sm.vlut[tok];
-          uint32_t r[32];
-          tc_lut_word(kc.x, klut.x, klut.y, r);
-          tc_lut_word(kc.y, klut.x, klut.y, r + 8);
-          tc_lut_word(kc.z, klut.x, klut.y, r + 16);
-          tc_lut_word(kc.w, klut.x, klut.y, r + 24);
-          tc::tmem_st32(t_a + 32 * q, r);
         } else {
           // staged stage: the (128 (it - n_int) + tok)-th staged position, fp32 rows
           const int j = (it - n_int) * kTcStage + tok;
           live = j < n_staged;
           pos = hi;
-          const float* srow_k = a.stage_k;
+          int64_t row_off = 0;
           if (live) {
             int lo_w = 0, hi_w = nwords - 1;  // last word whose prefix count is <= j
             while (lo_w < hi_w) {
@@ -485,55 +516,49 @@ __global__ void __maxnreg__(96)
             pos = lo + 32 * lo_w + bit;
             const int blk = sm.btab[(pos >> bs_log2) - page0];
             const int64_t seat = (int64_t)(blk % (int)a.stage_rows) * bs + (pos & (bs - 1));
-            srow_k = a.stage_k + (seat * a.hk + h) * D;
+            row_off = (seat * a.hk + h) * D;
           }
-          srow_v = a.stage_v + (srow_k - a.stage_k) + 64 * q;
-          srow_k += 64 * q;
-#pragma unroll 1
-          for (int w = 0; w < 4; ++w) {
-            uint32_t r[8];
-            tc_pack_word<T, false>(srow_k + 16 * w, live, r);
-            tc::tmem_st8(t_a + 32 * q + 8 * w, r);
+          const float* srow = (is_k ? a.stage_k : a.stage_v) + row_off + 128 * half;
+          if (is_k) {
+#pragma unroll 2
+            for (int w = 0; w < 8; ++w) {
+              uint32_t r[8];
+              tc_pack_word<T, false>(srow + 16 * w, live, r);
+              tc::tmem_st8(t_a + 8 * w, r);
+            }
+          } else {
+            if (it >= 2) {
+              wait(b_pv, (it - 2) & 1);
+              tc::tc_fence_after();
+              pv_done = true;
+            }
+            uint8_t* vt_row = sm.vt[b] + vt_off;
+#pragma unroll 2
+            for (int w = 0; w < 8; ++w) {
+              uint32_t r[8];
+              tc_pack_word<T, true>(srow + 16 * w, live, r);
+              *reinterpret_cast<uint4*>(vt_row + (2 * w) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
+              *reinterpret_cast<uint4*>(vt_row + (2 * w + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
+            }
           }
         }
-        if (q == 0) {
-          // bias k-step (columns 128..135): element 256 = 0 for live tokens, -inf for masked ones
-          const uint32_t bias[8] = {live ? 0u : neg_inf, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-          tc::tmem_st8(t_a + 128, bias);
-        }
-        tc::tmem_wait_st();
-        tc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(b_k + 8 * b);
-
-        // V -> V^T[b], once the PV of stage it - 2 (the last reader of V^T[b]) is done
-        if (it >= 2) {
-          wait(b_pv, (it - 2) & 1);
-          tc::tc_fence_after();
-        }
-        uint8_t* vt_row = sm.vt[b] + vt_off;
-        if (is_int) {
-          const uint32_t vw[4] = {vc.x, vc.y, vc.z, vc.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t r[8];
-            tc_lut_word(vw[j], vlut.x, vlut.y, r);
-            *reinterpret_cast<uint4*>(vt_row + (2 * j) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
-            *reinterpret_cast<uint4*>(vt_row + (2 * j + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
+        if (is_k) {
+          if (q == 0) {
+            // bias k-step (columns 128..135): element 256 = 0 for live tokens, -inf for masked ones
+            const uint32_t bias[8] = {live ? 0u : neg_inf, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+            tc::tmem_st8(t_a + 128, bias);
           }
+          tc::tmem_wait_st();
+          tc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(b_k + 8 * b);
         } else {
-#pragma unroll 1
-          for (int j = 0; j < 4; ++j) {
-            uint32_t r[8];
-            tc_pack_word<T, true>(srow_v + 16 * j, live, r);
-            *reinterpret_cast<uint4*>(vt_row + (2 * j) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
-            *reinterpret_cast<uint4*>(vt_row + (2 * j + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
-          }
+          tc::fence_async_smem();
         }
-        tc::fence_async_smem();
         pos_it = pos;
-      } else if (it >= 2) {
-        // last softmax: O must hold every earlier stage before a rescale
+      }
+      if (it >= 2 && !pv_done) {
+        // P^T[(it - 1) & 1] and, on a rescale, O: every PV up to stage it - 2 is done
         wait(b_pv, (it - 2) & 1);
         tc::tc_fence_after();
       }
