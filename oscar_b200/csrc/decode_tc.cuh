@@ -13,10 +13,15 @@
 //     [8 q, 8 q + 8) of their softmax.  The four roles of a scheduler wait on
 //     different buffers and overlap; no barrier spans the CTA inside a stage.
 //
-// Prologue: the split's staging owner tags are scanned into a bitmask of
-// staged positions (owner[(blk % rows) * bs + off] == blk, backend.py:172-176).
-// INT2 stages mask those positions; after them, "staged stages" attend the
-// staged positions (in position order, 128 per stage) from their fp32 rows.
+// Staging window (owner[(blk % rows) * bs + off] == blk, backend.py:172-176):
+// staged positions inside the split's own range are masked in its INT2 stages
+// (the owner tags of each stage's seats arrive by bulk copy with the stage).
+// The request's staged positions are attended by the CTAs of the request in
+// turn, 32-position group g by split g % splits, so that a sink or recent
+// window spreads over many CTAs instead of loading one SM with its fp32 rows:
+// the prologue scans this CTA's groups, and "staged stages" over their staged
+// positions (128 per stage) run before the INT2 stages, their fp32 loads
+// overlapping the TMA latency of the first INT2 stages.
 //
 // Per stage:
 //   K -> values T(fp16(code * scale + zero)) (streaming_attention.py:116-124)
@@ -38,9 +43,12 @@
 // The normalised partial (O, LSE) goes to the workspace;
 // decode_combine_kernel merges the splits with the causal current chunk.
 //
-// Dims inside each 16-dim group are permuted as [0,2,..,14,1,3,..,15] (the
-// order the look-up emits them); Q is loaded in the same order and the output
-// dims are mapped back when the partial is written.
+// Dim orders inside each 16-dim group: K columns (pairs of k elements) hold
+// dims (0,2) (1,3) (4,6) (5,7) (8,10) (9,11) (12,14) (13,15), so that the four
+// columns 2m, 2m + 1 of a token come from its dims 4m .. 4m + 3 (a 16-byte
+// piece of an fp32 row: staged rows load 64 contiguous bytes per token); Q is
+// loaded in the same order.  V's M index runs over dims [0,2,..,14,1,3,..,15]
+// (the order the look-up emits them), mapped back when the partial is written.
 #pragma once
 
 #include <climits>
@@ -77,8 +85,11 @@ struct TcSmem {
   uint8_t pt[2][kTcRows * kTcStage * 2];  // P^T: address(tok, n) = (n/8)*2048 + (tok/8)*128 + (tok%8)*16 + (n%8)*2
   uint8_t qb[kTcRows * kTcK * 2];      // Q:   address(n, k)   = (n/8)*4352 + (k/8)*128 + (n%8)*16 + (k%8)*2
   int btab[kTcMaxPages];
-  uint32_t smask[kTcMaxWords];  // staged positions of the split, bit (pos - lo)
-  int spref[kTcMaxWords + 1];   // exclusive prefix counts of smask
+  alignas(16) int64_t own[2][kTcStage];  // owner tags of the stage's seats (bulk-copied with the stage)
+  uint32_t gmask[kTcMaxWords];  // staged positions this CTA attends: 32-position group sp + k * splits
+  int gpref[kTcMaxWords + 1];   // exclusive prefix counts of gmask
+  int64_t srow[kTcStage];       // first staged stage: fp32 row offset per token slot (-1: none)
+  int spos[kTcStage];           // first staged stage: position per token slot
   int lim[kTcRows];             // cache-only chunks: row r sees positions < lim[r]
   alignas(16) int red[2][16][8];  // slow-path row maxima, double-buffered
   float lsum[16][8];
@@ -108,6 +119,15 @@ OSCAR_DEVINL void tc_lut_word(uint32_t w, uint32_t x, uint32_t y, uint32_t* r) {
     const uint32_t hi = prmt(y, 0u, sel[i]);  // high bytes
     r[2 * i] = prmt(lo, hi, 0x5140u);
     r[2 * i + 1] = prmt(lo, hi, 0x7362u);
+  }
+}
+
+// tc_lut_word's registers in the K column order: dims (0,2) (1,3) (4,6) (5,7) ..
+OSCAR_DEVINL void tc_k_order(const uint32_t* in, uint32_t* out) {
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    out[2 * m] = in[m];
+    out[2 * m + 1] = in[4 + m];
   }
 }
 
@@ -181,9 +201,10 @@ OSCAR_DEVINL int tc_ord(float v) {
 OSCAR_DEVINL float tc_unord(int k) { return __int_as_float(k >= 0 ? k : k ^ 0x7fffffff); }
 
 // TMA of INT2 stage s into ring slot s & 1: four 48-byte boxes (K [0,48),
-// K [48,96), V [0,48), V [16,64)) of `rows` tokens per page of the stage
-OSCAR_DEVINL void tc_issue_stage(TcSmem& sm, int s, int lo, int hi, int bs_log2, int page0, int h, int64_t ksh,
-                                 int64_t vsh, const CUtensorMap* tmk, const CUtensorMap* tmv, uint32_t b_full) {
+// K [48,96), V [0,48), V [16,64)) of `rows` tokens per page of the stage, and
+// (with a staging window) the owner tags of the same seats by one bulk copy
+OSCAR_DEVINL void tc_issue_stage(TcSmem& sm, const AttnArgs& a, int s, int lo, int hi, int bs_log2, int page0, int h,
+                                 const CUtensorMap* tmk, const CUtensorMap* tmv, uint32_t b_full) {
   const int bs = 1 << bs_log2;
   const int rows_box = min(bs, kTcStage);
   const int slot = s & 1;
@@ -191,17 +212,21 @@ OSCAR_DEVINL void tc_issue_stage(TcSmem& sm, int s, int lo, int hi, int bs_log2,
   const int end = min(base + kTcStage, hi);
   const int pg_first = base >> bs_log2, pg_last = (end - 1) >> bs_log2;
   const uint32_t bar = b_full + 8 * slot;
-  tc::mbar_expect_tx(bar, (uint32_t)((pg_last - pg_first + 1) * rows_box * 4 * kTcRow));
+  const bool tags = a.owner != nullptr;
+  tc::mbar_expect_tx(bar, (uint32_t)((pg_last - pg_first + 1) * rows_box * (4 * kTcRow + (tags ? 8 : 0))));
   for (int pg = pg_first; pg <= pg_last; ++pg) {
     const int blk = sm.btab[pg - page0];
     const int off0 = (bs > kTcStage) ? base - (pg << bs_log2) : 0;
     const int row = (pg << bs_log2) + off0 - base;
     const int y = (blk << bs_log2) + off0;
-    const int xk = (int)(h * ksh), xv = (int)(h * vsh);
+    const int xk = (int)(h * a.ksh), xv = (int)(h * a.vsh);
     tc::tma_load_2d(smem_u32(&sm.ka[slot][row][0]), tmk, xk, y, bar);
     tc::tma_load_2d(smem_u32(&sm.kb[slot][row][0]), tmk, xk + 48, y, bar);
     tc::tma_load_2d(smem_u32(&sm.va[slot][row][0]), tmv, xv, y, bar);
     tc::tma_load_2d(smem_u32(&sm.vb[slot][row][0]), tmv, xv + 16, y, bar);
+    if (tags)
+      tc::bulk_load(smem_u32(&sm.own[slot][row]), a.owner + (int64_t)(blk % (int)a.stage_rows) * bs + off0,
+                    (uint32_t)rows_box * 8u, bar);
   }
 }
 
@@ -241,7 +266,9 @@ __global__ void __maxnreg__(96)
   const int n_int = (hi > lo) ? (hi - lo + kTcStage - 1) / kTcStage : 0;  // INT2 stages
   const int page0 = lo >> bs_log2;
   const int npages = (hi > lo) ? ((hi - 1) >> bs_log2) - page0 + 1 : 0;
-  const int nwords = (hi > lo) ? (hi - lo + 31) >> 5 : 0;
+  const int nsplit = p.splits[ri];
+  const int ngroups32 = (prefix + 31) >> 5;
+  const int ngroups = min(sp < ngroups32 ? (ngroups32 - 1 - sp) / nsplit + 1 : 0, kTcMaxWords);
   constexpr int kWarps = kTcCompute / 32;
 
   const uint32_t b_full = smem_u32(&sm.bar_full[0]), b_empty = smem_u32(&sm.bar_empty[0]);
@@ -249,34 +276,47 @@ __global__ void __maxnreg__(96)
                  b_pv = smem_u32(&sm.bar_pv);
   const TcWait wait{&sm.abort};
 
-  // ---------------- prologue: barriers, block-table slice, Q operand, TMEM, staged bitmask
-  if (tid == 0) {
+  // ---------------- prologue.  The producer warp sets up barriers, the page
+  // slice and TMEM and issues the first two INT2 stages' TMA at once;
+  // meanwhile the dequant warps load Q, scan this CTA's staged groups and
+  // locate the rows of its first staged stage.  Staged stages run first, so
+  // their fp32 loads overlap the TMA of the first INT2 stages.
+  if (warp == kWarps) {
+    if (lane == 0) {
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(b_full + 8 * i, 1);
-      tc::mbar_init(b_empty + 8 * i, kWarps);
+      for (int i = 0; i < 2; ++i) {
+        tc::mbar_init(b_full + 8 * i, 1);
+        tc::mbar_init(b_empty + 8 * i, kWarps);
+      }
+      tc::mbar_init(b_k, kWarps);
+      tc::mbar_init(b_k + 8, kWarps);
+      tc::mbar_init(b_s, 1);
+      tc::mbar_init(b_s + 8, 1);
+      tc::mbar_init(b_p, kWarps);
+      tc::mbar_init(b_pv, 1);
+      sm.abort = 0;
+      tc::mbar_fence_init();
     }
-    tc::mbar_init(b_k, kWarps);
-    tc::mbar_init(b_k + 8, kWarps);
-    tc::mbar_init(b_s, 1);
-    tc::mbar_init(b_s + 8, 1);
-    tc::mbar_init(b_p, kWarps);
-    tc::mbar_init(b_pv, 1);
-    sm.abort = 0;
-    tc::mbar_fence_init();
-  }
-  if (tid < kTcRows) sm.lim[tid] = tid < R ? seq - qlen + tid / G + 1 : INT_MIN;
-  for (int i = tid; i < npages; i += kTcThreads) {
-    int blk = a.bt[(int64_t)req * a.bt_stride + page0 + i];
-    if (blk < 0 || blk >= a.num_blocks) {
-      flag_error(2u);
-      blk = 0;
+    for (int i = lane; i < npages; i += 32) {
+      int blk = a.bt[(int64_t)req * a.bt_stride + page0 + i];
+      if (blk < 0 || blk >= a.num_blocks) {
+        flag_error(2u);
+        blk = 0;
+      }
+      sm.btab[i] = blk;
     }
-    sm.btab[i] = blk;
-  }
-  if (tid < kTcCompute) {
-    // Q rows n < R, 16-dim word j: k-group 2j holds dims 16j + {0,2,..,14}, 2j+1 dims 16j + {1,3,..,15};
-    // k-groups 32, 33 hold the bias column: 1 at k = 256, zeros after
+    tc::tmem_alloc(smem_u32(&sm.tmem), kTcCols);
+    tc::tmem_relinquish();
+    __syncwarp();
+    if (tc::elect_one()) {
+      for (int s = 0; s < min(2, n_int); ++s) tc_issue_stage(sm, a, s, lo, hi, bs_log2, page0, h, &tmk, &tmv, b_full);
+    }
+    __syncwarp();
+  } else {
+    if (tid < kTcRows) sm.lim[tid] = tid < R ? seq - qlen + tid / G + 1 : INT_MIN;
+    // Q rows n < R, 16-dim word j: k-group 2j holds dims 16j + {0,2,1,3,4,6,5,7}, 2j+1 dims
+    // 16j + {8,10,9,11,12,14,13,15} (the K column order); k-groups 32, 33 hold the bias
+    // column: 1 at k = 256, zeros after
     for (int u = tid; u < kTcRows * 17; u += kTcCompute) {
       const int n = u / 17, j = u - 17 * (u / 17);
       uint4 ev = make_uint4(0, 0, 0, 0), od = ev;
@@ -287,51 +327,109 @@ __global__ void __maxnreg__(96)
             reinterpret_cast<const T*>(a.q) + ((int64_t)(q_start + n / G) * a.hq + (int64_t)h * G + n % G) * D;
         const uint4 q0 = *reinterpret_cast<const uint4*>(qrow + 16 * j);
         const uint4 q1 = *reinterpret_cast<const uint4*>(qrow + 16 * j + 8);
-        ev = make_uint4(prmt(q0.x, q0.y, 0x5410u), prmt(q0.z, q0.w, 0x5410u), prmt(q1.x, q1.y, 0x5410u),
-                        prmt(q1.z, q1.w, 0x5410u));
-        od = make_uint4(prmt(q0.x, q0.y, 0x7632u), prmt(q0.z, q0.w, 0x7632u), prmt(q1.x, q1.y, 0x7632u),
+        ev = make_uint4(prmt(q0.x, q0.y, 0x5410u), prmt(q0.x, q0.y, 0x7632u), prmt(q0.z, q0.w, 0x5410u),
+                        prmt(q0.z, q0.w, 0x7632u));
+        od = make_uint4(prmt(q1.x, q1.y, 0x5410u), prmt(q1.x, q1.y, 0x7632u), prmt(q1.z, q1.w, 0x5410u),
                         prmt(q1.z, q1.w, 0x7632u));
       }
       uint8_t* dst = sm.qb + (n >> 3) * kTcQSbo + (2 * j) * 128 + (n & 7) * 16;
       *reinterpret_cast<uint4*>(dst) = ev;
       *reinterpret_cast<uint4*>(dst + 128) = od;
     }
-  }
-  if (warp == kWarps) {
-    tc::tmem_alloc(smem_u32(&sm.tmem), kTcCols);
-    tc::tmem_relinquish();
-  }
-  __syncthreads();  // btab ready
-  if (tid < kTcCompute) {
-    for (int base = lo + (tid & ~31); base < hi; base += kTcCompute) {
-      const int pos = base + lane;
-      bool hit = false;
-      if (a.owner != nullptr && pos < hi) {
-        const int blk = sm.btab[(pos >> bs_log2) - page0];
-        hit = a.owner[(int64_t)(blk % (int)a.stage_rows) * bs + (pos & (bs - 1))] == (int64_t)blk;
-      }
-      const uint32_t bits = __ballot_sync(0xffffffffu, hit);
-      if (lane == 0) sm.smask[(base - lo) >> 5] = bits;
-    }
-  }
-  __syncthreads();  // smask ready
-  if (warp == 0) {
-    int run = 0;
-    for (int w0 = 0; w0 < nwords; w0 += 32) {
-      const int wi = w0 + lane;
-      const int c = (wi < nwords) ? __popc(sm.smask[wi]) : 0;
-      int incl = c;
+    // this CTA's groups of the whole request, g = sp + k * nsplit: up to four per
+    // warp (block-table loads first, then the owner tags), kept in registers until
+    // the prefix counts give each staged position its index j; the first staged
+    // stage's rows and positions (j < 128) then go to srow / spos
+    constexpr int kScanPer = 4;
+    const bool scan_all = ngroups <= kScanPer * kWarps;
+    int gblk[kScanPer];
+    bool ghit[kScanPer];
 #pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, d);
-        if (lane >= d) incl += y;
-      }
-      if (wi < nwords) sm.spref[wi] = run + incl - c;
-      run += __shfl_sync(0xffffffffu, incl, 31);
+    for (int u = 0; u < kScanPer; ++u) {
+      gblk[u] = -1;
+      ghit[u] = false;
     }
-    if (lane == 0) {
-      sm.spref[nwords] = run;
-      sm.n_staged = run;
+    for (int k0 = warp; k0 < ngroups; k0 += kScanPer * kWarps) {
+#pragma unroll
+      for (int u = 0; u < kScanPer; ++u) {
+        const int k = k0 + u * kWarps, pos = (sp + k * nsplit) * 32 + lane;
+        gblk[u] = -1;
+        if (a.owner != nullptr && k < ngroups && pos < prefix) {
+          gblk[u] = a.bt[(int64_t)req * a.bt_stride + (pos >> bs_log2)];
+          if (gblk[u] >= a.num_blocks) gblk[u] = -1;
+        }
+      }
+      int64_t tag[kScanPer];
+#pragma unroll
+      for (int u = 0; u < kScanPer; ++u) {
+        const int k = k0 + u * kWarps, pos = (sp + k * nsplit) * 32 + lane;
+        tag[u] = gblk[u] >= 0 ? a.owner[(int64_t)(gblk[u] % (int)a.stage_rows) * bs + (pos & (bs - 1))] : -2;
+      }
+#pragma unroll
+      for (int u = 0; u < kScanPer; ++u) {
+        const int k = k0 + u * kWarps;
+        ghit[u] = gblk[u] >= 0 && tag[u] == (int64_t)gblk[u];
+        const uint32_t bits = __ballot_sync(0xffffffffu, ghit[u]);
+        if (lane == 0 && k < ngroups) sm.gmask[k] = bits;
+      }
+    }
+    if (tid < kTcStage) {
+      sm.srow[tid] = -1;
+      sm.spos[tid] = hi;
+    }
+    tc::bar_sync(5, kTcCompute);  // gmask ready
+    if (warp == 0) {
+      int run = 0;
+      for (int w0 = 0; w0 < ngroups; w0 += 32) {
+        const int wi = w0 + lane;
+        const int c = (wi < ngroups) ? __popc(sm.gmask[wi]) : 0;
+        int incl = c;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, d);
+          if (lane >= d) incl += y;
+        }
+        if (wi < ngroups) sm.gpref[wi] = run + incl - c;
+        run += __shfl_sync(0xffffffffu, incl, 31);
+      }
+      if (lane == 0) {
+        sm.gpref[ngroups] = run;
+        sm.n_staged = run;
+      }
+    }
+    tc::bar_sync(5, kTcCompute);  // gpref ready
+    if (scan_all) {
+      // the registers hold this warp's (only) batch of groups
+#pragma unroll
+      for (int u = 0; u < kScanPer; ++u) {
+        const int k = warp + u * kWarps;
+        if (k < ngroups && ghit[u]) {
+          const int j = sm.gpref[k] + __popc(sm.gmask[k] & ((1u << lane) - 1u));
+          if (j < kTcStage) {
+            const int pos = (sp + k * nsplit) * 32 + lane;
+            const int64_t seat = (int64_t)(gblk[u] % (int)a.stage_rows) * bs + (pos & (bs - 1));
+            const int slot = (j & 3) * 32 + (j >> 2);  // token slot of staged index j
+            sm.srow[slot] = (seat * a.hk + h) * D;
+            sm.spos[slot] = pos;
+          }
+        }
+      }
+    } else if (tid < kTcStage) {
+      // more groups than one pass holds: search the prefix counts
+      const int j = (tid & 31) * 4 + (tid >> 5);
+      if (j < sm.n_staged) {
+        int lo_w = 0, hi_w = ngroups - 1;  // last group whose prefix count is <= j
+        while (lo_w < hi_w) {
+          const int mid = (lo_w + hi_w + 1) >> 1;
+          if (sm.gpref[mid] <= j) lo_w = mid; else hi_w = mid - 1;
+        }
+        const int bit = (int)__fns(sm.gmask[lo_w], 0u, j - sm.gpref[lo_w] + 1);
+        const int pos = (sp + lo_w * nsplit) * 32 + bit;
+        const int blk = a.bt[(int64_t)req * a.bt_stride + (pos >> bs_log2)];
+        const int64_t seat = (int64_t)(blk % (int)a.stage_rows) * bs + (pos & (bs - 1));
+        sm.srow[tid] = (seat * a.hk + h) * D;
+        sm.spos[tid] = pos;
+      }
     }
   }
   tc::fence_async_smem();
@@ -340,7 +438,8 @@ __global__ void __maxnreg__(96)
   tc::tc_fence_after();
   const uint32_t tmem = sm.tmem;
   const int n_staged = sm.n_staged;
-  const int nst = n_int + (n_staged + kTcStage - 1) / kTcStage;
+  const int n_sst = (n_staged + kTcStage - 1) / kTcStage;  // staged stages, run first
+  const int nst = n_sst + n_int;
 
   if (warp == kWarps) {
     // ============================ producer + MMA issuer
@@ -360,11 +459,6 @@ __global__ void __maxnreg__(96)
       const uint64_t dq0 = tc::smem_desc(smem_u32(sm.qb), 128, kTcQSbo);
       const uint64_t dv0 = tc::smem_desc(smem_u32(sm.vt[0]), 128, kTcVtSbo);
       const uint64_t dp0 = tc::smem_desc(smem_u32(sm.pt[0]), 128, kTcVtSbo);
-      if (tc::elect_one()) {
-        for (int s = 0; s < min(2, n_int); ++s)
-          tc_issue_stage(sm, s, lo, hi, bs_log2, page0, h, a.ksh, a.vsh, &tmk, &tmv, b_full);
-      }
-      __syncwarp();
       for (int qs = 0, ps = 0; ps < nst; ) {
         if (qs < nst && qs <= ps + 1) {
           // QK of stage qs into S[qs & 1] from A_K[qs & 1]
@@ -377,9 +471,10 @@ __global__ void __maxnreg__(96)
             tc::mma_commit(b_s + 8 * (qs & 1));
           }
           __syncwarp();
-          if (qs + 2 < n_int) {
-            wait(b_empty + 8 * (qs & 1), (qs >> 1) & 1);
-            if (tc::elect_one()) tc_issue_stage(sm, qs + 2, lo, hi, bs_log2, page0, h, a.ksh, a.vsh, &tmk, &tmv, b_full);
+          const int qi = qs - n_sst;  // INT2 stage index (the ring runs over INT2 stages only)
+          if (qi >= 0 && qi + 2 < n_int) {
+            wait(b_empty + 8 * (qi & 1), (qi >> 1) & 1);
+            if (tc::elect_one()) tc_issue_stage(sm, a, qi + 2, lo, hi, bs_log2, page0, h, &tmk, &tmv, b_full);
             __syncwarp();
           }
           ++qs;
@@ -461,18 +556,20 @@ __global__ void __maxnreg__(96)
         }
         int pos;
         bool live;
-        const bool is_int = it < n_int;
+        const bool is_int = it >= n_sst;
         if (is_int) {
-          const int slot = it & 1;
-          pos = lo + it * kTcStage + tok;
-          wait(b_full + 8 * slot, (it >> 1) & 1);
+          const int ii = it - n_sst;  // INT2 stage
+          const int slot = ii & 1;
+          pos = lo + ii * kTcStage + tok;
+          wait(b_full + 8 * slot, (ii >> 1) & 1);
           const uint8_t* raw = &sm.ka[slot][tok][0];
           const uint32_t meta = *reinterpret_cast<const uint32_t*>(raw + meta_off);
           const uint4 c0 = *reinterpret_cast<const uint4*>(raw + off0);
           const uint4 c1 = *reinterpret_cast<const uint4*>(raw + off1);
+          live = pos < hi;
+          if (live && a.owner != nullptr) live = sm.own[slot][tok] != (int64_t)sm.btab[(pos >> bs_log2) - page0];
           __syncwarp();
           if (lane == 0) tc::mbar_arrive(b_empty + 8 * slot);
-          live = pos < hi && !((sm.smask[(pos - lo) >> 5] >> ((pos - lo) & 31)) & 1u);
           uint2 lut = make_uint2(0, 0);
           if (live) lut = is_k ? tc_klut<T>(meta) : tc_vlut<T>(meta);
           const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
@@ -481,7 +578,11 @@ __global__ void __maxnreg__(96)
             for (int g = 0; g < 2; ++g) {
               uint32_t r[32];
 #pragma unroll
-              for (int j = 0; j < 4; ++j) tc_lut_word(cw[4 * g + j], lut.x, lut.y, r + 8 * j);
+              for (int j = 0; j < 4; ++j) {
+                uint32_t v[8];
+                tc_lut_word(cw[4 * g + j], lut.x, lut.y, v);
+                tc_k_order(v, r + 8 * j);
+              }
               tc::tmem_st32(t_a + 32 * g, r);
             }
           } else {
@@ -501,30 +602,83 @@ __global__ void __maxnreg__(96)
             }
           }
         } else {
-          // staged stage: the (128 (it - n_int) + tok)-th staged position, fp32 rows
-          const int j = (it - n_int) * kTcStage + tok;
+          // staged stage: the j-th staged position of this CTA's groups (fp32 rows);
+          // consecutive j go to different lane quarters, so a partial stage
+          // spreads its loads over all sixteen warps
+          const int j = it * kTcStage + (tok & 31) * 4 + (tok >> 5);
           live = j < n_staged;
           pos = hi;
           int64_t row_off = 0;
-          if (live) {
-            int lo_w = 0, hi_w = nwords - 1;  // last word whose prefix count is <= j
+          if (it == 0) {
+            // located in the prologue
+            row_off = live ? sm.srow[tok] : 0;
+            pos = sm.spos[tok];
+          } else if (live) {
+            int lo_w = 0, hi_w = ngroups - 1;  // last group whose prefix count is <= j
             while (lo_w < hi_w) {
               const int mid = (lo_w + hi_w + 1) >> 1;
-              if (sm.spref[mid] <= j) lo_w = mid; else hi_w = mid - 1;
+              if (sm.gpref[mid] <= j) lo_w = mid; else hi_w = mid - 1;
             }
-            const int bit = (int)__fns(sm.smask[lo_w], 0u, j - sm.spref[lo_w] + 1);
-            pos = lo + 32 * lo_w + bit;
-            const int blk = sm.btab[(pos >> bs_log2) - page0];
+            const int bit = (int)__fns(sm.gmask[lo_w], 0u, j - sm.gpref[lo_w] + 1);
+            pos = (sp + lo_w * nsplit) * 32 + bit;
+            const int blk = a.bt[(int64_t)req * a.bt_stride + (pos >> bs_log2)];
             const int64_t seat = (int64_t)(blk % (int)a.stage_rows) * bs + (pos & (bs - 1));
             row_off = (seat * a.hk + h) * D;
           }
-          const float* srow = (is_k ? a.stage_k : a.stage_v) + row_off + 128 * half;
+          // coalesced fp32 loads: a thread reads 16 bytes (dims 4 (lane % 4) .. + 3 of a 16-dim
+          // group) of the token of lane lane / 4 (+ 8, 16, 24) of the quarter, so each
+          // instruction covers 8 tokens x 64 contiguous bytes; dead tokens get zeros
+          const float* src = (is_k ? a.stage_k : a.stage_v) + 128 * half + 4 * (lane & 3);
+          // (loads of a pass are issued before any store: one memory round trip per pass)
           if (is_k) {
-#pragma unroll 2
-            for (int w = 0; w < 8; ++w) {
-              uint32_t r[8];
-              tc_pack_word<T, false>(srow + 16 * w, live, r);
-              tc::tmem_st8(t_a + 8 * w, r);
+            // tcgen05.st.16x256b: thread i writes lanes i / 4 and 8 + i / 4 of a 16-lane half,
+            // columns 2 (i % 4), + 1 of each 16-dim group: (dims 4m, 4m+2), (4m+1, 4m+3)
+#pragma unroll 1
+            for (int hb = 0; hb < 2; ++hb) {
+              const int la = 16 * hb + (lane >> 2), lb = la + 8;
+              const int64_t ra = __shfl_sync(0xffffffffu, row_off, la), rb = __shfl_sync(0xffffffffu, row_off, lb);
+              const bool va = __shfl_sync(0xffffffffu, (int)live, la) != 0;
+              const bool vb = __shfl_sync(0xffffffffu, (int)live, lb) != 0;
+              if (!__any_sync(0xffffffffu, vb)) {
+                // lanes 8..15 of the half are dead: one pass of 8 loads
+                float4 xs[8];
+#pragma unroll
+                for (int g = 0; g < 8; ++g)
+                  xs[g] = va ? __ldg(reinterpret_cast<const float4*>(src + ra + 16 * g)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int cb = 0; cb < 2; ++cb) {
+                  uint32_t r[16];
+#pragma unroll
+                  for (int g = 0; g < 4; ++g) {
+                    const float4 x = xs[4 * cb + g];
+                    r[4 * g] = pack2<T>(chain<T>(x.x), chain<T>(x.z));
+                    r[4 * g + 1] = pack2<T>(chain<T>(x.y), chain<T>(x.w));
+                    r[4 * g + 2] = 0u;
+                    r[4 * g + 3] = 0u;
+                  }
+                  tc::tmem_st16x256_x4(t_a + ((uint32_t)(16 * hb) << 16) + 32 * cb, r);
+                }
+              } else {
+#pragma unroll 1
+                for (int cb = 0; cb < 2; ++cb) {
+                  float4 xs[4], ys[4];
+#pragma unroll
+                  for (int g = 0; g < 4; ++g) {
+                    const int off = 16 * (4 * cb + g);
+                    xs[g] = va ? __ldg(reinterpret_cast<const float4*>(src + ra + off)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    ys[g] = vb ? __ldg(reinterpret_cast<const float4*>(src + rb + off)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                  }
+                  uint32_t r[16];
+#pragma unroll
+                  for (int g = 0; g < 4; ++g) {
+                    r[4 * g] = pack2<T>(chain<T>(xs[g].x), chain<T>(xs[g].z));
+                    r[4 * g + 1] = pack2<T>(chain<T>(xs[g].y), chain<T>(xs[g].w));
+                    r[4 * g + 2] = pack2<T>(chain<T>(ys[g].x), chain<T>(ys[g].z));
+                    r[4 * g + 3] = pack2<T>(chain<T>(ys[g].y), chain<T>(ys[g].w));
+                  }
+                  tc::tmem_st16x256_x4(t_a + ((uint32_t)(16 * hb) << 16) + 32 * cb, r);
+                }
+              }
             }
           } else {
             if (it >= 2) {
@@ -532,13 +686,24 @@ __global__ void __maxnreg__(96)
               tc::tc_fence_after();
               pv_done = true;
             }
-            uint8_t* vt_row = sm.vt[b] + vt_off;
-#pragma unroll 2
-            for (int w = 0; w < 8; ++w) {
-              uint32_t r[8];
-              tc_pack_word<T, true>(srow + 16 * w, live, r);
-              *reinterpret_cast<uint4*>(vt_row + (2 * w) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
-              *reinterpret_cast<uint4*>(vt_row + (2 * w + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
+            // V^T word of (token, dims 4m, 4m+2) at row group 2g, (4m+1, 4m+3) at 2g+1;
+            // the 8 tokens x 4 words of an instruction are 128 contiguous bytes
+            uint8_t* vt_q = sm.vt[b] + (16 * half) * kTcVtSbo + ((warp & 3) * 4) * 128 + 4 * lane;
+#pragma unroll 1
+            for (int o = 0; o < 4; ++o) {
+              const int lt = 8 * o + (lane >> 2);
+              const int64_t rt = __shfl_sync(0xffffffffu, row_off, lt);
+              const bool vt = __shfl_sync(0xffffffffu, (int)live, lt) != 0;
+              float4 xs[8];
+#pragma unroll
+              for (int g = 0; g < 8; ++g)
+                xs[g] = vt ? __ldg(reinterpret_cast<const float4*>(src + rt + 16 * g)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+              for (int g = 0; g < 8; ++g) {
+                uint32_t* dst = reinterpret_cast<uint32_t*>(vt_q + o * 128 + (2 * g) * kTcVtSbo);
+                dst[0] = pack2<__half>(chain_f16<T>(xs[g].x), chain_f16<T>(xs[g].z));
+                dst[kTcVtSbo / 4] = pack2<__half>(chain_f16<T>(xs[g].y), chain_f16<T>(xs[g].w));
+              }
             }
           }
         }

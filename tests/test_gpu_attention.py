@@ -185,3 +185,31 @@ def test_merge_of_sequence_shards_equals_whole(attn_path):
     kernels.merge_slab(a_out, a_lse, b_out, b_lse, 0, None)
     torch.testing.assert_close(a_out, whole, atol=2e-5, rtol=2e-5)
     torch.testing.assert_close(a_lse, whole_lse, atol=2e-5, rtol=2e-5)
+
+
+@pytest.mark.parametrize("frac", [0.02, 0.3])
+def test_scattered_staged_positions_match_oracle(frac, attn_path):
+    """Staged positions anywhere in the history (not only sink / recent
+    windows): every one is masked in its split's INT2 stages and attended
+    once from its fp32 row, by whichever CTA the kernel assigns it to."""
+    from oscar_b200 import kernels
+
+    dev = need_gpu()
+    case = make_case([5000, 3000, 700], [4, 2, 3], hk=2, seed=23)
+    sk, sv, owner = case.stage
+    rows, bs = owner.shape
+    g = torch.Generator().manual_seed(int(frac * 1000))
+    offset = 0
+    for r, prefix in enumerate([5000, 3000, 700]):
+        pos = torch.nonzero(torch.rand(prefix, generator=g) < frac).flatten()
+        blk = case.bt[r, pos // bs].long()
+        row, col = blk % rows, pos % bs
+        owner[row, col] = blk
+        sk[row, col] = case.old_k[offset + pos]
+        sv[row, col] = case.old_v[offset + pos]
+        offset += prefix
+    args, dt = case_to_oracle(case)
+    want_out, want_lse = orc.streaming_attention(*args, dtype=dt)
+    out, lse = kernels.slab_attention(*case_to_device(case, args[3], args[4], dev))
+    assert_attention_close(out, lse, want_out, want_lse)
+    assert kernels.device_error(dev) == 0
