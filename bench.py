@@ -109,7 +109,9 @@ def build_layers(torch, dev, n_layers):
             pos = torch.arange(p, p + n, device=dev)
             slots.append(case.bt[r, pos // 128].long() * 128 + pos % 128)
         md = NS(num_actual_tokens=case.q.shape[0], slot_mapping=torch.cat(slots), query_start_loc_cpu=torch.tensor(case.qsl),
-                seq_lens_list=case.seqs, block_tables=case.bt)
+                seq_lens_list=case.seqs, block_tables=case.bt,
+                query_start_loc=torch.tensor(case.qsl, dtype=torch.int32, device=dev),
+                seq_lens=torch.tensor(case.seqs, dtype=torch.int32, device=dev))
         out = torch.empty(case.q.shape[0], 6 * 256, dtype=torch.bfloat16, device=dev)
         layers.append(NS(layer=layer, cache=cache, q=case.q, k=case.k_new, v=case.v_new, md=md, out=out, case=case))
         del case.old_k, case.old_v
@@ -130,12 +132,20 @@ class ClockSampler:
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"oscar_clocks_{os.getpid()}.csv"
 
     def start(self):
+        """Start sampling and wait for the first sample, so that the sampler's
+        start-up (driver initialisation) is over before any timed region."""
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "100", "-i", str(self.gpu)], stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 10.0 and self.proc.poll() is None:
+            if self.path.exists() and self.path.stat().st_size > 0:
+                break
+            time.sleep(0.05)
 
     def stop(self):
         if self.proc is None:
@@ -228,6 +238,7 @@ def run_gpu(args):
     import torch
 
     from oscar_b200 import _native, kernels
+    from oscar_b200.graphs import GraphedForward
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -250,17 +261,32 @@ def run_gpu(args):
         lay = layers[i % L]
         impl.forward(lay.layer, lay.q, lay.k, lay.v, lay.cache, lay.md, output=lay.out)
 
+    clocks = ClockSampler(dev.index)
+    clocks.start()
     for i in range(max(args.warmup, 3)):
         step(i)
     torch.cuda.synchronize(dev)
     # bit-level sanity: no bounds violations in warm-up
     assert kernels.device_error(dev) == 0
-
-    clocks = ClockSampler(dev.index)
-    clocks.start()
     n0 = lib.oscar_launch_count()
-    ms = timed(torch, dev, step, args.steps, dist)
-    launches = lib.oscar_launch_count() - n0
+    step(0)
+    launches_per_step = lib.oscar_launch_count() - n0
+    torch.cuda.synchronize(dev)
+
+    # decode steps replay CUDA graphs of the forward (as vLLM does): one graph per layer
+    pool = torch.cuda.graph_pool_handle()
+    graphs = [GraphedForward(impl, lay.layer, lay.q, lay.k, lay.v, lay.cache, lay.md, lay.out, pool=pool)
+              for lay in layers]
+
+    def graph_step(i):
+        graphs[i % L].replay()
+
+    for i in range(max(args.warmup, 3)):
+        graph_step(i)
+    torch.cuda.synchronize(dev)
+    assert kernels.device_error(dev) == 0
+    ms = timed(torch, dev, graph_step, args.steps, dist)
+    launches = launches_per_step * args.steps
     ms_host_paced = timed(torch, dev, step, args.steps, dist, preroll=False)
     clk = clocks.stop()
 
@@ -300,17 +326,15 @@ def run_gpu(args):
     hk_b = [lay.k.cpu().pin_memory() for lay in layers]
     hv_b = [lay.v.cpu().pin_memory() for lay in layers]
     ho_b = [torch.empty(lay.out.shape, dtype=lay.out.dtype).pin_memory() for lay in layers]
-    dq = [torch.empty_like(lay.q) for lay in layers]
-    dk = [torch.empty_like(lay.k) for lay in layers]
-    dv = [torch.empty_like(lay.v) for lay in layers]
 
     def e2e_step(i):
+        # host inputs into the graph's static tensors, replay, result back to the host
         j = i % L
         lay = layers[j]
-        dq[j].copy_(hq_b[j], non_blocking=True)
-        dk[j].copy_(hk_b[j], non_blocking=True)
-        dv[j].copy_(hv_b[j], non_blocking=True)
-        impl.forward(lay.layer, dq[j], dk[j], dv[j], lay.cache, lay.md, output=lay.out)
+        lay.q.copy_(hq_b[j], non_blocking=True)
+        lay.k.copy_(hk_b[j], non_blocking=True)
+        lay.v.copy_(hv_b[j], non_blocking=True)
+        graphs[j].replay()
         ho_b[j].copy_(lay.out, non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
 
@@ -328,7 +352,8 @@ def run_gpu(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": workload_config(L),
         "step_latency_us": ms_step * 1e3,
-        "ms_per_step_host_paced": ms_host_paced / args.steps,
+        "ms_per_step_eager_host_paced": ms_host_paced / args.steps,
+        "step_mode": "CUDA graph replay of the backend forward (oscar_b200.graphs.GraphedForward), one per layer",
         "e2e": {"value": world * tokens / (ms_e2e / args.steps * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e / args.steps},
         "gpu_launches": int(launches),

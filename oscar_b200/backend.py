@@ -68,6 +68,21 @@ def _device_ints(values, device) -> torch.Tensor:
     return t.to(device)
 
 
+def _device_batch(attn_metadata, qsl: list, seqs: list, device) -> tuple:
+    """Device int32 (query_start_loc [B+1], seq_lens [B]) for the staging write:
+    the metadata's own device tensors when it carries them (as vLLM's does:
+    no host-to-device copy, and the call stays capturable in a CUDA graph),
+    else copies of the host lists."""
+    b = len(qsl) - 1
+    dq = getattr(attn_metadata, "query_start_loc", None)
+    ds = getattr(attn_metadata, "seq_lens", None)
+    if isinstance(dq, torch.Tensor) and isinstance(ds, torch.Tensor) and dq.device == device and \
+            ds.device == device and dq.dtype == torch.int32 and ds.dtype == torch.int32 and \
+            dq.numel() >= b + 1 and ds.numel() >= b:
+        return dq[: b + 1].contiguous(), ds[:b].contiguous()
+    return _device_ints(qsl, device), _device_ints(seqs[:b], device)
+
+
 class OscarAttentionImplMixin:
     """The OSCAR read/write/window paths.  Placed first in the MRO of a
     subclass of the running vLLM attention impl (plugin.install_impl)."""
@@ -226,10 +241,17 @@ class OscarAttentionImplMixin:
             hk, d = self.num_kv_heads, self.head_size
             rotated = (self._rotate(key[:n].reshape(n, hk, d), rk), self._rotate(value[:n].reshape(n, hk, d), rv))
         k_rot, v_rot = rotated
+        qsl_d, seqs_d = _device_batch(attn_metadata, qsl, seqs, dev)
+        if torch.cuda.is_current_stream_capturing():
+            # a replayed graph cannot advance a host epoch: the built-in scratch is cleared per call
+            kernels.staging_write_noalloc(k_rot, v_rot, slot.contiguous(), qsl_d, seqs_d, self.sink_eff,
+                                          self._oscar.recent_tokens, layer._oscar_stage_k, layer._oscar_stage_v,
+                                          layer._oscar_slot_owner)
+            return
         layer._oscar_stage_epoch += 1
-        kernels.staging_write(k_rot, v_rot, slot, _device_ints(qsl, dev), _device_ints(seqs[: len(qsl) - 1], dev),
-                              self.sink_eff, self._oscar.recent_tokens, layer._oscar_stage_k, layer._oscar_stage_v,
-                              layer._oscar_slot_owner, layer._oscar_seat_winner, layer._oscar_stage_epoch)
+        kernels.staging_write(k_rot, v_rot, slot, qsl_d, seqs_d, self.sink_eff, self._oscar.recent_tokens,
+                              layer._oscar_stage_k, layer._oscar_stage_v, layer._oscar_slot_owner,
+                              layer._oscar_seat_winner, layer._oscar_stage_epoch)
 
     def _stage(self, layer):
         if self._oscar.window_enabled and getattr(self, "_oscar_stage_ready", False) and \

@@ -131,6 +131,32 @@ def staging_write(k_rot: torch.Tensor, v_rot: torch.Tensor, slot_mapping: torch.
         rows, bs, seat_winner.data_ptr(), int(epoch) & 0xFFFFFFFF, _stream(dev)))
 
 
+def staging_write_noalloc(k_rot: torch.Tensor, v_rot: torch.Tensor, slot_mapping: torch.Tensor, qsl: torch.Tensor,
+                          seqs: torch.Tensor, sink_eff: int, recent_tokens: int, stage_k: torch.Tensor,
+                          stage_v: torch.Tensor, owner: torch.Tensor) -> None:
+    """staging_write with the library's built-in seat scratch, cleared on every
+    call instead of tagged by a host epoch: no caller scratch and no host state,
+    so it can be captured in a CUDA graph and replayed with new slots."""
+    dev = _require_cuda(k_rot, v_rot, slot_mapping, qsl, seqs, stage_k, stage_v, owner)
+    n, h, d = k_rot.shape
+    rows, bs = owner.shape
+    if stage_k.shape != (rows, bs, h, d) or stage_v.shape != stage_k.shape:
+        raise ValueError("Invalid streaming staging geometry")
+    for t in (stage_k, stage_v, owner):
+        if not t.is_contiguous():
+            raise ValueError("Streaming staging tensors must be contiguous")
+    for t in (k_rot, v_rot, slot_mapping, qsl, seqs):
+        if not t.is_contiguous():
+            raise ValueError("staging_write_noalloc: inputs must be contiguous")
+    if k_rot.dtype != torch.float32 or v_rot.dtype != torch.float32 or slot_mapping.dtype != torch.int64 \
+            or qsl.dtype != torch.int32 or seqs.dtype != torch.int32:
+        raise ValueError("staging_write_noalloc: fp32 rows, int64 slots and int32 qsl / seqs expected")
+    check(_native.lib().oscar_staging_write_noalloc(
+        k_rot.data_ptr(), v_rot.data_ptr(), n, h, d, slot_mapping.data_ptr(), qsl.data_ptr(), seqs.data_ptr(),
+        seqs.numel(), int(sink_eff), int(recent_tokens), stage_k.data_ptr(), stage_v.data_ptr(), owner.data_ptr(),
+        rows, bs, _stream(dev)))
+
+
 # ---------------------------------------------------------------------------
 def _validate_tensors(q, k, v, kc, vc, bt, qsl, seqs, stage):
     """streaming_attention._validate_tensors (streaming_attention.py:32-65)."""
