@@ -194,9 +194,9 @@ def timed(torch, dev, fn, steps, dist, preroll=True):
     torch.cuda.synchronize(dev)
     ms = start.elapsed_time(end)
     if dist is not None:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        from oscar_b200.shards import max_over_ranks
+
+        ms = max_over_ranks(ms, device=dev)
         dist.barrier()
     return ms
 
