@@ -55,7 +55,9 @@ int oscar_set_attention_path(int path);
 
 /* Synchronises `stream`, returns and clears the device-side bounds flag of the
  * current device: 0 = clean, otherwise a bitmask (1 = slot out of range,
- * 2 = block-table entry out of range, 8 = merge target row out of range).
+ * 2 = block-table entry out of range, 8 = merge target row out of range,
+ * 16 = a tensor-core decode wait timed out, 32 = more history splits per
+ * request than the tensor-core merge holds).
  * Debug/test helper; the hot path never synchronises. */
 int oscar_device_error(void* stream);
 

@@ -436,6 +436,8 @@ __global__ void __maxnreg__(96)
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
+  // the split merge may be scheduled now: it waits for this grid before reading partials
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   const uint32_t tmem = sm.tmem;
   const int n_staged = sm.n_staged;
   const int n_sst = (n_staged + kTcStage - 1) / kTcStage;  // staged stages, run first
@@ -850,11 +852,15 @@ __global__ void __maxnreg__(96)
         tc::tmem_ld8(t_o + 32 * hh, o);
         tc::tmem_wait_ld();
       }
+      // normalised O in fp16 (the merge reads it once; 2^-11 relative is far inside the
+      // output tolerance), zero for empty rows
       const int dim = tc_dim(128 * hh + tok);
+      __half* po = reinterpret_cast<__half*>(a.part_o);
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
-        const bool keep = (8 * q + r < R) && (L[r] > 0.0f || L[r] != L[r]);
-        if (keep) a.part_o[(prow0 + r) * D + dim] = __uint_as_float(o[r]) / L[r];
+        if (8 * q + r >= R) continue;
+        const bool keep = L[r] > 0.0f || L[r] != L[r];
+        po[(prow0 + r) * D + dim] = __float2half_rn(keep ? __uint_as_float(o[r]) / L[r] : 0.0f);
       }
     }
 #pragma unroll
@@ -869,6 +875,173 @@ __global__ void __maxnreg__(96)
   __syncthreads();
   tc::tc_fence_after();
   if (warp == kWarps) tc::tmem_dealloc(tmem, kTcCols);
+}
+
+// Merge of the splits (_merge_slab, slab_attention.py:156-194, joint form)
+// with the causal current chunk: one warp per query row, lane l owning dims
+// 8 l .. 8 l + 7, two rows per CTA, no block-wide barrier.  Launched as a
+// programmatic dependent of decode_tc_kernel: its CTAs fit beside an
+// attention CTA on an SM, score the current chunk while the attention grid
+// runs, then wait for it and read the splits' LSEs and fp16 partials (in
+// batches of eight 16-byte loads).
+constexpr int kTcCombineWarps = 2;  // 64 threads x <= 128 registers: fits beside an attention CTA
+
+template <typename T>
+__global__ void __launch_bounds__(32 * kTcCombineWarps)
+    tc_combine_kernel(const AttnArgs a, const __grid_constant__ AttnPlan p) {
+  constexpr int D = 256, kMaxKeys = 32, kBatch = 8;
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * kTcCombineWarps + (threadIdx.x >> 5);
+  const int per_req = a.hk * kTcRows;
+  const int ri = gw / per_req;
+  if (ri >= p.num_req) return;
+  const int h = (gw - ri * per_req) / kTcRows, row = gw - ri * per_req - h * kTcRows;
+  const int q_start = p.q_start[ri], qlen = p.q_len[ri], seq = p.seq[ri], prefix = p.prefix[ri];
+  const int G = a.group;
+  if (row >= qlen * G) return;
+  const int tl = row / G;
+  const int64_t qrow = (int64_t)(q_start + tl) * a.hq + (int64_t)h * G + (row - tl * G);
+  const int np = (prefix > 0) ? p.splits[ri] : 0;
+  const int nkeys = (a.k_new != nullptr) ? min(seq - prefix - (qlen - 1 - tl), kMaxKeys) : 0;
+  const int64_t pbase = p.part_begin[ri];
+  const __half* po = reinterpret_cast<const __half*>(a.part_o);
+  auto prow_of = [&](int i) -> int64_t { return ((pbase + i) * a.hk + h) * kTcRows + row; };
+  auto f8 = [](const uint4& u, float* f) {
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = Elem<T>::to_f32(e[i]);
+  };
+
+  // current-chunk scores (natural-log units): key j on every lane after a warp sum
+  const uint4 qu = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.q) + qrow * D + 8 * lane);
+  float qf[8];
+  f8(qu, qf);
+  float kscore = -INFINITY;  // lane j holds the score of key j
+  float gmax = -INFINITY;    // the row's maximum over splits and keys
+  for (int j0 = 0; j0 < nkeys; j0 += 4) {
+    uint4 ku[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      ku[u] = (j0 + u < nkeys) ? *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) +
+                                                                ((int64_t)(q_start + j0 + u) * a.hk + h) * D + 8 * lane)
+                               : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float kf[8];
+      f8(ku[u], kf);
+      float d = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) d = fmaf(qf[i], kf[i], d);
+#pragma unroll
+      for (int o2 = 16; o2 > 0; o2 >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o2);
+      if (lane == j0 + u && j0 + u < nkeys) kscore = d * a.scale_log2 * 0.69314718055994531f;
+    }
+  }
+  // the current chunk's values do not depend on the attention grid: load them now
+  constexpr int kPreV = 4;
+  uint4 vpre[kPreV];
+#pragma unroll
+  for (int j = 0; j < kPreV; ++j)
+    vpre[j] = (j < nkeys) ? *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v_new) +
+                                                           ((int64_t)(q_start + j) * a.hk + h) * D + 8 * lane)
+                          : make_uint4(0u, 0u, 0u, 0u);
+
+  // the partials are written by the attention grid this launch depends on
+  // (programmatic dependent launch: this grid may start while that one runs)
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  // one round of loads: every split's LSE (lane i % 32) and the first
+  // kBatch * 2 partial rows, then the maximum (NaN propagates) and weights
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+  float lsum = 0.0f;
+  for (int i32 = 0; i32 < np; i32 += 32) {
+    const int nb = min(32, np - i32);
+    const float ls = (lane < nb) ? __ldcg(a.part_lse + prow_of(i32 + lane)) : -INFINITY;
+    uint4 ou[2 * kBatch];
+#pragma unroll
+    for (int u = 0; u < 2 * kBatch; ++u)
+      ou[u] = (u < nb) ? __ldcg(reinterpret_cast<const uint4*>(po + prow_of(i32 + u) * D + 8 * lane))
+                       : make_uint4(0u, 0u, 0u, 0u);
+    float mx = (i32 == 0) ? kscore : -INFINITY;
+    mx = nan_max(mx, ls);
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) mx = nan_max(mx, __shfl_xor_sync(0xffffffffu, mx, o2));
+    if (i32 == 0) {
+      // more than 32 splits: the maximum over the later passes joins below
+      for (int j32 = 32; j32 < np; j32 += 32) {
+        float m2 = (j32 + lane < np) ? __ldcg(a.part_lse + prow_of(j32 + lane)) : -INFINITY;
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) m2 = nan_max(m2, __shfl_xor_sync(0xffffffffu, m2, o2));
+        mx = nan_max(mx, m2);
+      }
+      gmax = mx;
+    }
+    const float Mu = (gmax == -INFINITY) ? 0.0f : gmax;
+    const float w = (lane < nb && ls != -INFINITY) ? expf(ls - Mu) : 0.0f;
+    lsum += w;
+#pragma unroll
+    for (int u = 0; u < 2 * kBatch; ++u) {
+      const float wu = __shfl_sync(0xffffffffu, w, u);
+      if (u >= nb) break;
+      const __half* hv = reinterpret_cast<const __half*>(&ou[u]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(wu, __half2float(hv[e]), acc[e]);
+    }
+    for (int b0 = 2 * kBatch; b0 < nb; b0 += kBatch) {
+      uint4 ob[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        ob[u] = (b0 + u < nb) ? __ldcg(reinterpret_cast<const uint4*>(po + prow_of(i32 + b0 + u) * D + 8 * lane))
+                              : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const float wu = __shfl_sync(0xffffffffu, w, (b0 + u) & 31);
+        if (b0 + u >= nb) break;
+        const __half* hv = reinterpret_cast<const __half*>(&ob[u]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(wu, __half2float(hv[e]), acc[e]);
+      }
+    }
+  }
+  if (np == 0) gmax = kscore;
+  float mx = gmax;
+  if (np == 0) {
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) mx = nan_max(mx, __shfl_xor_sync(0xffffffffu, mx, o2));
+    gmax = mx;
+  }
+  const float Mu = (mx == -INFINITY) ? 0.0f : mx;
+  // the row's current-chunk keys
+  {
+    const float wk = (lane < nkeys) ? expf(kscore - Mu) : 0.0f;
+    lsum += wk;
+#pragma unroll
+    for (int j = 0; j < kPreV; ++j) {
+      const float wj = __shfl_sync(0xffffffffu, wk, j);
+      if (j >= nkeys) break;
+      float vf[8];
+      f8(vpre[j], vf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(wj, vf[e], acc[e]);
+    }
+    for (int j = kPreV; j < nkeys; ++j) {
+      const float wj = __shfl_sync(0xffffffffu, wk, j);
+      const uint4 vu = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v_new) +
+                                                       ((int64_t)(q_start + j) * a.hk + h) * D + 8 * lane);
+      float vf[8];
+      f8(vu, vf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(wj, vf[e], acc[e]);
+    }
+  }
+#pragma unroll
+  for (int o2 = 16; o2 > 0; o2 >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o2);
+  const float den = (lsum > 0.0f || lsum != lsum) ? lsum : 1.0f;
+  float4* dst = reinterpret_cast<float4*>(a.out + qrow * D + 8 * lane);
+  dst[0] = make_float4(acc[0] / den, acc[1] / den, acc[2] / den, acc[3] / den);
+  dst[1] = make_float4(acc[4] / den, acc[5] / den, acc[6] / den, acc[7] / den);
+  if (lane == 0) a.lse[qrow] = (mx == -INFINITY) ? -INFINITY : Mu + logf(den);
 }
 
 }  // namespace oscar

@@ -114,8 +114,8 @@ int oscar_store_int2(const float* k_rot, const float* v_rot, int64_t n_tokens, i
                      v_stride_block, v_stride_token, v_stride_head};
   const int kidx = clip_index(k_clip_ratio, head_dim), vidx = clip_index(v_clip_ratio, head_dim);
   const int64_t vecs = n_tokens * num_kv_heads;
-  // one warp per vector, four per CTA (one per scheduler): the kernel is latency-bound at decode sizes
-  const int64_t blocks = std::min<int64_t>((vecs + 3) / 4, (int64_t)device_info().sms * 64);
+  // one warp per (vector, K or V), four per CTA (one per scheduler): the kernel is latency-bound at decode sizes
+  const int64_t blocks = std::min<int64_t>((2 * vecs + 3) / 4, (int64_t)device_info().sms * 64);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int grid = (int)std::max<int64_t>(blocks, 1);
   if (head_dim > 128)
@@ -516,15 +516,27 @@ int run_decode_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs,
     return kDecodeNoFit;
   for (const DecodePlanned& pl : plans) {
     oscar::AttnArgs a = base;
-    a.part_o = reinterpret_cast<float*>(workspace);
+    a.part_o = reinterpret_cast<float*>(workspace);  // fp16 partials in the fp32-sized slots
     a.part_lse = a.part_o + (int64_t)pl.plan.total_items * base.hk * oscar::kTcRows * 256;
     oscar::decode_tc_kernel<T><<<dim3(pl.plan.total_items, base.hk), oscar::kTcThreads, sizeof(oscar::TcSmem), s>>>(
         a, pl.plan, tmk, tmv);
     int st = cuda_status("decode_tc_kernel");
     if (st) return st;
-    oscar::decode_combine_kernel<T><<<dim3(pl.plan.num_req, base.hk * oscar::kTcRows), 256, 0, s>>>(
-        a, pl.plan, oscar::kTcRows, 0);
-    st = cuda_status("decode_combine_kernel");
+    // the merge is a programmatic dependent of the attention grid
+    const int warps = pl.plan.num_req * base.hk * oscar::kTcRows;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)((warps + oscar::kTcCombineWarps - 1) / oscar::kTcCombineWarps));
+    cfg.blockDim = dim3(32 * oscar::kTcCombineWarps);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, oscar::tc_combine_kernel<T>, a, pl.plan) != cudaSuccess)
+      return fail(OSCAR_ERR_CUDA, "tc_combine_kernel launch failed");
+    st = cuda_status("tc_combine_kernel");
     if (st) return st;
   }
   return OSCAR_OK;

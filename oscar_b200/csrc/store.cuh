@@ -2,9 +2,9 @@
 //
 // K1 restates kernels/store_kernel.py:54-102 (oscar_store_ref, built on
 // format.py:51-88) with the clamp of backend.py:140-146 folded in.  One warp
-// owns one (token, kv-head) vector; lane L owns code bytes L and L+32
-// (dims 4L..4L+3 and 4L+128..4L+131), so loads are float4-coalesced and each
-// code byte is produced by exactly one lane.  All arithmetic is IEEE fp32 with
+// owns the K or the V half of one (token, kv-head) vector; lane L owns code
+// bytes L and L+32 (dims 4L..4L+3 and 4L+128..4L+131), so loads are
+// float4-coalesced and each code byte is produced by exactly one lane.  All arithmetic is IEEE fp32 with
 // explicit round-to-nearest intrinsics (no FMA contraction), which makes the
 // codes and fp16 scale/zero bytes bit-identical to the torch CPU reference.
 #pragma once
@@ -28,9 +28,11 @@ struct StoreGeom {
   int64_t vsb, vst, vsh;  // V cache strides in bytes
 };
 
-// k-th smallest |x| (k = clip_idx, 0-based) over the warp's vector, as the
-// bit pattern descent of a lower bound: the smallest u with #{|x| <= u} > k.
-// Non-negative floats order like their uint32 bit patterns.
+// k-th smallest |x| (k = clip_idx, 0-based) over the warp's vector: the
+// smallest u with #{|x| <= u} > k, found two bits per step (radix 4) over the
+// bit patterns (non-negative floats order like their uint32 patterns).  Step b
+// keeps the largest j in 0..3 with #{|x| <= ans + j 2^b - 1} <= k; the three
+// counts are independent, so a step costs one reduction latency.
 template <int BPL>
 OSCAR_DEVINL float kth_abs(const float (&x)[BPL][4], const bool (&act)[BPL], int k) {
   uint32_t a[BPL][4];
@@ -39,15 +41,22 @@ OSCAR_DEVINL float kth_abs(const float (&x)[BPL][4], const bool (&act)[BPL], int
 #pragma unroll
     for (int e = 0; e < 4; ++e) a[j][e] = act[j] ? (__float_as_uint(x[j][e]) & 0x7fffffffu) : 0xffffffffu;
   uint32_t ans = 0;
-  for (int b = 30; b >= 0; --b) {
-    uint32_t probe = ans + ((1u << b) - 1u);
-    int c = 0;
+#pragma unroll 1
+  for (int b = 30; b >= 0; b -= 2) {
+    const uint32_t p1 = ans + ((1u << b) - 1u), p2 = ans + ((2u << b) - 1u), p3 = ans + ((3u << b) - 1u);
+    int c1 = 0, c2 = 0, c3 = 0;
 #pragma unroll
     for (int j = 0; j < BPL; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) c += (a[j][e] <= probe) ? 1 : 0;
-    c = __reduce_add_sync(0xffffffffu, c);
-    if (c <= k) ans += (1u << b);
+      for (int e = 0; e < 4; ++e) {
+        c1 += (a[j][e] <= p1) ? 1 : 0;
+        c2 += (a[j][e] <= p2) ? 1 : 0;
+        c3 += (a[j][e] <= p3) ? 1 : 0;
+      }
+    c1 = __reduce_add_sync(0xffffffffu, c1);
+    c2 = __reduce_add_sync(0xffffffffu, c2);
+    c3 = __reduce_add_sync(0xffffffffu, c3);
+    ans += (uint32_t)((c1 <= k ? 1 : 0) + (c2 <= k ? 1 : 0) + (c3 <= k ? 1 : 0)) << b;
   }
   return __uint_as_float(ans);
 }
@@ -103,6 +112,9 @@ OSCAR_DEVINL uint32_t quantize_vec(float (&x)[BPL][4], const bool (&act)[BPL], i
   return (uint32_t)__half_as_ushort(sh) | ((uint32_t)__half_as_ushort(zh) << 16);
 }
 
+// One warp per (token, kv head, K or V): the K and V halves of a vector are
+// quantized by two warps at once (warp 2 v + 0 writes the K codes and the K
+// scale/zero bytes [0:4] of the K slot, warp 2 v + 1 the V codes and [4:8]).
 template <int BPL>
 __global__ void __launch_bounds__(128) store_int2_kernel(const float* __restrict__ k_rot,
                                                          const float* __restrict__ v_rot, int64_t n, int hk, int D,
@@ -113,7 +125,9 @@ __global__ void __launch_bounds__(128) store_int2_kernel(const float* __restrict
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int bs_log2 = (g.block_size & (g.block_size - 1)) == 0 ? __ffs(g.block_size) - 1 : -1;
-  for (int64_t vec = warp; vec < n * hk; vec += nwarps) {
+  for (int64_t task = warp; task < 2 * n * hk; task += nwarps) {
+    const int64_t vec = task >> 1;
+    const bool is_v = (task & 1) != 0;
     int64_t tok;
     int h;
     if (hk == 1) {
@@ -137,44 +151,39 @@ __global__ void __launch_bounds__(128) store_int2_kernel(const float* __restrict
       off = slot - blk * g.block_size;
     }
     if (blk >= g.num_blocks) {
-      if (lane == 0) flag_error(1u);
+      if (lane == 0 && !is_v) flag_error(1u);
       continue;
     }
-    float kx[BPL][4], vx[BPL][4];
+    const float* src = (is_v ? v_rot : k_rot) + vec * (int64_t)D;
+    float x[BPL][4];
     bool act[BPL];
 #pragma unroll
     for (int j = 0; j < BPL; ++j) {
       const int b = lane + 32 * j;
       act[j] = b < NB;
       if (act[j]) {
-        const float4 a = *reinterpret_cast<const float4*>(k_rot + vec * (int64_t)D + 4 * b);
-        const float4 c = *reinterpret_cast<const float4*>(v_rot + vec * (int64_t)D + 4 * b);
-        kx[j][0] = a.x; kx[j][1] = a.y; kx[j][2] = a.z; kx[j][3] = a.w;
-        vx[j][0] = c.x; vx[j][1] = c.y; vx[j][2] = c.z; vx[j][3] = c.w;
+        const float4 a = *reinterpret_cast<const float4*>(src + 4 * b);
+        x[j][0] = a.x; x[j][1] = a.y; x[j][2] = a.z; x[j][3] = a.w;
       } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) kx[j][e] = vx[j][e] = 0.0f;
+        for (int e = 0; e < 4; ++e) x[j][e] = 0.0f;
       }
     }
-    uint8_t kcode[BPL], vcode[BPL];
-    const uint32_t kmeta = quantize_vec<BPL>(kx, act, k_clip_idx, kcode);
-    const uint32_t vmeta = quantize_vec<BPL>(vx, act, v_clip_idx, vcode);
+    uint8_t code[BPL];
+    const uint32_t meta = quantize_vec<BPL>(x, act, is_v ? v_clip_idx : k_clip_idx, code);
     uint8_t* kslot = g.kc + blk * g.ksb + off * g.kst + (int64_t)h * g.ksh;
-    uint8_t* vslot = g.vc + blk * g.vsb + off * g.vst + (int64_t)h * g.vsh;
+    uint8_t* dst = is_v ? g.vc + blk * g.vsb + off * g.vst + (int64_t)h * g.vsh : kslot + kKIdxOff;
 #pragma unroll
     for (int j = 0; j < BPL; ++j) {
       const int b = lane + 32 * j;
-      if (act[j]) {
-        kslot[kKIdxOff + b] = kcode[j];
-        vslot[b] = vcode[j];
-      }
+      if (act[j]) dst[b] = code[j];
     }
-    if (lane < 4) {
-      // [0:2] K scale, [2:4] K zero, [4:6] V scale, [6:8] V zero (little endian)
-      const uint32_t m = (lane < 2) ? kmeta : vmeta;
-      const uint16_t bits = (uint16_t)((lane & 1) ? (m >> 16) : (m & 0xffffu));
-      kslot[2 * lane] = (uint8_t)(bits & 0xffu);
-      kslot[2 * lane + 1] = (uint8_t)(bits >> 8);
+    if (lane < 2) {
+      // K slot bytes [0:2] K scale, [2:4] K zero, [4:6] V scale, [6:8] V zero (little endian)
+      const uint16_t bits = (uint16_t)(lane ? (meta >> 16) : (meta & 0xffffu));
+      uint8_t* mb = kslot + (is_v ? 4 : 0) + 2 * lane;
+      mb[0] = (uint8_t)(bits & 0xffu);
+      mb[1] = (uint8_t)(bits >> 8);
     }
   }
 }
