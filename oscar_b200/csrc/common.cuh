@@ -17,6 +17,14 @@ __device__ unsigned int g_bounds_error;
 
 OSCAR_DEVINL void flag_error(unsigned int bit) { atomicOr(&g_bounds_error, bit); }
 
+// Programmatic dependent launch.  pdl_release lets the next kernel of the
+// stream (launched with programmatic stream serialisation) start once every
+// CTA of this grid has released; pdl_wait blocks until the previous kernel
+// of the stream has completed and its memory is visible.  Both are no-ops
+// for kernels launched without the attribute.
+OSCAR_DEVINL void pdl_release() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+OSCAR_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
 // ---------------------------------------------------------------------------
 // element types
 template <typename T> struct Elem;

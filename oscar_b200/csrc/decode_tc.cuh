@@ -275,6 +275,9 @@ __global__ void __maxnreg__(96)
   const uint32_t b_k = smem_u32(&sm.bar_k[0]), b_s = smem_u32(&sm.bar_s[0]), b_p = smem_u32(&sm.bar_p),
                  b_pv = smem_u32(&sm.bar_pv);
   const TcWait wait{&sm.abort};
+  // programmatic dependent launch: the launch and the index set-up above overlap
+  // the previous kernel (the staging write); every global read comes after this
+  pdl_wait();
 
   // ---------------- prologue.  The producer warp sets up barriers, the page
   // slice and TMEM and issues the first two INT2 stages' TMA at once;

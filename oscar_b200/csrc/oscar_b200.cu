@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/oscar_b200.h"
@@ -39,6 +40,25 @@ int cuda_status(const char* what, int launches = 1) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(OSCAR_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return OSCAR_OK;
+}
+
+// Launch with programmatic stream serialisation: the kernel may start while the
+// previous kernel of the stream finishes; it waits (pdl_wait) before reading
+// anything that kernel writes.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 struct DeviceInfo {
@@ -119,11 +139,11 @@ int oscar_store_int2(const float* k_rot, const float* v_rot, int64_t n_tokens, i
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int grid = (int)std::max<int64_t>(blocks, 1);
   if (head_dim > 128)
-    oscar::store_int2_kernel<2><<<grid, 128, 0, s>>>(k_rot, v_rot, n_tokens, num_kv_heads, head_dim, kidx, vidx, g,
-                                                      slot_mapping);
+    launch_pdl(oscar::store_int2_kernel<2>, dim3(grid), dim3(128), 0, s, k_rot, v_rot, n_tokens, num_kv_heads,
+               head_dim, kidx, vidx, g, slot_mapping);
   else
-    oscar::store_int2_kernel<1><<<grid, 128, 0, s>>>(k_rot, v_rot, n_tokens, num_kv_heads, head_dim, kidx, vidx, g,
-                                                      slot_mapping);
+    launch_pdl(oscar::store_int2_kernel<1>, dim3(grid), dim3(128), 0, s, k_rot, v_rot, n_tokens, num_kv_heads,
+               head_dim, kidx, vidx, g, slot_mapping);
   return cuda_status("store_int2_kernel");
 }
 
@@ -133,8 +153,8 @@ int oscar_staging_invalidate(const int64_t* slot_mapping, int64_t n_tokens, int6
   if (n_tokens == 0) return OSCAR_OK;
   if (!slot_mapping || !owner) return fail(OSCAR_ERR_INVALID, "staging: null pointer");
   const int grid = (int)std::min<int64_t>((n_tokens + 255) / 256, 4096);
-  oscar::staging_invalidate_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      slot_mapping, n_tokens, owner, stage_rows, block_size);
+  launch_pdl(oscar::staging_invalidate_kernel, dim3(grid), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+             slot_mapping, n_tokens, owner, stage_rows, block_size);
   return cuda_status("staging_invalidate_kernel");
 }
 
@@ -156,13 +176,12 @@ int oscar_staging_write(const float* k_rot, const float* v_rot, int64_t n_tokens
     return fail(OSCAR_ERR_INVALID, "staging: fp32 arrays must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int grid1 = (int)std::min<int64_t>((n_tokens + 255) / 256, 4096);
-  oscar::staging_winner_kernel<<<grid1, 256, 0, s>>>(slot_mapping, n_tokens, stage_rows, block_size,
-                                                      reinterpret_cast<unsigned long long*>(seat_winner), epoch);
+  launch_pdl(oscar::staging_winner_kernel, dim3(grid1), dim3(256), 0, s, slot_mapping, n_tokens, stage_rows,
+             block_size, reinterpret_cast<unsigned long long*>(seat_winner), epoch);
   const int grid2 = (int)std::min<int64_t>((n_tokens + 7) / 8, (int64_t)device_info().sms * 16);
-  oscar::staging_write_kernel<<<std::max(grid2, 1), 256, 0, s>>>(
-      k_rot, v_rot, n_tokens, num_kv_heads, head_dim, slot_mapping, qsl, seqs, num_requests, sink_eff,
-      recent_tokens, stage_k, stage_v, owner, stage_rows, block_size,
-      reinterpret_cast<const unsigned long long*>(seat_winner), epoch);
+  launch_pdl(oscar::staging_write_kernel, dim3(std::max(grid2, 1)), dim3(256), 0, s, k_rot, v_rot, n_tokens,
+             num_kv_heads, head_dim, slot_mapping, qsl, seqs, num_requests, sink_eff, recent_tokens, stage_k, stage_v,
+             owner, stage_rows, block_size, reinterpret_cast<const unsigned long long*>(seat_winner), epoch);
   return cuda_status("staging kernels", 2);
 }
 
@@ -518,24 +537,14 @@ int run_decode_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs,
     oscar::AttnArgs a = base;
     a.part_o = reinterpret_cast<float*>(workspace);  // fp16 partials in the fp32-sized slots
     a.part_lse = a.part_o + (int64_t)pl.plan.total_items * base.hk * oscar::kTcRows * 256;
-    oscar::decode_tc_kernel<T><<<dim3(pl.plan.total_items, base.hk), oscar::kTcThreads, sizeof(oscar::TcSmem), s>>>(
-        a, pl.plan, tmk, tmv);
+    launch_pdl(oscar::decode_tc_kernel<T>, dim3(pl.plan.total_items, base.hk), dim3(oscar::kTcThreads),
+               sizeof(oscar::TcSmem), s, a, pl.plan, tmk, tmv);
     int st = cuda_status("decode_tc_kernel");
     if (st) return st;
     // the merge is a programmatic dependent of the attention grid
     const int warps = pl.plan.num_req * base.hk * oscar::kTcRows;
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)((warps + oscar::kTcCombineWarps - 1) / oscar::kTcCombineWarps));
-    cfg.blockDim = dim3(32 * oscar::kTcCombineWarps);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, oscar::tc_combine_kernel<T>, a, pl.plan) != cudaSuccess)
-      return fail(OSCAR_ERR_CUDA, "tc_combine_kernel launch failed");
+    launch_pdl(oscar::tc_combine_kernel<T>, dim3((warps + oscar::kTcCombineWarps - 1) / oscar::kTcCombineWarps),
+               dim3(32 * oscar::kTcCombineWarps), 0, s, a, pl.plan);
     st = cuda_status("tc_combine_kernel");
     if (st) return st;
   }
@@ -821,11 +830,12 @@ int oscar_staging_write_noalloc(const float* k_rot, const float* v_rot, int64_t 
     return fail(OSCAR_ERR_CUDA, "staging (no-alloc): clearing the scratch failed");
   const uint32_t epoch = 1;
   const int grid1 = (int)std::min<int64_t>((n_tokens + 255) / 256, 4096);
-  oscar::staging_winner_kernel<<<grid1, 256, 0, s>>>(slot_mapping, n_tokens, stage_rows, block_size, winner, epoch);
+  launch_pdl(oscar::staging_winner_kernel, dim3(grid1), dim3(256), 0, s, slot_mapping, n_tokens, stage_rows,
+             block_size, winner, epoch);
   const int grid2 = (int)std::min<int64_t>((n_tokens + 7) / 8, (int64_t)device_info().sms * 16);
-  oscar::staging_write_kernel<<<std::max(grid2, 1), 256, 0, s>>>(
-      k_rot, v_rot, n_tokens, num_kv_heads, head_dim, slot_mapping, qsl, seqs, num_requests, sink_eff,
-      recent_tokens, stage_k, stage_v, owner, stage_rows, block_size, winner, epoch);
+  launch_pdl(oscar::staging_write_kernel, dim3(std::max(grid2, 1)), dim3(256), 0, s, k_rot, v_rot, n_tokens,
+             num_kv_heads, head_dim, slot_mapping, qsl, seqs, num_requests, sink_eff, recent_tokens, stage_k, stage_v,
+             owner, stage_rows, block_size, const_cast<const unsigned long long*>(winner), epoch);
   return cuda_status("staging kernels (no-alloc)", 2);
 }
 
@@ -848,7 +858,7 @@ int launch_rotate_d(const oscar::RotBatch& b, cudaStream_t s) {
     cfg_dev = dev;
   }
   dim3 grid((unsigned)b.tile_begin[b.n], (unsigned)(D / oscar::kRotCols));
-  oscar::rotate_rows_kernel<InT, OutT, D><<<grid, 256, smem, s>>>(b);
+  launch_pdl(oscar::rotate_rows_kernel<InT, OutT, D>, grid, dim3(256), smem, s, b);
   return cuda_status("rotate_rows_kernel");
 }
 

@@ -80,6 +80,8 @@ struct RotIn<float> {
 
 template <typename InT, typename OutT, int D>
 __global__ void __launch_bounds__(256) rotate_rows_kernel(const __grid_constant__ RotBatch b) {
+  pdl_release();
+  pdl_wait();
   extern __shared__ __align__(16) float rsm[];
   float* rblk = rsm;                 // [D][32]: R[k][c0 + j] (R^T: R[c0 + j][k])
   float* xt = rsm + D * kRotCols;    // [D][16]: x[r0 + r][k] at k * 16 + r

@@ -120,6 +120,8 @@ __global__ void __launch_bounds__(128) store_int2_kernel(const float* __restrict
                                                          const float* __restrict__ v_rot, int64_t n, int hk, int D,
                                                          int k_clip_idx, int v_clip_idx, StoreGeom g,
                                                          const int64_t* __restrict__ slots) {
+  pdl_release();
+  pdl_wait();
   const int NB = D / 4;  // code bytes per vector; BPL = code bytes per lane (1 or 2)
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -199,6 +201,8 @@ OSCAR_DEVINL int64_t staging_seat(int64_t slot, int bs, int64_t rows, int64_t* b
 
 __global__ void staging_invalidate_kernel(const int64_t* __restrict__ slots, int64_t n, int64_t* __restrict__ owner,
                                           int64_t rows, int bs) {
+  pdl_release();
+  pdl_wait();
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t slot = slots[t];
     if (slot < 0) continue;
@@ -212,6 +216,8 @@ __global__ void staging_invalidate_kernel(const int64_t* __restrict__ slots, int
 // earlier calls lose without clearing the scratch.
 __global__ void staging_winner_kernel(const int64_t* __restrict__ slots, int64_t n, int64_t rows, int bs,
                                       unsigned long long* __restrict__ winner, uint32_t epoch) {
+  pdl_release();
+  pdl_wait();
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t slot = slots[t];
     if (slot < 0) continue;
@@ -229,6 +235,8 @@ __global__ void __launch_bounds__(256) staging_write_kernel(
     int num_req, int sink_eff, int recent, float* __restrict__ stage_k, float* __restrict__ stage_v,
     int64_t* __restrict__ owner, int64_t rows, int bs, const unsigned long long* __restrict__ winner,
     uint32_t epoch) {
+  pdl_release();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
