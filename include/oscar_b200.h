@@ -110,6 +110,22 @@ int oscar_staging_write(const float* k_rot, const float* v_rot, /* [n_tokens, nu
                         uint64_t* seat_winner, uint32_t epoch,
                         void* stream);
 
+/* The write side of a decode-sized step in one launch: oscar_store_int2 and
+ * oscar_staging_write of the same tokens (same arguments), for at most 256
+ * tokens and 256 requests (OSCAR_ERR_UNSUPPORTED beyond).  No counterpart in
+ * the reference, whose forward runs do_kv_cache_update (owner invalidation,
+ * rotate/clip, store; backend.py:151-198) then _staging_write
+ * (backend.py:513-555): the invalidation is left out because every seat it
+ * clears is rewritten by that seat's last writer, and the last writer per seat
+ * is found without scratch or epoch (the call can be replayed from a graph). */
+int oscar_write_step(const float* k_rot, const float* v_rot, int64_t n_tokens, int32_t num_kv_heads, int32_t head_dim,
+                     float k_clip_ratio, float v_clip_ratio, uint8_t* k_cache, uint8_t* v_cache, int64_t num_blocks,
+                     int32_t block_size, int64_t k_stride_block, int64_t k_stride_token, int64_t k_stride_head,
+                     int64_t v_stride_block, int64_t v_stride_token, int64_t v_stride_head,
+                     const int64_t* slot_mapping, const int32_t* qsl, const int32_t* seqs, int32_t num_requests,
+                     int32_t sink_eff, int32_t recent_tokens, float* stage_k, float* stage_v, int64_t* owner,
+                     int64_t stage_rows, void* stream);
+
 /* Staging-window write for callers that cannot allocate device memory.
  * No counterpart in the reference.  Same semantics and arguments as
  * oscar_staging_write, minus seat_winner/epoch: the scratch is a static

@@ -39,6 +39,9 @@ SIGNATURES = {
     "oscar_store_int2": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _F32, _F32, _P, _P, _I64, _I32,
                                         _I64, _I64, _I64, _I64, _I64, _I64, _P, _P]),
     "oscar_staging_invalidate": (ctypes.c_int, [_P, _I64, _P, _I64, _I32, _P]),
+    "oscar_write_step": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _F32, _F32, _P, _P, _I64, _I32,
+                                        _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _I32,
+                                        _I32, _I32, _P, _P, _P, _I64, _P]),
     "oscar_staging_write": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _P, _P, _P, _I32, _I32, _I32,
                                            _P, _P, _P, _I64, _I32, _P, _U32, _P]),
     "oscar_staging_write_noalloc": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _P, _P, _P, _I32, _I32, _I32,

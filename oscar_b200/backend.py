@@ -170,11 +170,21 @@ class OscarAttentionImplMixin:
         ``query_rows`` is given, the rotated queries (q @ R_k, query dtype),
         all from one rotation launch."""
         n = slot_mapping.shape[0]
+        if invalidate and getattr(layer, "_oscar_stage_ready", False):
+            kernels.staging_invalidate(slot_mapping, layer._oscar_slot_owner, self.stage_block)
+        rotated = self._rotate_step(layer, key, value, n, query_rows)
+        kernels.oscar_store(rotated[0], rotated[1], self.key_cache, self.value_cache, slot_mapping,
+                            self._oscar.k_clip_ratio, self._oscar.v_clip_ratio)
+        self._oscar_stats["writes"] += 1
+        self._oscar_stats["kv_bytes_written"] += n * self.num_kv_heads * 160
+        return rotated
+
+    def _rotate_step(self, layer, key, value, n, query_rows=None):
+        """(k_rot, v_rot, k_lo, v_lo, q_lo) of the step's n tokens, from one
+        rotation launch (q_lo is None when query_rows is not given)."""
         hk, d = self.num_kv_heads, self.head_size
         k = key[:n].reshape(n, hk, d)
         v = value[:n].reshape(n, hk, d)
-        if invalidate and getattr(layer, "_oscar_stage_ready", False):
-            kernels.staging_invalidate(slot_mapping, layer._oscar_slot_owner, self.stage_block)
         rk, rv = self._layer_rots(layer, k.device)
         k_rot, v_rot = (torch.empty(n, hk, d, dtype=torch.float32, device=k.device) for _ in range(2))
         k_lo = torch.empty((n, hk, d), dtype=k.dtype, device=k.device)
@@ -189,10 +199,6 @@ class OscarAttentionImplMixin:
         else:
             kernels.rotate_rows(k, rk, out=k_lo, out_f32=k_rot)
             kernels.rotate_rows(v, rv, out=v_lo, out_f32=v_rot)
-        kernels.oscar_store(k_rot, v_rot, self.key_cache, self.value_cache, slot_mapping,
-                            self._oscar.k_clip_ratio, self._oscar.v_clip_ratio)
-        self._oscar_stats["writes"] += 1
-        self._oscar_stats["kv_bytes_written"] += n * hk * 160
         return k_rot, v_rot, k_lo, v_lo, q_lo
 
     def do_kv_cache_update(self, layer, key, value, kv_cache, slot_mapping) -> None:
@@ -274,11 +280,26 @@ class OscarAttentionImplMixin:
             n = attn_metadata.num_actual_tokens
             slots = attn_metadata.slot_mapping[:n].to(device=key.device, dtype=torch.int64)
             rotated = None
+            qsl, seqs = metadata_batch_lists(attn_metadata)
+            fused = self._oscar.window_enabled and 0 < n <= kernels.WRITE_STEP_MAX_TOKENS and \
+                len(qsl) - 1 <= kernels.WRITE_STEP_MAX_REQUESTS and slots.shape[0] == n
             if slots.shape[0] > 0:
                 q_rows = self._whole_batch_rotated_queries(query, key, attn_metadata)
-                rotated = self._store(layer, key, value, slots, invalidate=not self._oscar.window_enabled,
-                                      query_rows=q_rows)
-            if self._oscar.window_enabled:
+                if fused:
+                    # store + staging write of a decode-sized step in one launch
+                    self._ensure_staging(layer, kv_cache)
+                    rotated = self._rotate_step(layer, key, value, n, q_rows)
+                    qsl_d, seqs_d = _device_batch(attn_metadata, qsl, seqs, key.device)
+                    kernels.write_step(rotated[0], rotated[1], self.key_cache, self.value_cache, slots,
+                                       self._oscar.k_clip_ratio, self._oscar.v_clip_ratio, qsl_d, seqs_d,
+                                       self.sink_eff, self._oscar.recent_tokens, layer._oscar_stage_k,
+                                       layer._oscar_stage_v, layer._oscar_slot_owner)
+                    self._oscar_stats["writes"] += 1
+                    self._oscar_stats["kv_bytes_written"] += n * self.num_kv_heads * 160
+                else:
+                    rotated = self._store(layer, key, value, slots, invalidate=not self._oscar.window_enabled,
+                                          query_rows=q_rows)
+            if self._oscar.window_enabled and not (fused and slots.shape[0] > 0):
                 self._ensure_staging(layer, kv_cache)
                 self._staging_write(layer, key, value, attn_metadata, rotated=None if rotated is None else rotated[:2])
             return self._streaming_attention(layer, query, key, value, kv_cache, attn_metadata, output,

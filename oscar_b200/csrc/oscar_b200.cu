@@ -147,6 +147,50 @@ int oscar_store_int2(const float* k_rot, const float* v_rot, int64_t n_tokens, i
   return cuda_status("store_int2_kernel");
 }
 
+int oscar_write_step(const float* k_rot, const float* v_rot, int64_t n_tokens, int32_t num_kv_heads, int32_t head_dim,
+                     float k_clip_ratio, float v_clip_ratio, uint8_t* k_cache, uint8_t* v_cache, int64_t num_blocks,
+                     int32_t block_size, int64_t k_stride_block, int64_t k_stride_token, int64_t k_stride_head,
+                     int64_t v_stride_block, int64_t v_stride_token, int64_t v_stride_head,
+                     const int64_t* slot_mapping, const int32_t* qsl, const int32_t* seqs, int32_t num_requests,
+                     int32_t sink_eff, int32_t recent_tokens, float* stage_k, float* stage_v, int64_t* owner,
+                     int64_t stage_rows, void* stream) {
+  if (n_tokens < 0 || num_kv_heads < 1 || block_size < 1 || num_blocks < 0 || stage_rows < 1 || num_requests < 0)
+    return fail(OSCAR_ERR_INVALID, "write_step: invalid geometry");
+  if (n_tokens > oscar::kFusedMaxTokens || num_requests > oscar::kFusedMaxReqs || stage_rows * block_size >= INT32_MAX)
+    return fail(OSCAR_ERR_UNSUPPORTED, "write_step: at most %d tokens and %d requests (use oscar_store_int2 + "
+                                       "oscar_staging_write)", oscar::kFusedMaxTokens, oscar::kFusedMaxReqs);
+  if (head_dim % 4 != 0 || head_dim / 4 > 64 || head_dim < 4)
+    return fail(OSCAR_ERR_INVALID, "store: D=%d must be a multiple of 4 and at most 256", head_dim);
+  if (!(k_clip_ratio >= 0.0f && k_clip_ratio <= 1.0f && v_clip_ratio >= 0.0f && v_clip_ratio <= 1.0f))
+    return fail(OSCAR_ERR_INVALID, "store: clip ratios must be in [0, 1]");
+  if (k_stride_head < 32 + head_dim / 4 || v_stride_head < head_dim / 4)
+    return fail(OSCAR_ERR_INVALID, "store: slot of %lld/%lld bytes cannot hold the K (%d B) / V (%d B) layout",
+                (long long)k_stride_head, (long long)v_stride_head, 32 + head_dim / 4, head_dim / 4);
+  if (n_tokens == 0) return OSCAR_OK;
+  if (!k_rot || !v_rot || !k_cache || !v_cache || !slot_mapping || !stage_k || !stage_v || !owner ||
+      (num_requests > 0 && (!qsl || !seqs)))
+    return fail(OSCAR_ERR_INVALID, "write_step: null pointer");
+  if ((reinterpret_cast<uintptr_t>(k_rot) | reinterpret_cast<uintptr_t>(v_rot) | reinterpret_cast<uintptr_t>(stage_k) |
+       reinterpret_cast<uintptr_t>(stage_v)) & 15)
+    return fail(OSCAR_ERR_INVALID, "write_step: fp32 arrays must be 16-byte aligned");
+  oscar::StoreGeom g{k_cache, v_cache, num_blocks, block_size, k_stride_block, k_stride_token, k_stride_head,
+                     v_stride_block, v_stride_token, v_stride_head};
+  oscar::StageArgs st{qsl, seqs, num_requests, sink_eff, recent_tokens, stage_k, stage_v, owner, stage_rows,
+                      block_size};
+  const int kidx = clip_index(k_clip_ratio, head_dim), vidx = clip_index(v_clip_ratio, head_dim);
+  const int64_t tasks = 2 * n_tokens * num_kv_heads;
+  // one warp per (token, head, K or V) task, four per CTA
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((tasks + 3) / 4, (int64_t)device_info().sms * 64));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (head_dim > 128)
+    launch_pdl(oscar::write_step_kernel<2>, dim3(grid), dim3(128), 0, s, k_rot, v_rot, n_tokens, num_kv_heads,
+               head_dim, kidx, vidx, g, slot_mapping, st);
+  else
+    launch_pdl(oscar::write_step_kernel<1>, dim3(grid), dim3(128), 0, s, k_rot, v_rot, n_tokens, num_kv_heads,
+               head_dim, kidx, vidx, g, slot_mapping, st);
+  return cuda_status("write_step_kernel");
+}
+
 int oscar_staging_invalidate(const int64_t* slot_mapping, int64_t n_tokens, int64_t* owner, int64_t stage_rows,
                              int32_t block_size, void* stream) {
   if (n_tokens < 0 || stage_rows < 1 || block_size < 1) return fail(OSCAR_ERR_INVALID, "staging: invalid geometry");

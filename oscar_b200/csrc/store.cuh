@@ -115,19 +115,15 @@ OSCAR_DEVINL uint32_t quantize_vec(float (&x)[BPL][4], const bool (&act)[BPL], i
 // One warp per (token, kv head, K or V): the K and V halves of a vector are
 // quantized by two warps at once (warp 2 v + 0 writes the K codes and the K
 // scale/zero bytes [0:4] of the K slot, warp 2 v + 1 the V codes and [4:8]).
+// Warps warp0, warp0 + nwarps, ... of the task list.
 template <int BPL>
-__global__ void __launch_bounds__(128) store_int2_kernel(const float* __restrict__ k_rot,
-                                                         const float* __restrict__ v_rot, int64_t n, int hk, int D,
-                                                         int k_clip_idx, int v_clip_idx, StoreGeom g,
-                                                         const int64_t* __restrict__ slots) {
-  pdl_release();
-  pdl_wait();
+OSCAR_DEVINL void store_tasks(int64_t warp0, int64_t nwarps, const float* __restrict__ k_rot,
+                              const float* __restrict__ v_rot, int64_t n, int hk, int D, int k_clip_idx,
+                              int v_clip_idx, const StoreGeom& g, const int64_t* __restrict__ slots) {
   const int NB = D / 4;  // code bytes per vector; BPL = code bytes per lane (1 or 2)
   const int lane = threadIdx.x & 31;
-  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int bs_log2 = (g.block_size & (g.block_size - 1)) == 0 ? __ffs(g.block_size) - 1 : -1;
-  for (int64_t task = warp; task < 2 * n * hk; task += nwarps) {
+  for (int64_t task = warp0; task < 2 * n * hk; task += nwarps) {
     const int64_t vec = task >> 1;
     const bool is_v = (task & 1) != 0;
     int64_t tok;
@@ -188,6 +184,17 @@ __global__ void __launch_bounds__(128) store_int2_kernel(const float* __restrict
       mb[1] = (uint8_t)(bits >> 8);
     }
   }
+}
+
+template <int BPL>
+__global__ void __launch_bounds__(128) store_int2_kernel(const float* __restrict__ k_rot,
+                                                         const float* __restrict__ v_rot, int64_t n, int hk, int D,
+                                                         int k_clip_idx, int v_clip_idx, StoreGeom g,
+                                                         const int64_t* __restrict__ slots) {
+  pdl_release();
+  pdl_wait();
+  store_tasks<BPL>(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5, ((int64_t)gridDim.x * blockDim.x) >> 5,
+                   k_rot, v_rot, n, hk, D, k_clip_idx, v_clip_idx, g, slots);
 }
 
 // ---------------------------------------------------------------------------
@@ -271,6 +278,96 @@ __global__ void __launch_bounds__(256) staging_write_kernel(
       vd[i] = vs[i];
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// The write side of a decode-sized step in one launch: the INT2 store and the
+// staging write (backend.py:513-555) of n <= kFusedMaxTokens tokens.  Every
+// CTA loads the step's staging seats into shared memory; the warp that
+// quantizes the K (or V) half of a (token, head) vector also stages that
+// half: it is the seat's last writer when no later token of the step maps to
+// the same seat (checked by the 32 lanes at once), the K warp of head 0 writes
+// the owner tag, and a kept token's fp32 row half is copied into the arena.
+// No scratch and no epoch are needed, so the launch can be replayed from a
+// graph.  The owner invalidation that precedes the store in
+// do_kv_cache_update (backend.py:170-176) is left out: every seat it clears
+// is rewritten by that seat's last writer here.
+constexpr int kFusedMaxTokens = 256;
+constexpr int kFusedMaxReqs = 256;
+
+struct StageArgs {
+  const int32_t* qsl;
+  const int32_t* seqs;
+  int num_req, sink_eff, recent;
+  float* stage_k;
+  float* stage_v;
+  int64_t* owner;
+  int64_t rows;
+  int bs;
+};
+
+template <int BPL>
+__global__ void __launch_bounds__(128) write_step_kernel(const float* __restrict__ k_rot,
+                                                         const float* __restrict__ v_rot, int64_t n, int hk, int D,
+                                                         int k_clip_idx, int v_clip_idx, StoreGeom g,
+                                                         const int64_t* __restrict__ slots, StageArgs st) {
+  pdl_release();
+  pdl_wait();
+  __shared__ int s_seat[kFusedMaxTokens];  // -1: slot < 0
+  __shared__ int s_qsl[kFusedMaxReqs + 1];
+  __shared__ int s_seq[kFusedMaxReqs];
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int nt = (int)n;
+  for (int t = tid; t < nt; t += blockDim.x) {
+    const int64_t slot = slots[t];
+    int64_t blk;
+    s_seat[t] = slot < 0 ? -1 : (int)staging_seat(slot, st.bs, st.rows, &blk);
+  }
+  for (int r = tid; r <= st.num_req; r += blockDim.x) s_qsl[r] = st.qsl[r];
+  for (int r = tid; r < st.num_req; r += blockDim.x) s_seq[r] = st.seqs[r];
+  __syncthreads();
+
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t task = warp; task < 2 * n * hk; task += nwarps) {
+    const int64_t vec = task >> 1;
+    const bool is_v = (task & 1) != 0;
+    const int tok = (int)(vec / hk), h = (int)(vec - (int64_t)tok * hk);
+    const int seat = s_seat[tok];
+    if (seat < 0) continue;
+    // staging: the seat's last writer among the step's tokens (stable sort + last of run)
+    bool later = false;
+    for (int u0 = tok + 1; u0 < nt; u0 += 32) {
+      const int u = u0 + lane;
+      later = later || (u < nt && s_seat[u] == seat);
+    }
+    if (!__any_sync(0xffffffffu, later)) {
+      int lo = 0, hi = st.num_req;  // the last r with qsl[r] <= tok
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (s_qsl[mid] <= tok) lo = mid; else hi = mid;
+      }
+      bool keep = false;
+      if (st.num_req > 0 && s_qsl[lo] <= tok && tok < s_qsl[lo + 1]) {
+        const int64_t seq = s_seq[lo];
+        const int64_t pos = seq - s_qsl[lo + 1] + tok;
+        keep = (pos >= seq - st.recent) || (pos < st.sink_eff);
+      }
+      if (!is_v && h == 0 && lane == 0) st.owner[seat] = keep ? slots[tok] / st.bs : -1;
+      if (keep) {
+        const float4* src = reinterpret_cast<const float4*>((is_v ? v_rot : k_rot) + vec * (int64_t)D);
+        float4* dst = reinterpret_cast<float4*>((is_v ? st.stage_v : st.stage_k) + ((int64_t)seat * hk + h) * D);
+        float4 x[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) x[j] = (lane + 32 * j < D / 4) ? src[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          if (lane + 32 * j < D / 4) dst[lane + 32 * j] = x[j];
+      }
+    }
+  }
+  // the INT2 store of the same vectors (after the staging reads of this warp's rows)
+  store_tasks<BPL>(warp, nwarps, k_rot, v_rot, n, hk, D, k_clip_idx, v_clip_idx, g, slots);
 }
 
 }  // namespace oscar

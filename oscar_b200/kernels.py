@@ -131,6 +131,46 @@ def staging_write(k_rot: torch.Tensor, v_rot: torch.Tensor, slot_mapping: torch.
         rows, bs, seat_winner.data_ptr(), int(epoch) & 0xFFFFFFFF, _stream(dev)))
 
 
+WRITE_STEP_MAX_TOKENS = 256
+WRITE_STEP_MAX_REQUESTS = 256
+
+
+def write_step(k_rot: torch.Tensor, v_rot: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+               slot_mapping: torch.Tensor, k_clip_ratio: float, v_clip_ratio: float, qsl: torch.Tensor,
+               seqs: torch.Tensor, sink_eff: int, recent_tokens: int, stage_k: torch.Tensor, stage_v: torch.Tensor,
+               owner: torch.Tensor) -> None:
+    """oscar_store + staging_write of the same tokens in one launch (at most
+    WRITE_STEP_MAX_TOKENS tokens and WRITE_STEP_MAX_REQUESTS requests): the
+    write side of a decode step with the staging window on.  Needs no seat
+    scratch and no epoch, so it can be captured in a CUDA graph."""
+    dev = _require_cuda(k_rot, v_rot, k_cache, v_cache, slot_mapping, qsl, seqs, stage_k, stage_v, owner)
+    if k_rot.shape != v_rot.shape or k_rot.ndim != 3:
+        raise ValueError("k_rot/v_rot must be [N, H, D] with equal shapes")
+    n, h, d = k_rot.shape
+    check_d(d)
+    k8, v8 = _byte_view(k_cache), _byte_view(v_cache)
+    if k8.shape[:3] != v8.shape[:3] or k8.shape[2] != h:
+        raise ValueError("cache geometry does not match [N, H, D] input")
+    rows, bs = owner.shape
+    if stage_k.shape != (rows, bs, h, d) or stage_v.shape != stage_k.shape or bs != k8.shape[1]:
+        raise ValueError("Invalid streaming staging geometry")
+    for t in (stage_k, stage_v, owner):
+        if not t.is_contiguous():
+            raise ValueError("Streaming staging tensors must be contiguous")
+    k_rot = k_rot.to(torch.float32).contiguous()
+    v_rot = v_rot.to(torch.float32).contiguous()
+    slots = slot_mapping.to(device=dev, dtype=torch.int64).contiguous()
+    qsl = qsl.to(device=dev, dtype=torch.int32).contiguous()
+    seqs = seqs.to(device=dev, dtype=torch.int32).contiguous()
+    if slots.numel() < n:
+        raise ValueError("slot_mapping shorter than the token count")
+    check(_native.lib().oscar_write_step(
+        k_rot.data_ptr(), v_rot.data_ptr(), n, h, d, _clip_ok(k_clip_ratio), _clip_ok(v_clip_ratio),
+        k8.data_ptr(), v8.data_ptr(), k8.shape[0], k8.shape[1], *k8.stride()[:3], *v8.stride()[:3],
+        slots.data_ptr(), qsl.data_ptr(), seqs.data_ptr(), seqs.numel(), int(sink_eff), int(recent_tokens),
+        stage_k.data_ptr(), stage_v.data_ptr(), owner.data_ptr(), rows, _stream(dev)))
+
+
 def staging_write_noalloc(k_rot: torch.Tensor, v_rot: torch.Tensor, slot_mapping: torch.Tensor, qsl: torch.Tensor,
                           seqs: torch.Tensor, sink_eff: int, recent_tokens: int, stage_k: torch.Tensor,
                           stage_v: torch.Tensor, owner: torch.Tensor) -> None:
