@@ -61,12 +61,18 @@
 namespace oscar {
 
 constexpr int kTcStage = 128;
-constexpr int kTcThreads = 544;  // 16 dequant/softmax warps + the producer warp
-constexpr int kTcCompute = 512;
+constexpr int kTcDeqWarps = 16;  // dequant warps: K / V halves x TMEM lane quarters
+constexpr int kTcSmWarps = 8;    // softmax warps: one per (TMEM lane quarter, 16-row half of the query rows)
+constexpr int kTcQuarters = 4;   // TMEM lane quarters (a warp reaches lanes 32 (warp % 4) .. + 31)
+constexpr int kTcProdWarp = kTcDeqWarps + kTcSmWarps;  // TMA producer and MMA issuer
+constexpr int kTcThreads = 32 * (kTcProdWarp + 1);     // 800
+constexpr int kTcCompute = 32 * kTcDeqWarps;
 constexpr int kTcRows = 32;   // N of both MMAs: query rows (GQA group x MTP tokens)
 constexpr int kTcK = 272;     // QK reduction: 256 dims + the bias k-step
-constexpr int kTcCols = 512;  // TMEM columns: A_K[0] [0,136) | S[0] [160,192) | S[1] [192,224) | O [224,288) | A_K[1] [288,424)
-constexpr int kTcColA0 = 0, kTcColA1 = 288, kTcColS = 160, kTcColO = 224;
+// TMEM columns: A_K[0] [0,136) | ones [136,144) | S[0] [160,192) | S[1] [192,224) | O [224,288) |
+// A_K[1] [288,424) | row sums L [448,480)
+constexpr int kTcCols = 512;
+constexpr int kTcColA0 = 0, kTcColOnes = 136, kTcColA1 = 288, kTcColS = 160, kTcColO = 224, kTcColL = 448;
 constexpr int kTcMaxStages = 64;  // INT2 stages per split (staged bitmask capacity)
 constexpr int kTcMaxWords = kTcMaxStages * kTcStage / 32;
 constexpr int kTcMaxPages = kTcMaxStages * kTcStage / 8 + 2;
@@ -91,9 +97,11 @@ struct TcSmem {
   int64_t srow[kTcStage];       // first staged stage: fp32 row offset per token slot (-1: none)
   int spos[kTcStage];           // first staged stage: position per token slot
   int lim[kTcRows];             // cache-only chunks: row r sees positions < lim[r]
-  alignas(16) int red[2][16][8];  // slow-path row maxima, double-buffered
-  float lsum[16][8];
-  unsigned long long bar_full[2], bar_empty[2], bar_k[2], bar_s[2], bar_p, bar_pv;  // k, s per TMEM buffer
+  alignas(16) int red[kTcQuarters][kTcRows];    // slow-path row maxima of the softmax warps ([quarter][row])
+  alignas(16) float mrow[kTcQuarters][kTcRows];  // running row maxima (log2 units), a copy per softmax warp
+  // per buffer (a barrier that could complete twice before its waiter looks
+  // would be read as not complete by a parity wait)
+  unsigned long long bar_full[2], bar_empty[2], bar_k[2], bar_s[2], bar_v[2], bar_p[2], bar_pv[2];
   uint32_t tmem;
   int abort;
   int n_staged;
@@ -244,8 +252,106 @@ struct TcWait {
   }
 };
 
+// staged index j of this CTA's groups -> fp32 row offset of its seat (and its
+// position): the last group whose prefix count is <= j holds it
+OSCAR_DEVINL int64_t tc_staged_row(const TcSmem& sm, const AttnArgs& a, int j, int ngroups, int sp, int nsplit,
+                                   int req, int bs_log2, int h, int* pos_out) {
+  int lo_w = 0, hi_w = ngroups - 1;
+  while (lo_w < hi_w) {
+    const int mid = (lo_w + hi_w + 1) >> 1;
+    if (sm.gpref[mid] <= j) lo_w = mid; else hi_w = mid - 1;
+  }
+  const int bit = (int)__fns(sm.gmask[lo_w], 0u, j - sm.gpref[lo_w] + 1);
+  const int pos = (sp + lo_w * nsplit) * 32 + bit;
+  const int blk = a.bt[(int64_t)req * a.bt_stride + (pos >> bs_log2)];
+  const int64_t seat = (int64_t)(blk % (int)a.stage_rows) * a.bs + (pos & (a.bs - 1));
+  *pos_out = pos;
+  return (seat * a.hk + h) * 256;
+}
+
+// staged K rows of a warp's 32 tokens (one per lane: row_off, live) into its
+// TMEM lane quarter at t_a (64 columns: 128 dims as fp16/bf16 pairs).
+// tcgen05.st.16x256b: thread i writes lanes i / 4 and 8 + i / 4 of a 16-lane
+// half, columns 2 (i % 4), + 1 of each 16-dim group: (dims 4m, 4m+2), (4m+1,
+// 4m+3).  src points at dims 4 (lane % 4) of the thread's 128-dim half; a load
+// instruction covers 8 tokens x 64 contiguous bytes; dead tokens get zeros.
 template <typename T>
-__global__ void __maxnreg__(96)
+OSCAR_DEVINL void tc_staged_k(uint32_t t_a, const float* src, int64_t row_off, bool live, int lane) {
+#pragma unroll 1
+  for (int hb = 0; hb < 2; ++hb) {
+    const int la = 16 * hb + (lane >> 2), lb = la + 8;
+    const int64_t ra = __shfl_sync(0xffffffffu, row_off, la), rb = __shfl_sync(0xffffffffu, row_off, lb);
+    const bool va = __shfl_sync(0xffffffffu, (int)live, la) != 0;
+    const bool vb = __shfl_sync(0xffffffffu, (int)live, lb) != 0;
+    if (!__any_sync(0xffffffffu, vb)) {
+      // lanes 8..15 of the half are dead: one pass of 8 loads
+      float4 xs[8];
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        xs[g] = va ? __ldg(reinterpret_cast<const float4*>(src + ra + 16 * g)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int cb = 0; cb < 2; ++cb) {
+        uint32_t r[16];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const float4 x = xs[4 * cb + g];
+          r[4 * g] = pack2<T>(chain<T>(x.x), chain<T>(x.z));
+          r[4 * g + 1] = pack2<T>(chain<T>(x.y), chain<T>(x.w));
+          r[4 * g + 2] = 0u;
+          r[4 * g + 3] = 0u;
+        }
+        tc::tmem_st16x256_x4(t_a + ((uint32_t)(16 * hb) << 16) + 32 * cb, r);
+      }
+    } else {
+#pragma unroll 1
+      for (int cb = 0; cb < 2; ++cb) {
+        float4 xs[4], ys[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int off = 16 * (4 * cb + g);
+          xs[g] = va ? __ldg(reinterpret_cast<const float4*>(src + ra + off)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          ys[g] = vb ? __ldg(reinterpret_cast<const float4*>(src + rb + off)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        uint32_t r[16];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          r[4 * g] = pack2<T>(chain<T>(xs[g].x), chain<T>(xs[g].z));
+          r[4 * g + 1] = pack2<T>(chain<T>(xs[g].y), chain<T>(xs[g].w));
+          r[4 * g + 2] = pack2<T>(chain<T>(ys[g].x), chain<T>(ys[g].z));
+          r[4 * g + 3] = pack2<T>(chain<T>(ys[g].y), chain<T>(ys[g].w));
+        }
+        tc::tmem_st16x256_x4(t_a + ((uint32_t)(16 * hb) << 16) + 32 * cb, r);
+      }
+    }
+  }
+}
+
+// staged V rows of a warp's 32 tokens into V^T (fp16).  vt_q points at the
+// warp's first token group, + 4 lane; the V^T word of (token, dims 4m, 4m+2)
+// sits at row group 2g, (4m+1, 4m+3) at 2g+1, so the 8 tokens x 4 words of an
+// instruction are 128 contiguous bytes.
+template <typename T>
+OSCAR_DEVINL void tc_staged_v(uint8_t* vt_q, const float* src, int64_t row_off, bool live, int lane) {
+#pragma unroll 1
+  for (int o = 0; o < 4; ++o) {
+    const int lt = 8 * o + (lane >> 2);
+    const int64_t rt = __shfl_sync(0xffffffffu, row_off, lt);
+    const bool vt = __shfl_sync(0xffffffffu, (int)live, lt) != 0;
+    float4 xs[8];
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+      xs[g] = vt ? __ldg(reinterpret_cast<const float4*>(src + rt + 16 * g)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      uint32_t* dst = reinterpret_cast<uint32_t*>(vt_q + o * 128 + (2 * g) * kTcVtSbo);
+      dst[0] = pack2<__half>(chain_f16<T>(xs[g].x), chain_f16<T>(xs[g].z));
+      dst[kTcVtSbo / 4] = pack2<__half>(chain_f16<T>(xs[g].y), chain_f16<T>(xs[g].w));
+    }
+  }
+}
+
+template <typename T>
+__global__ void __maxnreg__(72)
     decode_tc_kernel(const AttnArgs a, const __grid_constant__ AttnPlan p, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv) {
   constexpr int D = 256;
@@ -272,8 +378,8 @@ __global__ void __maxnreg__(96)
   constexpr int kWarps = kTcCompute / 32;
 
   const uint32_t b_full = smem_u32(&sm.bar_full[0]), b_empty = smem_u32(&sm.bar_empty[0]);
-  const uint32_t b_k = smem_u32(&sm.bar_k[0]), b_s = smem_u32(&sm.bar_s[0]), b_p = smem_u32(&sm.bar_p),
-                 b_pv = smem_u32(&sm.bar_pv);
+  const uint32_t b_k = smem_u32(&sm.bar_k[0]), b_s = smem_u32(&sm.bar_s[0]), b_v = smem_u32(&sm.bar_v[0]),
+                 b_p = smem_u32(&sm.bar_p[0]), b_pv = smem_u32(&sm.bar_pv[0]);
   const TcWait wait{&sm.abort};
   // programmatic dependent launch: the launch and the index set-up above overlap
   // the previous kernel (the staging write); every global read comes after this
@@ -284,19 +390,18 @@ __global__ void __maxnreg__(96)
   // meanwhile the dequant warps load Q, scan this CTA's staged groups and
   // locate the rows of its first staged stage.  Staged stages run first, so
   // their fp32 loads overlap the TMA of the first INT2 stages.
-  if (warp == kWarps) {
+  if (warp == kTcProdWarp) {
     if (lane == 0) {
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         tc::mbar_init(b_full + 8 * i, 1);
-        tc::mbar_init(b_empty + 8 * i, kWarps);
+        tc::mbar_init(b_empty + 8 * i, kWarps);           // every dequant warp read the slot
+        tc::mbar_init(b_k + 8 * i, kWarps / 2 + kTcSmWarps);  // K warps wrote A_K, softmax warps freed S
+        tc::mbar_init(b_s + 8 * i, 1);
+        tc::mbar_init(b_v + 8 * i, kWarps / 2);            // V warps wrote V^T
+        tc::mbar_init(b_p + 8 * i, kTcSmWarps);            // softmax warps wrote P^T
+        tc::mbar_init(b_pv + 8 * i, 1);
       }
-      tc::mbar_init(b_k, kWarps);
-      tc::mbar_init(b_k + 8, kWarps);
-      tc::mbar_init(b_s, 1);
-      tc::mbar_init(b_s + 8, 1);
-      tc::mbar_init(b_p, kWarps);
-      tc::mbar_init(b_pv, 1);
       sm.abort = 0;
       tc::mbar_fence_init();
     }
@@ -315,6 +420,13 @@ __global__ void __maxnreg__(96)
       for (int s = 0; s < min(2, n_int); ++s) tc_issue_stage(sm, a, s, lo, hi, bs_log2, page0, h, &tmk, &tmv, b_full);
     }
     __syncwarp();
+  } else if (warp >= kTcDeqWarps) {
+    // softmax warps: row maxima start at -inf; P^T starts zeroed, so the rows
+    // >= R that the softmax never writes hold zeros
+    const int st_tid = tid - kTcCompute;
+    if (st_tid < kTcQuarters * kTcRows) (&sm.mrow[0][0])[st_tid] = -INFINITY;
+    for (int i = st_tid; i < (int)(sizeof(sm.pt) / 16); i += 32 * kTcSmWarps)
+      reinterpret_cast<uint4*>(&sm.pt[0][0])[i] = make_uint4(0u, 0u, 0u, 0u);
   } else {
     if (tid < kTcRows) sm.lim[tid] = tid < R ? seq - qlen + tid / G + 1 : INT_MIN;
     // Q rows n < R, 16-dim word j: k-group 2j holds dims 16j + {0,2,1,3,4,6,5,7}, 2j+1 dims
@@ -446,82 +558,94 @@ __global__ void __maxnreg__(96)
   const int n_sst = (n_staged + kTcStage - 1) / kTcStage;  // staged stages, run first
   const int nst = n_sst + n_int;
 
-  if (warp == kWarps) {
+  if (warp == kTcProdWarp) {
     // ============================ producer + MMA issuer
-    // order: QK(0); then per stage st: QK(st + 1), PV(st) -- the dequant warps
-    // write stage st + 1's operands before stage st's probabilities.  The K and
-    // S barriers exist per TMEM buffer: with two stages in flight a single
-    // barrier could complete twice before its waiter looks, and a parity wait
-    // cannot tell that apart from no completion.
-    // The whole warp runs the schedule and waits (warp-uniform control flow
-    // keeps the MMA operands in uniform registers); one elected lane issues
-    // each batch of MMAs with its commit, and each stage's TMA.
-    {
-      constexpr uint32_t idesc_qk = tc::instr_desc(std::is_same<T, __nv_bfloat16>::value ? 1u : 0u, 0, 0, 128, kTcRows);
-      constexpr uint32_t idesc_pv = tc::instr_desc(0u, 1, 1, 128, kTcRows);
-      // descriptors of k-step 0; k-step j starts 256 * j bytes later (+16 * j in the start field);
-      // buffer 1 of V^T / P^T sits sizeof(vt[0]) / sizeof(pt[0]) bytes after buffer 0
-      const uint64_t dq0 = tc::smem_desc(smem_u32(sm.qb), 128, kTcQSbo);
-      const uint64_t dv0 = tc::smem_desc(smem_u32(sm.vt[0]), 128, kTcVtSbo);
-      const uint64_t dp0 = tc::smem_desc(smem_u32(sm.pt[0]), 128, kTcVtSbo);
-      for (int qs = 0, ps = 0; ps < nst; ) {
-        if (qs < nst && qs <= ps + 1) {
-          // QK of stage qs into S[qs & 1] from A_K[qs & 1]
-          wait(b_k + 8 * (qs & 1), (qs >> 1) & 1);
-          tc::tc_fence_after();
-          const uint32_t d_s = tmem + kTcColS + 32 * (qs & 1), a_k = tmem + ((qs & 1) ? kTcColA1 : kTcColA0);
-          if (tc::elect_one()) {
+    // an event loop over three independent queues, none of which blocks the
+    // others: QK(qs) once A_K[qs & 1] is written and S[qs & 1] is free; PV(ps)
+    // once V^T and P^T of stage ps are written; the TMA of INT2 stage rf once
+    // its ring slot is empty.  (Each barrier's next phase needs this warp's
+    // own next issue, so a test of the current parity is never ambiguous.)
+    // The whole warp runs the loop (lane 0's test results are broadcast, so
+    // control flow stays warp-uniform); one elected lane issues.
+    constexpr uint32_t idesc_qk = tc::instr_desc(std::is_same<T, __nv_bfloat16>::value ? 1u : 0u, 0, 0, 128, kTcRows);
+    constexpr uint32_t idesc_pv = tc::instr_desc(0u, 1, 1, 128, kTcRows);
+    constexpr uint32_t idesc_l = tc::instr_desc(0u, 0, 1, 128, kTcRows);  // ones (TMEM) x P^T: row sums
+    // descriptors of k-step 0; k-step j starts 256 * j bytes later (+16 * j in the start field);
+    // buffer 1 of V^T / P^T sits sizeof(vt[0]) / sizeof(pt[0]) bytes after buffer 0
+    const uint64_t dq0 = tc::smem_desc(smem_u32(sm.qb), 128, kTcQSbo);
+    const uint64_t dv0 = tc::smem_desc(smem_u32(sm.vt[0]), 128, kTcVtSbo);
+    const uint64_t dp0 = tc::smem_desc(smem_u32(sm.pt[0]), 128, kTcVtSbo);
+    uint32_t idle = 0;
+    for (int qs = 0, ps = 0, rf = 2; ps < nst;) {
+      bool prog = false;
+      if (ps < qs && __shfl_sync(0xffffffffu, (int)(tc::mbar_test(b_v + 8 * (ps & 1), (ps >> 1) & 1) &&
+                                                  tc::mbar_test(b_p + 8 * (ps & 1), (ps >> 1) & 1)), 0)) {
+        // PV of stage ps from V^T[ps & 1], P^T[ps & 1]
+        tc::tc_fence_after();
+        const uint64_t dva = dv0 + (uint64_t)((ps & 1) * (sizeof(sm.vt[0]) >> 4));
+        const uint64_t dvb = dva + (16 * kTcVtSbo >> 4);
+        const uint64_t dpa = dp0 + (uint64_t)((ps & 1) * (sizeof(sm.pt[0]) >> 4));
+        const uint32_t d_o = tmem + kTcColO;
+        const uint32_t acc0 = ps > 0 ? 1u : 0u;
+        if (tc::elect_one()) {
 #pragma unroll
-            for (int j = 0; j < kTcK / 16; ++j) tc::mma_ts(d_s, a_k + 8 * j, dq0 + 16 * j, idesc_qk, j > 0 ? 1u : 0u);
-            tc::mma_commit(b_s + 8 * (qs & 1));
+          for (int j = 0; j < kTcStage / 16; ++j) {
+            tc::mma_ss(d_o, dva + 16 * j, dpa + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
+            tc::mma_ss(d_o + 32, dvb + 16 * j, dpa + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
+            // the row sums of P accumulate beside O, from the same fp16 P (every lane of L
+            // holds them; one 16-token block of ones serves every k-step).  The tensor
+            // pipe has room for them: its cost per MMA is the same at N = 32 as at 64,
+            // and the softmax warps, not the MMAs, bound a stage.
+            tc::mma_ts(tmem + kTcColL, tmem + kTcColOnes, dpa + 16 * j, idesc_l, j > 0 ? 1u : acc0);
           }
-          __syncwarp();
-          const int qi = qs - n_sst;  // INT2 stage index (the ring runs over INT2 stages only)
-          if (qi >= 0 && qi + 2 < n_int) {
-            wait(b_empty + 8 * (qi & 1), (qi >> 1) & 1);
-            if (tc::elect_one()) tc_issue_stage(sm, a, qi + 2, lo, hi, bs_log2, page0, h, &tmk, &tmv, b_full);
-            __syncwarp();
-          }
-          ++qs;
-        } else {
-          // PV of stage ps from V^T[ps & 1], P^T[ps & 1]
-          wait(b_p, ps & 1);
-          tc::tc_fence_after();
-          const uint64_t dva = dv0 + (uint64_t)((ps & 1) * (sizeof(sm.vt[0]) >> 4));
-          const uint64_t dvb = dva + (16 * kTcVtSbo >> 4);
-          const uint64_t dpa = dp0 + (uint64_t)((ps & 1) * (sizeof(sm.pt[0]) >> 4));
-          const uint32_t d_o = tmem + kTcColO;
-          const uint32_t acc0 = ps > 0 ? 1u : 0u;
-          if (tc::elect_one()) {
-#pragma unroll
-            for (int j = 0; j < kTcStage / 16; ++j) {
-              tc::mma_ss(d_o, dva + 16 * j, dpa + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
-              tc::mma_ss(d_o + 32, dvb + 16 * j, dpa + 16 * j, idesc_pv, j > 0 ? 1u : acc0);
-            }
-            tc::mma_commit(b_pv);
-          }
-          __syncwarp();
-          ++ps;
+          tc::mma_commit(b_pv + 8 * (ps & 1));
         }
+        __syncwarp();
+        ++ps;
+        prog = true;
       }
-      // drain: the last MMAs complete before TMEM is released
-      if (nst > 0 && !tc::mbar_wait(b_pv, (nst - 1) & 1)) flag_error(16u);
+      if (qs < nst && __shfl_sync(0xffffffffu, (int)tc::mbar_test(b_k + 8 * (qs & 1), (qs >> 1) & 1), 0)) {
+        // QK of stage qs into S[qs & 1] from A_K[qs & 1]
+        tc::tc_fence_after();
+        const uint32_t d_s = tmem + kTcColS + 32 * (qs & 1), a_k = tmem + ((qs & 1) ? kTcColA1 : kTcColA0);
+        if (tc::elect_one()) {
+#pragma unroll
+          for (int j = 0; j < kTcK / 16; ++j) tc::mma_ts(d_s, a_k + 8 * j, dq0 + 16 * j, idesc_qk, j > 0 ? 1u : 0u);
+          tc::mma_commit(b_s + 8 * (qs & 1));
+        }
+        __syncwarp();
+        ++qs;
+        prog = true;
+      }
+      if (rf < n_int && __shfl_sync(0xffffffffu, (int)tc::mbar_test(b_empty + 8 * (rf & 1), ((rf - 2) >> 1) & 1), 0)) {
+        // ring slot rf & 1 was read by every dequant warp (INT2 stage rf - 2)
+        if (tc::elect_one()) tc_issue_stage(sm, a, rf, lo, hi, bs_log2, page0, h, &tmk, &tmv, b_full);
+        __syncwarp();
+        ++rf;
+        prog = true;
+      }
+      if (prog) {
+        idle = 0;
+      } else if (__shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&sm.abort), 0) != 0) {
+        break;  // another warp timed out: drain
+      } else if (++idle > 4 * tc::kSpinLimit) {
+        if (lane == 0) {
+          *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+          flag_error(16u);
+        }
+        break;
+      }
     }
-  } else {
-    // ============================ dequant + softmax warps.  Warp w serves the 32
-    // tokens of TMEM lane quarter w % 4 (tok = 32 (w % 4) + lane) in role
-    // q = w / 4: K dims [0, 128) (q = 0), K dims [128, 256) (1), V dims
-    // [0, 128) (2), V dims [128, 256) (3); in the softmax, thread (tok, q) owns
-    // query rows [8 q, 8 q + 8).  Each role waits only on the buffers it
-    // touches (no CTA-wide barrier per stage), so the four roles that share a
-    // scheduler overlap.  Iteration it: operands of stage it (K -> TMEM,
-    // V -> V^T[it & 1]), then the softmax of stage it - 1, whose QK ran meanwhile.
+  } else if (warp < kTcDeqWarps) {
+    // ============================ dequant warps.  Warp w serves the 32 tokens of
+    // TMEM lane quarter w % 4 (tok = 32 (w % 4) + lane) in role q = w / 4: K dims
+    // [0, 128) (q = 0), K dims [128, 256) (1), V dims [0, 128) (2), V dims
+    // [128, 256) (3).  K goes into TMEM (A operand), V into V^T in shared memory;
+    // the softmax runs in its own warps, so these warps only dequantise.
     const int q = warp >> 2, tok = tid & 127;
     const bool is_k = q < 2;
     const int half = q & 1;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const bool need_lim = hi > seq - qlen + 1;  // history reaches the causal window (cache-only chunks)
-    const float scale = a.scale_log2;
     const uint32_t neg_inf = std::is_same<T, __nv_bfloat16>::value ? 0xFF80u : 0xFC00u;
     // this thread's 32 code bytes as two 16-byte pieces of the raw rows (offsets
     // from ka[slot][tok]; kb / va / vb follow ka at fixed distances):
@@ -533,351 +657,317 @@ __global__ void __maxnreg__(96)
     const int off0 = (q == 0) ? 32 : (q == 1) ? kKb + 16 : (q == 2) ? kVa : kVb + 16;
     const int off1 = (q == 0) ? kKb : (q == 1) ? kKb + 32 : (q == 2) ? kVa + 16 : kVb + 32;
     const int meta_off = is_k ? 0 : 4;  // K (scale, zero) at slot bytes [0, 4), V at [4, 8)
-    float mrow[8], muse[8], lrow[8];  // running maxima, the same with -inf -> 0, sums
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      mrow[r] = -INFINITY;
-      muse[r] = 0.0f;
-      lrow[r] = 0.0f;
-    }
-    int nslow = 0;
-    int pos_prev = hi;  // position of this thread's token in the stage whose softmax runs next
     const int vt_off = (16 * half) * kTcVtSbo + (tok >> 3) * 128 + (tok & 7) * 16;
-    const int pt_off = q * kTcVtSbo + (tok >> 3) * 128 + (tok & 7) * 16;
 
-    for (int it = 0; it <= nst; ++it) {
-      int pos_it = hi;
-      bool pv_done = false;  // this warp has waited for the PV of stage it - 2
-      if (it < nst) {
-        // ======== operands of stage it
-        const int b = it & 1;
-        const uint32_t t_a = tmem + lane_base + (b ? kTcColA1 : kTcColA0) + 64 * half;
-        if (!is_k) {
-          // V warps count in the K barrier too: their arrival releases S[b], which
-          // they last read in the softmax of stage it - 2, to the QK of stage it
-          tc::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(b_k + 8 * b);
+    for (int it = 0; it < nst; ++it) {
+      const int b = it & 1;
+      const uint32_t t_a = tmem + lane_base + (b ? kTcColA1 : kTcColA0) + 64 * half;
+      // A_K[b] was last read by the QK of stage it - 2, V^T[b] by its PV
+      auto wait_out = [&]() {
+        if (it >= 2) {
+          if (is_k) wait(b_s + 8 * b, ((it - 2) >> 1) & 1);
+          else wait(b_pv + 8 * b, ((it - 2) >> 1) & 1);
+          tc::tc_fence_after();
         }
-        int pos;
-        bool live;
-        const bool is_int = it >= n_sst;
-        if (is_int) {
-          const int ii = it - n_sst;  // INT2 stage
-          const int slot = ii & 1;
-          pos = lo + ii * kTcStage + tok;
-          wait(b_full + 8 * slot, (ii >> 1) & 1);
-          const uint8_t* raw = &sm.ka[slot][tok][0];
-          const uint32_t meta = *reinterpret_cast<const uint32_t*>(raw + meta_off);
-          const uint4 c0 = *reinterpret_cast<const uint4*>(raw + off0);
-          const uint4 c1 = *reinterpret_cast<const uint4*>(raw + off1);
-          live = pos < hi;
-          if (live && a.owner != nullptr) live = sm.own[slot][tok] != (int64_t)sm.btab[(pos >> bs_log2) - page0];
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(b_empty + 8 * slot);
-          uint2 lut = make_uint2(0, 0);
-          if (live) lut = is_k ? tc_klut<T>(meta) : tc_vlut<T>(meta);
-          const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-          if (is_k) {
-#pragma unroll
-            for (int g = 0; g < 2; ++g) {
-              uint32_t r[32];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                uint32_t v[8];
-                tc_lut_word(cw[4 * g + j], lut.x, lut.y, v);
-                tc_k_order(v, r + 8 * j);
-              }
-              tc::tmem_st32(t_a + 32 * g, r);
-            }
-          } else {
-            if (it >= 2) {
-              // V^T[b] was last read by the PV of stage it - 2
-              wait(b_pv, (it - 2) & 1);
-              tc::tc_fence_after();
-              pv_done = true;
-            }
-            uint8_t* vt_row = sm.vt[b] + vt_off;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              uint32_t r[8];
-              tc_lut_word(cw[j], lut.x, lut.y, r);
-              *reinterpret_cast<uint4*>(vt_row + (2 * j) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
-              *reinterpret_cast<uint4*>(vt_row + (2 * j + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
-            }
-          }
-        } else {
-          // staged stage: the j-th staged position of this CTA's groups (fp32 rows);
-          // consecutive j go to different lane quarters, so a partial stage
-          // spreads its loads over all sixteen warps
-          const int j = it * kTcStage + (tok & 31) * 4 + (tok >> 5);
-          live = j < n_staged;
-          pos = hi;
-          int64_t row_off = 0;
-          if (it == 0) {
-            // located in the prologue
-            row_off = live ? sm.srow[tok] : 0;
-            pos = sm.spos[tok];
-          } else if (live) {
-            int lo_w = 0, hi_w = ngroups - 1;  // last group whose prefix count is <= j
-            while (lo_w < hi_w) {
-              const int mid = (lo_w + hi_w + 1) >> 1;
-              if (sm.gpref[mid] <= j) lo_w = mid; else hi_w = mid - 1;
-            }
-            const int bit = (int)__fns(sm.gmask[lo_w], 0u, j - sm.gpref[lo_w] + 1);
-            pos = (sp + lo_w * nsplit) * 32 + bit;
-            const int blk = a.bt[(int64_t)req * a.bt_stride + (pos >> bs_log2)];
-            const int64_t seat = (int64_t)(blk % (int)a.stage_rows) * bs + (pos & (bs - 1));
-            row_off = (seat * a.hk + h) * D;
-          }
-          // coalesced fp32 loads: a thread reads 16 bytes (dims 4 (lane % 4) .. + 3 of a 16-dim
-          // group) of the token of lane lane / 4 (+ 8, 16, 24) of the quarter, so each
-          // instruction covers 8 tokens x 64 contiguous bytes; dead tokens get zeros
-          const float* src = (is_k ? a.stage_k : a.stage_v) + 128 * half + 4 * (lane & 3);
-          // (loads of a pass are issued before any store: one memory round trip per pass)
-          if (is_k) {
-            // tcgen05.st.16x256b: thread i writes lanes i / 4 and 8 + i / 4 of a 16-lane half,
-            // columns 2 (i % 4), + 1 of each 16-dim group: (dims 4m, 4m+2), (4m+1, 4m+3)
-#pragma unroll 1
-            for (int hb = 0; hb < 2; ++hb) {
-              const int la = 16 * hb + (lane >> 2), lb = la + 8;
-              const int64_t ra = __shfl_sync(0xffffffffu, row_off, la), rb = __shfl_sync(0xffffffffu, row_off, lb);
-              const bool va = __shfl_sync(0xffffffffu, (int)live, la) != 0;
-              const bool vb = __shfl_sync(0xffffffffu, (int)live, lb) != 0;
-              if (!__any_sync(0xffffffffu, vb)) {
-                // lanes 8..15 of the half are dead: one pass of 8 loads
-                float4 xs[8];
-#pragma unroll
-                for (int g = 0; g < 8; ++g)
-                  xs[g] = va ? __ldg(reinterpret_cast<const float4*>(src + ra + 16 * g)) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int cb = 0; cb < 2; ++cb) {
-                  uint32_t r[16];
-#pragma unroll
-                  for (int g = 0; g < 4; ++g) {
-                    const float4 x = xs[4 * cb + g];
-                    r[4 * g] = pack2<T>(chain<T>(x.x), chain<T>(x.z));
-                    r[4 * g + 1] = pack2<T>(chain<T>(x.y), chain<T>(x.w));
-                    r[4 * g + 2] = 0u;
-                    r[4 * g + 3] = 0u;
-                  }
-                  tc::tmem_st16x256_x4(t_a + ((uint32_t)(16 * hb) << 16) + 32 * cb, r);
-                }
-              } else {
-#pragma unroll 1
-                for (int cb = 0; cb < 2; ++cb) {
-                  float4 xs[4], ys[4];
-#pragma unroll
-                  for (int g = 0; g < 4; ++g) {
-                    const int off = 16 * (4 * cb + g);
-                    xs[g] = va ? __ldg(reinterpret_cast<const float4*>(src + ra + off)) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    ys[g] = vb ? __ldg(reinterpret_cast<const float4*>(src + rb + off)) : make_float4(0.f, 0.f, 0.f, 0.f);
-                  }
-                  uint32_t r[16];
-#pragma unroll
-                  for (int g = 0; g < 4; ++g) {
-                    r[4 * g] = pack2<T>(chain<T>(xs[g].x), chain<T>(xs[g].z));
-                    r[4 * g + 1] = pack2<T>(chain<T>(xs[g].y), chain<T>(xs[g].w));
-                    r[4 * g + 2] = pack2<T>(chain<T>(ys[g].x), chain<T>(ys[g].z));
-                    r[4 * g + 3] = pack2<T>(chain<T>(ys[g].y), chain<T>(ys[g].w));
-                  }
-                  tc::tmem_st16x256_x4(t_a + ((uint32_t)(16 * hb) << 16) + 32 * cb, r);
-                }
-              }
-            }
-          } else {
-            if (it >= 2) {
-              wait(b_pv, (it - 2) & 1);
-              tc::tc_fence_after();
-              pv_done = true;
-            }
-            // V^T word of (token, dims 4m, 4m+2) at row group 2g, (4m+1, 4m+3) at 2g+1;
-            // the 8 tokens x 4 words of an instruction are 128 contiguous bytes
-            uint8_t* vt_q = sm.vt[b] + (16 * half) * kTcVtSbo + ((warp & 3) * 4) * 128 + 4 * lane;
-#pragma unroll 1
-            for (int o = 0; o < 4; ++o) {
-              const int lt = 8 * o + (lane >> 2);
-              const int64_t rt = __shfl_sync(0xffffffffu, row_off, lt);
-              const bool vt = __shfl_sync(0xffffffffu, (int)live, lt) != 0;
-              float4 xs[8];
-#pragma unroll
-              for (int g = 0; g < 8; ++g)
-                xs[g] = vt ? __ldg(reinterpret_cast<const float4*>(src + rt + 16 * g)) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-              for (int g = 0; g < 8; ++g) {
-                uint32_t* dst = reinterpret_cast<uint32_t*>(vt_q + o * 128 + (2 * g) * kTcVtSbo);
-                dst[0] = pack2<__half>(chain_f16<T>(xs[g].x), chain_f16<T>(xs[g].z));
-                dst[kTcVtSbo / 4] = pack2<__half>(chain_f16<T>(xs[g].y), chain_f16<T>(xs[g].w));
-              }
-            }
-          }
-        }
+      };
+      bool live;
+      if (it >= n_sst) {
+        const int ii = it - n_sst;  // INT2 stage
+        const int slot = ii & 1;
+        const int pos = lo + ii * kTcStage + tok;
+        wait(b_full + 8 * slot, (ii >> 1) & 1);
+        const uint8_t* raw = &sm.ka[slot][tok][0];
+        const uint32_t meta = *reinterpret_cast<const uint32_t*>(raw + meta_off);
+        const uint4 c0 = *reinterpret_cast<const uint4*>(raw + off0);
+        const uint4 c1 = *reinterpret_cast<const uint4*>(raw + off1);
+        live = pos < hi;
+        if (live && a.owner != nullptr) live = sm.own[slot][tok] != (int64_t)sm.btab[(pos >> bs_log2) - page0];
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(b_empty + 8 * slot);
+        uint2 lut = make_uint2(0, 0);
+        if (live) lut = is_k ? tc_klut<T>(meta) : tc_vlut<T>(meta);
+        const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        // (the ring slot is released before waiting for the output buffer, so the
+        // next TMA into it does not wait for the slowest consumer's PV / QK)
+        wait_out();
         if (is_k) {
-          if (q == 0) {
-            // bias k-step (columns 128..135): element 256 = 0 for live tokens, -inf for masked ones
-            const uint32_t bias[8] = {live ? 0u : neg_inf, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-            tc::tmem_st8(t_a + 128, bias);
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            uint32_t r[32];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint32_t v[8];
+              tc_lut_word(cw[4 * g + j], lut.x, lut.y, v);
+              tc_k_order(v, r + 8 * j);
+            }
+            tc::tmem_st32(t_a + 32 * g, r);
           }
-          tc::tmem_wait_st();
-          tc::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(b_k + 8 * b);
         } else {
-          tc::fence_async_smem();
+          uint8_t* vt_row = sm.vt[b] + vt_off;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint32_t r[8];
+            tc_lut_word(cw[j], lut.x, lut.y, r);
+            *reinterpret_cast<uint4*>(vt_row + (2 * j) * kTcVtSbo) = make_uint4(r[0], r[1], r[2], r[3]);
+            *reinterpret_cast<uint4*>(vt_row + (2 * j + 1) * kTcVtSbo) = make_uint4(r[4], r[5], r[6], r[7]);
+          }
         }
-        pos_it = pos;
+      } else {
+        // staged stage: the j-th staged position of this CTA's groups (fp32 rows);
+        // consecutive j go to different lane quarters, so a partial stage
+        // spreads its loads over all sixteen warps
+        const int j = it * kTcStage + (tok & 31) * 4 + (tok >> 5);
+        live = j < n_staged;
+        wait_out();
+        int64_t row_off = 0;
+        if (it == 0) {
+          row_off = live ? sm.srow[tok] : 0;  // located in the prologue
+        } else if (live) {
+          int pos;
+          row_off = tc_staged_row(sm, a, j, ngroups, sp, nsplit, req, bs_log2, h, &pos);
+        }
+        // coalesced fp32 loads: a thread reads 16 bytes (dims 4 (lane % 4) .. + 3 of a 16-dim
+        // group) of the token of lane lane / 4 (+ 8, 16, 24) of the quarter, so each
+        // instruction covers 8 tokens x 64 contiguous bytes; dead tokens get zeros
+        const float* src = (is_k ? a.stage_k : a.stage_v) + 128 * half + 4 * (lane & 3);
+        if (is_k) {
+          tc_staged_k<T>(t_a, src, row_off, live, lane);
+        } else {
+          tc_staged_v<T>(sm.vt[b] + (16 * half) * kTcVtSbo + ((warp & 3) * 4) * 128 + 4 * lane, src, row_off, live,
+                         lane);
+        }
       }
-      if (it >= 2 && !pv_done) {
-        // P^T[(it - 1) & 1] and, on a rescale, O: every PV up to stage it - 2 is done
-        wait(b_pv, (it - 2) & 1);
-        tc::tc_fence_after();
+      if (is_k) {
+        if (q == 0) {
+          // bias k-step (columns 128..135): element 256 = 0 for live tokens, -inf for masked ones
+          const uint32_t bias[8] = {live ? 0u : neg_inf, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+          tc::tmem_st8(t_a + 128, bias);
+        }
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(b_k + 8 * b);
+      } else {
+        tc::fence_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(b_v + 8 * b);
       }
-      if (it >= 1) {
-        // ======== softmax of stage st = it - 1 (its QK ran meanwhile)
-        const int st = it - 1;
-        wait(b_s + 8 * (st & 1), (st >> 1) & 1);
-        tc::tc_fence_after();
-        const uint32_t t_s = tmem + lane_base + kTcColS + 32 * (st & 1) + 8 * q;
-        const uint32_t t_o = tmem + lane_base + kTcColO + 8 * q;
-        float x[8];
-        {
-          uint32_t sraw[8];
-          tc::tmem_ld8(t_s, sraw);
+    }
+  } else {
+    // ============================ softmax warps.  Warp 16 + 4 hr + lq serves the
+    // tokens of TMEM lane quarter lq, one token per thread, for query rows
+    // 16 hr .. 16 hr + 15: it reads the token's scores from S^T (lane = token,
+    // column = row), keeps the running row maxima (a copy per warp, in
+    // sm.mrow) and writes the token's P^T column; the row sums of P come from
+    // the tensor cores (L beside O), so O and l see the same fp16 P.  A half
+    // with no query row (16 hr >= R) keeps only the barrier protocol.  The
+    // running maximum moves only when a score exceeds it by more than 15 (log2
+    // units): P stays <= 2^15 in fp16, and O / l are rescaled on those stages
+    // only.  The four warps of a half vote and reduce on named barrier 1 + hr.
+    const int lq = (warp - kTcDeqWarps) & 3, hr = (warp - kTcDeqWarps) >> 2, tok = 32 * lq + lane;
+    const uint32_t lane_base = (uint32_t)(32 * lq) << 16;
+    const bool need_lim = hi > seq - qlen + 1;  // history reaches the causal window (cache-only chunks)
+    const float scale = a.scale_log2;
+    const bool active = 16 * hr < R;
+    const int pt_off = (tok >> 3) * 128 + (tok & 7) * 16;
+    if (hr == 0) {
+      // the ones block of the row-sum MMA (fp16 1.0 pairs), this quarter's lanes
+      const uint32_t ones[8] = {0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u,
+                                0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u};
+      tc::tmem_st8(tmem + lane_base + kTcColOnes, ones);
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+    }
+    // S[0] and S[1] are free for the QKs of stages 0 and 1
+    if (lane == 0) {
+      tc::mbar_arrive(b_k);
+      tc::mbar_arrive(b_k + 8);
+    }
+    for (int st = 0; st < nst; ++st) {
+      const int b = st & 1;
+      int pos = hi;  // position of this thread's token (for the causal limit of cache-only chunks)
+      if (need_lim && active) {
+        if (st >= n_sst) {
+          pos = lo + (st - n_sst) * kTcStage + tok;
+        } else {
+          const int j = st * kTcStage + (tok & 31) * 4 + (tok >> 5);
+          if (st == 0) pos = sm.spos[tok];
+          else if (j < n_staged) tc_staged_row(sm, a, j, ngroups, sp, nsplit, req, bs_log2, h, &pos);
+        }
+      }
+      wait(b_s + 8 * b, (st >> 1) & 1);
+      tc::tc_fence_after();
+      if (st >= 2) {
+        // P^T[b] was last read by the PV of stage st - 2
+        wait(b_pv + 8 * b, ((st - 2) >> 1) & 1);
+      }
+      if (active) {
+        // the token's scaled, masked scores of rows 16 hr .. 16 hr + 15
+        auto load_x = [&](float (&x)[16]) {
+          uint32_t sraw[16];
+          tc::tmem_ld16(tmem + lane_base + kTcColS + 32 * b + 16 * hr, sraw);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int r = 0; r < 8; ++r) x[r] = __uint_as_float(sraw[r]) * scale;
-        }
-        if (need_lim) {
+          for (int i = 0; i < 16; ++i) x[i] = __uint_as_float(sraw[i]) * scale;
+          if (need_lim) {
 #pragma unroll
-          for (int r = 0; r < 8; ++r)
-            if (pos_prev >= sm.lim[8 * q + r]) x[r] = -INFINITY;
-        }
+            for (int i = 0; i < 16; ++i)
+              if (pos >= sm.lim[16 * hr + i]) x[i] = -INFINITY;
+          }
+        };
+        float x[16];
+        load_x(x);
+        // running maxima: every softmax warp keeps its own copy (all compute the same values)
+        auto load_m = [&](float (&m)[16]) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            const float4 m4 = *reinterpret_cast<const float4*>(&sm.mrow[lq][16 * hr + i]);
+            m[i] = m4.x;
+            m[i + 1] = m4.y;
+            m[i + 2] = m4.z;
+            m[i + 3] = m4.w;
+          }
+        };
+        float mcur[16];
+        load_m(mcur);
         bool need = false;
 #pragma unroll
-        for (int r = 0; r < 8; ++r) need = need || (x[r] > mrow[r] + kTcHeadroom);
-        if (tc::bar_or(1 + q, 128, need)) {
-          // new row maxima over the stage's 128 tokens; rescale l and (if they moved) O.
-          // (the reduction buffer alternates: the vote barrier of any later stage
-          // orders these reads before the buffer's next writes)
-          int(*red)[8] = sm.red[nslow & 1];
-          ++nslow;
-          int rm[8];
+        for (int i = 0; i < 16; ++i) need = need || (x[i] > mcur[i] + kTcHeadroom);
+        if (hr == 0 ? tc::bar_or(1, 128, need) : tc::bar_or(2, 128, need)) {
+          // new row maxima over the stage's 128 tokens; rescale O and L if they moved
 #pragma unroll
-          for (int r = 0; r < 8; ++r) rm[r] = __reduce_max_sync(0xffffffffu, tc_ord(x[r]));
-          if (lane == 0) {
-            *reinterpret_cast<int4*>(&red[warp][0]) = make_int4(rm[0], rm[1], rm[2], rm[3]);
-            *reinterpret_cast<int4*>(&red[warp][4]) = make_int4(rm[4], rm[5], rm[6], rm[7]);
+          for (int i = 0; i < 16; i += 4) {
+            const int4 v4 = make_int4(__reduce_max_sync(0xffffffffu, tc_ord(x[i])),
+                                      __reduce_max_sync(0xffffffffu, tc_ord(x[i + 1])),
+                                      __reduce_max_sync(0xffffffffu, tc_ord(x[i + 2])),
+                                      __reduce_max_sync(0xffffffffu, tc_ord(x[i + 3])));
+            if (lane == 0) *reinterpret_cast<int4*>(&sm.red[lq][16 * hr + i]) = v4;
           }
-          tc::bar_sync(1 + q, 128);
+          if (hr == 0) tc::bar_sync(1, 128); else tc::bar_sync(2, 128);
+          // (the scores and maxima are read again after the rescale: no registers held
+          // across it.  sm.red is rewritten only after the next vote, which every warp
+          // reaches after these reads)
+          // lane i (and i + 16) handles row 16 hr + i: its alpha (the O / L columns fetch
+          // it by shuffle) and this warp's copy of its new maximum
+          float alpha_l;
+          {
+            const int rl = 16 * hr + (lane & 15);
+            const float mold = sm.mrow[lq][rl];
+            int mx = sm.red[0][rl];
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            if (w == (warp & 3)) continue;  // own warp's maxima are already in rm
-            const int4 a4 = *reinterpret_cast<const int4*>(&red[4 * q + w][0]);
-            const int4 b4 = *reinterpret_cast<const int4*>(&red[4 * q + w][4]);
-            rm[0] = max(rm[0], a4.x);
-            rm[1] = max(rm[1], a4.y);
-            rm[2] = max(rm[2], a4.z);
-            rm[3] = max(rm[3], a4.w);
-            rm[4] = max(rm[4], b4.x);
-            rm[5] = max(rm[5], b4.y);
-            rm[6] = max(rm[6], b4.z);
-            rm[7] = max(rm[7], b4.w);
+            for (int w = 1; w < kTcQuarters; ++w) mx = max(mx, sm.red[w][rl]);
+            const float mnew = fmaxf(mold, tc_unord(mx));
+            alpha_l = (mold == -INFINITY) ? 0.0f : tc_exp2(mold - mnew);
+            __syncwarp();
+            if (lane < 16) sm.mrow[lq][rl] = mnew;
+            __syncwarp();
           }
-          float alpha[8];
-          bool moved = false;
+          if (st > 0 && __any_sync(0xffffffffu, alpha_l != 1.0f)) {
+            // O holds every PV before stage st once the PV of stage st - 1 is done
+            wait(b_pv + 8 * (b ^ 1), ((st - 1) >> 1) & 1);
+            tc::tc_fence_after();
 #pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            const float mn = fmaxf(mrow[r], tc_unord(rm[r]));
-            alpha[r] = (mrow[r] == -INFINITY) ? 0.0f : tc_exp2(mrow[r] - mn);
-            moved = moved || alpha[r] != 1.0f;
-            lrow[r] *= alpha[r];
-            mrow[r] = mn;
-            muse[r] = (mn == -INFINITY) ? 0.0f : mn;
-          }
-          if (st > 0 && moved) {
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              uint32_t o[8];
-              tc::tmem_ld8(t_o + 32 * hh, o);
+            for (int hh = 0; hh < 3; ++hh) {
+              // O dims [0, 128), [128, 256), then L
+              const uint32_t col = tmem + lane_base + (hh < 2 ? kTcColO + 32 * hh : kTcColL) + 16 * hr;
+              uint32_t o[16];
+              tc::tmem_ld16(col, o);
               tc::tmem_wait_ld();
 #pragma unroll
-              for (int r = 0; r < 8; ++r) o[r] = __float_as_uint(__uint_as_float(o[r]) * alpha[r]);
-              tc::tmem_st8(t_o + 32 * hh, o);
+              for (int i = 0; i < 16; ++i)
+                o[i] = __float_as_uint(__uint_as_float(o[i]) * __shfl_sync(0xffffffffu, alpha_l, i));
+              tc::tmem_st16(col, o);
             }
             tc::tmem_wait_st();
           }
+          load_m(mcur);
+          load_x(x);
         }
-        // P^T[st & 1] (fp16) and l
-        uint32_t pk[4];
+        // P^T[b] (fp16) rows 16 hr .. 16 hr + 15 and l
+        uint32_t pk[8];
 #pragma unroll
-        for (int r = 0; r < 8; r += 2) {
-          const float p0 = tc_exp2(x[r] - muse[r]), p1 = tc_exp2(x[r + 1] - muse[r + 1]);
-          lrow[r] += p0;
-          lrow[r + 1] += p1;
-          const __half2 ph = __floats2half2_rn(p0, p1);
-          pk[r >> 1] = *reinterpret_cast<const uint32_t*>(&ph);
+        for (int i = 0; i < 16; i += 2) {
+          const float mu0 = (mcur[i] == -INFINITY) ? 0.0f : mcur[i];
+          const float mu1 = (mcur[i + 1] == -INFINITY) ? 0.0f : mcur[i + 1];
+          x[i] = tc_exp2(x[i] - mu0);
+          x[i + 1] = tc_exp2(x[i + 1] - mu1);
+          const __half2 ph = __floats2half2_rn(x[i], x[i + 1]);
+          pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&ph);
         }
-        *reinterpret_cast<uint4*>(sm.pt[st & 1] + pt_off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        tc::fence_async_smem();
-        tc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(b_p);
+        uint8_t* pt = sm.pt[b] + pt_off + (2 * hr) * kTcVtSbo;
+        *reinterpret_cast<uint4*>(pt) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(pt + kTcVtSbo) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
-      pos_prev = pos_it;
+      // S[b] is read: free it for the QK of stage st + 2; P^T[b] is written
+      tc::tc_fence_before();
+      tc::fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tc::mbar_arrive(b_k + 8 * b);
+        tc::mbar_arrive(b_p + 8 * b);
+      }
     }
 
-    // ---------------- epilogue: l over the 128 tokens, normalised partial O and LSE
+    // ---------------- epilogue: normalised partial O and LSE
     if (nst > 0) {
-      wait(b_pv, (nst - 1) & 1);
+      wait(b_pv + 8 * ((nst - 1) & 1), ((nst - 1) >> 1) & 1);
       tc::tc_fence_after();
     }
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      float v = lrow[r];
-#pragma unroll
-      for (int o2 = 16; o2 > 0; o2 >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o2);
-      if (lane == 0) sm.lsum[warp][r] = v;
-    }
-    tc::bar_sync(1 + q, 128);
-    float L[8];
-#pragma unroll
-    for (int r = 0; r < 8; ++r)
-      L[r] = (sm.lsum[4 * q][r] + sm.lsum[4 * q + 1][r]) + (sm.lsum[4 * q + 2][r] + sm.lsum[4 * q + 3][r]);
     const int64_t pslot = p.part_begin[ri] + sp;
-    const int64_t prow0 = (pslot * a.hk + h) * kTcRows + 8 * q;
-    const uint32_t t_o = tmem + lane_base + kTcColO + 8 * q;
+    const int64_t prow0 = (pslot * a.hk + h) * kTcRows;
+    __half* po = reinterpret_cast<__half*>(a.part_o);
+    if (active) {
+      float L[16];
+      {
+        uint32_t lr[16];
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      uint32_t o[8];
+        for (int i = 0; i < 16; ++i) lr[i] = 0u;
+        if (nst > 0) {
+          tc::tmem_ld16(tmem + lane_base + kTcColL + 16 * hr, lr);
+          tc::tmem_wait_ld();
+        }
 #pragma unroll
-      for (int r = 0; r < 8; ++r) o[r] = 0u;
-      if (nst > 0) {
-        tc::tmem_ld8(t_o + 32 * hh, o);
-        tc::tmem_wait_ld();
+        for (int i = 0; i < 16; ++i) L[i] = __uint_as_float(lr[i]);
       }
-      // normalised O in fp16 (the merge reads it once; 2^-11 relative is far inside the
-      // output tolerance), zero for empty rows
-      const int dim = tc_dim(128 * hh + tok);
-      __half* po = reinterpret_cast<__half*>(a.part_o);
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        if (8 * q + r >= R) continue;
-        const bool keep = L[r] > 0.0f || L[r] != L[r];
-        po[(prow0 + r) * D + dim] = __float2half_rn(keep ? __uint_as_float(o[r]) / L[r] : 0.0f);
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t o[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = 0u;
+        if (nst > 0) {
+          tc::tmem_ld16(tmem + lane_base + kTcColO + 32 * hh + 16 * hr, o);
+          tc::tmem_wait_ld();
+        }
+        // normalised O in fp16 (the merge reads it once; 2^-11 relative is far inside the
+        // output tolerance), zero for empty rows
+        const int dim = tc_dim(128 * hh + tok);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int r = 16 * hr + i;
+          if (r >= R) continue;
+          const bool keep = L[i] > 0.0f || L[i] != L[i];
+          po[(prow0 + r) * D + dim] = __float2half_rn(keep ? __uint_as_float(o[i]) / L[i] : 0.0f);
+        }
+      }
+      if (lq == 0 && lane < 16 && 16 * hr + lane < R) {
+        float Li = 0.0f, mi = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (lane == i) {
+            Li = L[i];
+            mi = sm.mrow[lq][16 * hr + i];
+          }
+        a.part_lse[prow0 + 16 * hr + lane] =
+            (Li > 0.0f || Li != Li) ? (mi + log2f(Li)) * 0.69314718055994531f : -INFINITY;
       }
     }
-#pragma unroll
-    for (int r = 0; r < 8; ++r)
-      if (tok == r && 8 * q + r < R)
-        a.part_lse[prow0 + r] =
-            (L[r] > 0.0f || L[r] != L[r]) ? (mrow[r] + log2f(L[r])) * 0.69314718055994531f : -INFINITY;
   }
 
   // ---------------- teardown
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
-  if (warp == kWarps) tc::tmem_dealloc(tmem, kTcCols);
+  if (warp == kTcProdWarp) tc::tmem_dealloc(tmem, kTcCols);
 }
 
 // Merge of the splits (_merge_slab, slab_attention.py:156-194, joint form)

@@ -34,6 +34,16 @@ OSCAR_DEVINL bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// non-blocking: has the phase with the given parity completed?
+OSCAR_DEVINL bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // true when the phase with the given parity completed; false after kSpinLimit polls
 OSCAR_DEVINL bool mbar_wait(uint32_t bar, uint32_t parity) {
   for (uint32_t i = 0; i < kSpinLimit; ++i)
