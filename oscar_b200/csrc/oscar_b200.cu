@@ -956,6 +956,37 @@ extern "C" int oscar_rotate_rows_batch(const oscar_rotate_seg* segs, int32_t n_s
   }
   if (b.n == 0) return OSCAR_OK;
   b.tile_begin[b.n] = (int)tiles;
+  // The kernel reads the rotation matrices before it waits for the launch in
+  // front of it, unless that launch may have written one: the outputs of this
+  // thread's previous rotation launch are remembered and checked for overlap.
+  // (No other library kernel writes anything a caller could pass as a rotation.)
+  {
+    struct Range {
+      uintptr_t lo, hi;
+    };
+    static thread_local Range prev[2 * oscar::kRotMaxSegs];
+    static thread_local int n_prev = 0;
+    const size_t out_es = out_dtype == OSCAR_DTYPE_F32 ? 4 : 2;
+    const size_t rot_bytes = (size_t)head_dim * head_dim * sizeof(float);
+    b.rot_early = 1;
+    for (int i = 0; i < b.n; ++i) {
+      const uintptr_t lo = reinterpret_cast<uintptr_t>(b.seg[i].rot), hi = lo + rot_bytes;
+      for (int j = 0; j < n_prev; ++j)
+        if (lo < prev[j].hi && prev[j].lo < hi) b.rot_early = 0;
+    }
+    n_prev = 0;
+    for (int i = 0; i < b.n; ++i) {
+      const oscar::RotSeg& d = b.seg[i];
+      if (d.out != nullptr) {
+        const uintptr_t lo = reinterpret_cast<uintptr_t>(d.out);
+        prev[n_prev++] = {lo, lo + ((size_t)(d.rows - 1) * d.out_stride + head_dim) * out_es};
+      }
+      if (d.out_f32 != nullptr) {
+        const uintptr_t lo = reinterpret_cast<uintptr_t>(d.out_f32);
+        prev[n_prev++] = {lo, lo + ((size_t)(d.rows - 1) * d.out_f32_stride + head_dim) * 4};
+      }
+    }
+  }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (x_dtype == OSCAR_DTYPE_F32) return rotate_out<float>(out_dtype, b, head_dim, s);
   if (x_dtype == OSCAR_DTYPE_BF16) return rotate_out<__nv_bfloat16>(out_dtype, b, head_dim, s);

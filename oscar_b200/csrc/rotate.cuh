@@ -39,6 +39,7 @@ struct RotBatch {
   RotSeg seg[kRotMaxSegs];
   int tile_begin[kRotMaxSegs + 1];  // first row tile of each segment; tile_begin[n] = all tiles
   int n;
+  int rot_early;  // 1: no rotation matrix was written by the launch in front (its loads may overlap it)
 };
 
 template <int D>
@@ -81,7 +82,7 @@ struct RotIn<float> {
 template <typename InT, typename OutT, int D>
 __global__ void __launch_bounds__(256) rotate_rows_kernel(const __grid_constant__ RotBatch b) {
   pdl_release();
-  pdl_wait();
+  if (!b.rot_early) pdl_wait();
   extern __shared__ __align__(16) float rsm[];
   float* rblk = rsm;                 // [D][32]: R[k][c0 + j] (R^T: R[c0 + j][k])
   float* xt = rsm + D * kRotCols;    // [D][16]: x[r0 + r][k] at k * 16 + r
@@ -114,6 +115,10 @@ __global__ void __launch_bounds__(256) rotate_rows_kernel(const __grid_constant_
       rbuf[u] = *reinterpret_cast<const float4*>(rot + (int64_t)(c0 + j) * D + 4 * k4);
     }
   }
+  // rotation matrices are layer constants: unless the launch in front wrote one
+  // (rot_early = 0), their loads overlap that launch's tail (programmatic
+  // dependent launch) and only the rows x wait for it
+  pdl_wait();
   uint4 xbuf[kXLoads];
 #pragma unroll
   for (int u = 0; u < kXLoads; ++u) {

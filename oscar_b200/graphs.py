@@ -55,3 +55,41 @@ class GraphedForward:
         inputs; returns the static output tensor."""
         self.graph.replay()
         return self.output
+
+
+class GraphedSequence:
+    """Several backend forwards captured in order into one CUDA graph — the
+    attention layers of a model step, as vLLM captures a whole model forward —
+    so one launch replays all of them and consecutive layers' kernels overlap
+    through programmatic dependent launch.  ``calls``: a list of
+    ``(impl, layer, query, key, value, kv_cache, attn_metadata, output)``
+    tuples under the same contract as :class:`GraphedForward` (static tensors,
+    fixed batch geometry per call); a layer may appear more than once."""
+
+    def __init__(self, calls, warmup: int = 1, pool=None):
+        if not calls:
+            raise ValueError("GraphedSequence needs at least one forward")
+        if not torch.cuda.is_available() or calls[0][2].device.type != "cuda":
+            raise ValueError("GraphedSequence needs CUDA tensors")
+        self.calls = list(calls)
+        dev = self.calls[0][2].device
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            seen = set()
+            for impl, layer, q, k, v, cache, md, out in self.calls:
+                if id(layer) in seen:
+                    continue
+                seen.add(id(layer))
+                for _ in range(max(1, warmup)):
+                    impl.forward(layer, q, k, v, cache, md, output=out)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, pool=pool):
+            for impl, layer, q, k, v, cache, md, out in self.calls:
+                impl.forward(layer, q, k, v, cache, md, output=out)
+
+    def replay(self) -> None:
+        """Run every captured forward, in order, on the current contents of
+        their static inputs."""
+        self.graph.replay()

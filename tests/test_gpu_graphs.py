@@ -75,3 +75,31 @@ def test_graph_replay_leaves_staging_window_as_eager_forward():
     torch.testing.assert_close(got.float(), want.float(), atol=0, rtol=0)
     assert torch.equal(layer_g._oscar_slot_owner, layer_e._oscar_slot_owner)
     assert torch.equal(layer_g._oscar_stage_k, layer_e._oscar_stage_k)
+
+
+def test_graphed_sequence_of_layers_matches_eager_forwards():
+    """Two layers captured in one graph (layer A, layer B, layer A again): the
+    replay gives each eager forward's output, in order, with the second A step
+    seeing the staging window the first one left."""
+    from oscar_b200.graphs import GraphedSequence
+
+    dev = need_gpu()
+    impl_a, layer_a, case_a, cache_a, md_a = _layer_setup(dev, 51)
+    impl_b, layer_b, case_b, cache_b, md_b = _layer_setup(dev, 52)
+    ea = _layer_setup(dev, 51)
+    eb = _layer_setup(dev, 52)
+    outs = [torch.empty(8, 6 * 256, dtype=torch.bfloat16, device=dev) for _ in range(3)]
+    seq = GraphedSequence([(impl_a, layer_a, case_a.q, case_a.k_new, case_a.v_new, cache_a, md_a, outs[0]),
+                           (impl_b, layer_b, case_b.q, case_b.k_new, case_b.v_new, cache_b, md_b, outs[1]),
+                           (impl_a, layer_a, case_a.q, case_a.k_new, case_a.v_new, cache_a, md_a, outs[2])])
+    # the capture's warm-up ran one eager forward per distinct layer
+    for impl, layer, case, cache, md in (ea, eb):
+        impl.forward(layer, case.q, case.k_new, case.v_new, cache, md, output=torch.empty_like(outs[0]))
+    seq.replay()
+    want = [torch.empty_like(outs[0]) for _ in range(3)]
+    for w, (impl, layer, case, cache, md) in zip(want, (ea, eb, ea)):
+        impl.forward(layer, case.q, case.k_new, case.v_new, cache, md, output=w)
+    torch.cuda.synchronize()
+    for g, w in zip(outs, want):
+        torch.testing.assert_close(g.float(), w.float(), atol=0, rtol=0)
+    assert torch.equal(layer_a._oscar_slot_owner, ea[1]._oscar_slot_owner)

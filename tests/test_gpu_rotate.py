@@ -62,3 +62,24 @@ def test_rotate_rows_many_one_launch_matches_separate_products(d):
             torch.testing.assert_close(f32.double(), want, atol=2e-5, rtol=2e-5)
             torch.testing.assert_close(lo, f32.to(lo.dtype), atol=0, rtol=0)
         torch.testing.assert_close(lo.double(), want.to(lo.dtype).double(), atol=1e-2, rtol=1e-2)
+
+
+def test_rotation_output_used_as_the_next_rotation_matrix():
+    """The kernel loads rotation matrices before waiting for the launch in front
+    of it; a matrix that launch just wrote (here: R1 @ R2 computed by the
+    library, then used to rotate) must be read after it is complete."""
+    from oscar_b200 import kernels
+
+    dev = need_gpu()
+    d = 256
+    g = torch.Generator(device="cpu").manual_seed(11)
+    r1 = torch.linalg.qr(torch.randn(d, d, generator=g, dtype=torch.float64)).Q.float().to(dev)
+    r2 = torch.linalg.qr(torch.randn(d, d, generator=g, dtype=torch.float64)).Q.float().to(dev)
+    x = torch.randn(64, d, generator=g).to(dev)
+    for _ in range(3):
+        prod = torch.full((d, d), float("nan"), device=dev)
+        kernels.rotate_rows(r1, r2, out=prod)  # prod = r1 @ r2, written by this launch
+        out = torch.empty(64, d, device=dev)
+        kernels.rotate_rows(x, prod, out=out)  # reads prod as its rotation right after
+        want = x.double() @ (r1.double() @ r2.double())
+        torch.testing.assert_close(out.double(), want, atol=5e-5, rtol=5e-5)
