@@ -47,10 +47,13 @@ const char* oscar_last_error(void);
 uint64_t oscar_launch_count(void);
 
 /* Selects the attention kernel family for later oscar_slab_attention calls
- * in this process: 0 = automatic (the decode kernel where eligible: D = 256,
- * at most 24 query rows per GQA group), 1 = the tile kernel only, 2 = same as
- * 0.  Both families compute the same function; the switch keeps both
- * parity-tested. */
+ * in this process: 0 = automatic (the tcgen05 decode kernel where eligible —
+ * D = 256, at most 32 query rows per GQA group, a history that fits its
+ * plan — else the mma.sync decode kernel where eligible, else the tile
+ * kernel), 1 = the tile kernel only, 2 = the mma.sync decode kernel where
+ * eligible (else the tile kernel), 3 = the tcgen05 decode kernel where
+ * eligible (else the tile kernel).  All families compute the same function;
+ * the switch keeps each of them parity-tested.  Other values: status 1. */
 int oscar_set_attention_path(int path);
 
 /* Synchronises `stream`, returns and clears the device-side bounds flag of the
