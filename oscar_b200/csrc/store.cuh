@@ -32,7 +32,7 @@ struct StoreGeom {
 // smallest u with #{|x| <= u} > k, found two bits per step (radix 4) over the
 // bit patterns (non-negative floats order like their uint32 patterns).  Step b
 // keeps the largest j in 0..3 with #{|x| <= ans + j 2^b - 1} <= k; the three
-// counts are independent, so a step costs one reduction latency.
+// counts travel packed in one word, so a step costs one warp reduction.
 template <int BPL>
 OSCAR_DEVINL float kth_abs(const float (&x)[BPL][4], const bool (&act)[BPL], int k) {
   uint32_t a[BPL][4];
@@ -44,21 +44,81 @@ OSCAR_DEVINL float kth_abs(const float (&x)[BPL][4], const bool (&act)[BPL], int
 #pragma unroll 1
   for (int b = 30; b >= 0; b -= 2) {
     const uint32_t p1 = ans + ((1u << b) - 1u), p2 = ans + ((2u << b) - 1u), p3 = ans + ((3u << b) - 1u);
-    int c1 = 0, c2 = 0, c3 = 0;
+    // the three counts (each <= 256) in 10-bit fields of one word: one warp sum per digit.
+    // p1 < p2 < p3, so a value below t of them adds to the last t fields:
+    // 0x100401 masked by ~0 << (30 - 10 t).  Contributions are independent and
+    // summed as a tree, keeping the step's dependency chain short.
+    uint32_t v[4 * BPL];
 #pragma unroll
     for (int j = 0; j < BPL; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        c1 += (a[j][e] <= p1) ? 1 : 0;
-        c2 += (a[j][e] <= p2) ? 1 : 0;
-        c3 += (a[j][e] <= p3) ? 1 : 0;
+        const uint32_t x = a[j][e];
+        const int t = (x <= p1 ? 1 : 0) + (x <= p2 ? 1 : 0) + (x <= p3 ? 1 : 0);
+        v[4 * j + e] = 0x100401u & (0xffffffffu << (30 - 10 * t));
       }
-    c1 = __reduce_add_sync(0xffffffffu, c1);
-    c2 = __reduce_add_sync(0xffffffffu, c2);
-    c3 = __reduce_add_sync(0xffffffffu, c3);
+#pragma unroll
+    for (int w = 1; w < 4 * BPL; w <<= 1)
+#pragma unroll
+      for (int i = 0; i + w < 4 * BPL; i += 2 * w) v[i] += v[i + w];
+    const uint32_t c = __reduce_add_sync(0xffffffffu, v[0]);
+    const int c1 = (int)(c & 1023u), c2 = (int)((c >> 10) & 1023u), c3 = (int)(c >> 20);
     ans += (uint32_t)((c1 <= k ? 1 : 0) + (c2 <= k ? 1 : 0) + (c3 <= k ? 1 : 0)) << b;
   }
   return __uint_as_float(ans);
+}
+
+// The same k-th smallest |x| when it is near the top (the clip ratios in use
+// keep 92-96 % of a vector, so it is the 11th or 21st largest of 256): a
+// tournament over the warp.  Each lane sorts its values descending; a round
+// takes the warp maximum of the lanes' heads, counts its copies (one ballot;
+// a reduction only when some lane holds two) and pops them, until the count
+// reaches the rank from the top.  Values order by their bit patterns, as in
+// kth_abs; inactive values are 0 and can only be reached when the answer is 0.
+template <int BPL>
+OSCAR_DEVINL float kth_abs_top(const float (&x)[BPL][4], const bool (&act)[BPL], int rank) {
+  constexpr int V = 4 * BPL;
+  uint32_t a[V];
+#pragma unroll
+  for (int j = 0; j < BPL; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) a[4 * j + e] = act[j] ? (__float_as_uint(x[j][e]) & 0x7fffffffu) : 0u;
+  // odd-even transposition sort, descending (V <= 8 values: V rounds)
+#pragma unroll
+  for (int r = 0; r < V; ++r)
+#pragma unroll
+    for (int i = r & 1; i + 1 < V; i += 2) {
+      const uint32_t hi = max(a[i], a[i + 1]), lo = min(a[i], a[i + 1]);
+      a[i] = hi;
+      a[i + 1] = lo;
+    }
+  uint32_t m = 0;
+  for (int round = 0; round < 32 * V; ++round) {
+    m = __reduce_max_sync(0xffffffffu, a[0]);
+    const bool eq0 = a[0] == m;
+    const uint32_t b0 = __ballot_sync(0xffffffffu, eq0);
+    const bool dup = V > 1 && __any_sync(0xffffffffu, eq0 && a[V > 1 ? 1 : 0] == m);
+    int c;
+    if (!dup) {
+      c = __popc(b0);
+    } else {
+      int cl = 0;
+#pragma unroll
+      for (int i = 0; i < V; ++i) cl += a[i] == m ? 1 : 0;
+      c = __reduce_add_sync(0xffffffffu, cl);
+    }
+    if (c >= rank) break;
+    rank -= c;
+    // pop every copy of m: one branch-free shift, more only if a lane held duplicates
+#pragma unroll 1
+    for (int s = 0; s < (dup ? V : 1); ++s) {
+      const bool p = a[0] == m;
+#pragma unroll
+      for (int i = 0; i + 1 < V; ++i) a[i] = p ? a[i + 1] : a[i];
+      a[V - 1] = p ? 0u : a[V - 1];
+    }
+  }
+  return __uint_as_float(m);
 }
 
 // Quantize the warp's vector (format.quantize, format.py:67-88).
@@ -67,7 +127,11 @@ template <int BPL>
 OSCAR_DEVINL uint32_t quantize_vec(float (&x)[BPL][4], const bool (&act)[BPL], int clip_idx,
                                    uint8_t (&code)[BPL]) {
   if (clip_idx >= 0) {
-    const float thr = kth_abs<BPL>(x, act, clip_idx);
+    int n_act = 0;
+#pragma unroll
+    for (int j = 0; j < BPL; ++j) n_act += __popc(__ballot_sync(0xffffffffu, act[j])) * 4;
+    const float thr = (n_act - clip_idx <= 32) ? kth_abs_top<BPL>(x, act, n_act - clip_idx)
+                                               : kth_abs<BPL>(x, act, clip_idx);
 #pragma unroll
     for (int j = 0; j < BPL; ++j)
 #pragma unroll
@@ -312,20 +376,26 @@ __global__ void __launch_bounds__(128) write_step_kernel(const float* __restrict
                                                          int k_clip_idx, int v_clip_idx, StoreGeom g,
                                                          const int64_t* __restrict__ slots, StageArgs st) {
   pdl_release();
-  pdl_wait();
+  __shared__ int64_t s_slot[kFusedMaxTokens];
   __shared__ int s_seat[kFusedMaxTokens];  // -1: slot < 0
   __shared__ int s_qsl[kFusedMaxReqs + 1];
   __shared__ int s_seq[kFusedMaxReqs];
   const int tid = threadIdx.x, lane = tid & 31;
   const int nt = (int)n;
+  // The step's slot mapping and request lists are the engine's inputs: no
+  // kernel of this library writes them, so they are read while the launch in
+  // front (the rotation whose rows this kernel stores) is still running; only
+  // the rows wait for it.
   for (int t = tid; t < nt; t += blockDim.x) {
     const int64_t slot = slots[t];
     int64_t blk;
+    s_slot[t] = slot;
     s_seat[t] = slot < 0 ? -1 : (int)staging_seat(slot, st.bs, st.rows, &blk);
   }
   for (int r = tid; r <= st.num_req; r += blockDim.x) s_qsl[r] = st.qsl[r];
   for (int r = tid; r < st.num_req; r += blockDim.x) s_seq[r] = st.seqs[r];
   __syncthreads();
+  pdl_wait();
 
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -353,7 +423,7 @@ __global__ void __launch_bounds__(128) write_step_kernel(const float* __restrict
         const int64_t pos = seq - s_qsl[lo + 1] + tok;
         keep = (pos >= seq - st.recent) || (pos < st.sink_eff);
       }
-      if (!is_v && h == 0 && lane == 0) st.owner[seat] = keep ? slots[tok] / st.bs : -1;
+      if (!is_v && h == 0 && lane == 0) st.owner[seat] = keep ? s_slot[tok] / st.bs : -1;
       if (keep) {
         const float4* src = reinterpret_cast<const float4*>((is_v ? v_rot : k_rot) + vec * (int64_t)D);
         float4* dst = reinterpret_cast<float4*>((is_v ? st.stage_v : st.stage_k) + ((int64_t)seat * hk + h) * D);
@@ -367,7 +437,7 @@ __global__ void __launch_bounds__(128) write_step_kernel(const float* __restrict
     }
   }
   // the INT2 store of the same vectors (after the staging reads of this warp's rows)
-  store_tasks<BPL>(warp, nwarps, k_rot, v_rot, n, hk, D, k_clip_idx, v_clip_idx, g, slots);
+  store_tasks<BPL>(warp, nwarps, k_rot, v_rot, n, hk, D, k_clip_idx, v_clip_idx, g, s_slot);
 }
 
 }  // namespace oscar
