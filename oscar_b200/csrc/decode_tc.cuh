@@ -1,17 +1,20 @@
 // Decode / MTP attention over paged INT2 history on the 5th-generation tensor
 // cores: the tcgen05 + TMEM + TMA kernel.
 //
-// One CTA per SM = one (request, kv head, history split); 544 threads.
-//   warp 16, lane 0: TMA producer and MMA issuer.  The split's INT2 history
-//     arrives in 128-token stages through a 2-slot ring: K slot bytes [0:48)
-//     and [48:96), V slot bytes [0:48) and [16:64) of every token, four 2D
-//     tensor-map boxes per page whose 48-byte rows put the 8 tokens of a
-//     shared-memory wavefront on 8 distinct bank groups.
-//   warps 0-15: warp w serves tokens 32 (w % 4) .. + 31 (its TMEM lane
-//     quarter) in role q = w / 4: K dims [0, 128), K dims [128, 256), V dims
-//     [0, 128) or V dims [128, 256) of those tokens, and query rows
-//     [8 q, 8 q + 8) of their softmax.  The four roles of a scheduler wait on
-//     different buffers and overlap; no barrier spans the CTA inside a stage.
+// One CTA per SM = one (request, kv head, history split); 800 threads.
+//   warp 24: TMA producer and MMA issuer, an event loop over its three queues
+//     (QK, PV, TMA refills).  The split's INT2 history arrives in 128-token
+//     stages through a 2-slot ring: K slot bytes [0:48) and [48:96), V slot
+//     bytes [0:48) and [16:64) of every token, four 2D tensor-map boxes per
+//     page whose 48-byte rows put the 8 tokens of a shared-memory wavefront on
+//     8 distinct bank groups.
+//   warps 0-15 (dequant): warp w serves tokens 32 (w % 4) .. + 31 (its TMEM
+//     lane quarter) in role q = w / 4: K dims [0, 128), K dims [128, 256), V
+//     dims [0, 128) or V dims [128, 256) of those tokens.
+//   warps 16-23 (softmax): warp 16 + 4 hr + lq serves the tokens of lane
+//     quarter lq for query rows [16 hr, 16 hr + 16).
+//   Each role waits only on the buffers it touches; no barrier spans the CTA
+//   inside a stage.
 //
 // Staging window (owner[(blk % rows) * bs + off] == blk, backend.py:172-176):
 // staged positions inside the split's own range are masked in its INT2 stages
@@ -34,14 +37,14 @@
 //     in shared memory (K-major, loaded once).
 //   V -> fp16 values (the chain's values are fp16-exact) in a shared V^T tile
 //     (MN-major: dims contiguous per token).
-//   softmax: each thread loads its token's 8 scores from TMEM.  The running
+//   softmax: each thread loads its token's 16 scores from TMEM.  The running
 //     row maximum moves only when a score exceeds it by more than 15 (log2
 //     units): P = 2^(x - m) stays <= 2^15 in fp16, and O/l are rescaled on
 //     those stages only.  P^T goes to shared memory (MN-major).
 //   O^T += V^T P^T: two M = 128 dim halves, N = 32 rows, K = 16 tokens per
-//     instruction, accumulated in TMEM across the split.
-// The normalised partial (O, LSE) goes to the workspace;
-// decode_combine_kernel merges the splits with the causal current chunk.
+//     instruction, accumulated in TMEM across the split; L += 1 P^T beside it.
+// The normalised partial (O in fp16, LSE) goes to the workspace;
+// tc_combine_kernel merges the splits with the causal current chunk.
 //
 // Dim orders inside each 16-dim group: K columns (pairs of k elements) hold
 // dims (0,2) (1,3) (4,6) (5,7) (8,10) (9,11) (12,14) (13,15), so that the four
@@ -210,9 +213,13 @@ OSCAR_DEVINL float tc_unord(int k) { return __int_as_float(k >= 0 ? k : k ^ 0x7f
 
 // TMA of INT2 stage s into ring slot s & 1: four 48-byte boxes (K [0,48),
 // K [48,96), V [0,48), V [16,64)) of `rows` tokens per page of the stage, and
-// (with a staging window) the owner tags of the same seats by one bulk copy
+// (with a staging window) the owner tags of the same seats by one bulk copy.
+// `parts`: kTcBoxes (the boxes, and the transaction count of the whole stage),
+// kTcTags (the owner tags), or both.
+constexpr int kTcBoxes = 1, kTcTags = 2;
 OSCAR_DEVINL void tc_issue_stage(TcSmem& sm, const AttnArgs& a, int s, int lo, int hi, int bs_log2, int page0, int h,
-                                 const CUtensorMap* tmk, const CUtensorMap* tmv, uint32_t b_full) {
+                                 const CUtensorMap* tmk, const CUtensorMap* tmv, uint32_t b_full,
+                                 int parts = kTcBoxes | kTcTags) {
   const int bs = 1 << bs_log2;
   const int rows_box = min(bs, kTcStage);
   const int slot = s & 1;
@@ -221,18 +228,21 @@ OSCAR_DEVINL void tc_issue_stage(TcSmem& sm, const AttnArgs& a, int s, int lo, i
   const int pg_first = base >> bs_log2, pg_last = (end - 1) >> bs_log2;
   const uint32_t bar = b_full + 8 * slot;
   const bool tags = a.owner != nullptr;
-  tc::mbar_expect_tx(bar, (uint32_t)((pg_last - pg_first + 1) * rows_box * (4 * kTcRow + (tags ? 8 : 0))));
+  if (parts & kTcBoxes)
+    tc::mbar_expect_tx(bar, (uint32_t)((pg_last - pg_first + 1) * rows_box * (4 * kTcRow + (tags ? 8 : 0))));
   for (int pg = pg_first; pg <= pg_last; ++pg) {
     const int blk = sm.btab[pg - page0];
     const int off0 = (bs > kTcStage) ? base - (pg << bs_log2) : 0;
     const int row = (pg << bs_log2) + off0 - base;
     const int y = (blk << bs_log2) + off0;
     const int xk = (int)(h * a.ksh), xv = (int)(h * a.vsh);
-    tc::tma_load_2d(smem_u32(&sm.ka[slot][row][0]), tmk, xk, y, bar);
-    tc::tma_load_2d(smem_u32(&sm.kb[slot][row][0]), tmk, xk + 48, y, bar);
-    tc::tma_load_2d(smem_u32(&sm.va[slot][row][0]), tmv, xv, y, bar);
-    tc::tma_load_2d(smem_u32(&sm.vb[slot][row][0]), tmv, xv + 16, y, bar);
-    if (tags)
+    if (parts & kTcBoxes) {
+      tc::tma_load_2d(smem_u32(&sm.ka[slot][row][0]), tmk, xk, y, bar);
+      tc::tma_load_2d(smem_u32(&sm.kb[slot][row][0]), tmk, xk + 48, y, bar);
+      tc::tma_load_2d(smem_u32(&sm.va[slot][row][0]), tmv, xv, y, bar);
+      tc::tma_load_2d(smem_u32(&sm.vb[slot][row][0]), tmv, xv + 16, y, bar);
+    }
+    if (tags && (parts & kTcTags))
       tc::bulk_load(smem_u32(&sm.own[slot][row]), a.owner + (int64_t)(blk % (int)a.stage_rows) * bs + off0,
                     (uint32_t)rows_box * 8u, bar);
   }
@@ -381,15 +391,16 @@ __global__ void __maxnreg__(72)
   const uint32_t b_k = smem_u32(&sm.bar_k[0]), b_s = smem_u32(&sm.bar_s[0]), b_v = smem_u32(&sm.bar_v[0]),
                  b_p = smem_u32(&sm.bar_p[0]), b_pv = smem_u32(&sm.bar_pv[0]);
   const TcWait wait{&sm.abort};
-  // programmatic dependent launch: the launch and the index set-up above overlap
-  // the previous kernel (the staging write); every global read comes after this
-  pdl_wait();
 
-  // ---------------- prologue.  The producer warp sets up barriers, the page
-  // slice and TMEM and issues the first two INT2 stages' TMA at once;
-  // meanwhile the dequant warps load Q, scan this CTA's staged groups and
-  // locate the rows of its first staged stage.  Staged stages run first, so
-  // their fp32 loads overlap the TMA of the first INT2 stages.
+  // ---------------- prologue.  Programmatic dependent launch: this grid may
+  // start while the kernels in front of it (the write step, the rotation)
+  // still run.  Before waiting for them, the producer warp sets up barriers,
+  // TMEM and the page slice and issues the TMA boxes of the first two INT2
+  // stages: the block table is the engine's input and the history below the
+  // prefix was written by earlier steps, so none of it depends on those
+  // kernels.  After the wait: the owner tags (the write step updates them), Q
+  // (the rotation writes it) and the staged-group scan.  Staged stages run
+  // first, so their fp32 loads overlap the TMA of the first INT2 stages.
   if (warp == kTcProdWarp) {
     if (lane == 0) {
 #pragma unroll
@@ -417,7 +428,8 @@ __global__ void __maxnreg__(72)
     tc::tmem_relinquish();
     __syncwarp();
     if (tc::elect_one()) {
-      for (int s = 0; s < min(2, n_int); ++s) tc_issue_stage(sm, a, s, lo, hi, bs_log2, page0, h, &tmk, &tmv, b_full);
+      for (int s = 0; s < min(2, n_int); ++s)
+        tc_issue_stage(sm, a, s, lo, hi, bs_log2, page0, h, &tmk, &tmv, b_full, kTcBoxes);
     }
     __syncwarp();
   } else if (warp >= kTcDeqWarps) {
@@ -427,7 +439,15 @@ __global__ void __maxnreg__(72)
     if (st_tid < kTcQuarters * kTcRows) (&sm.mrow[0][0])[st_tid] = -INFINITY;
     for (int i = st_tid; i < (int)(sizeof(sm.pt) / 16); i += 32 * kTcSmWarps)
       reinterpret_cast<uint4*>(&sm.pt[0][0])[i] = make_uint4(0u, 0u, 0u, 0u);
-  } else {
+  }
+  pdl_wait();
+  if (warp == kTcProdWarp) {
+    if (a.owner != nullptr && tc::elect_one()) {
+      for (int s = 0; s < min(2, n_int); ++s)
+        tc_issue_stage(sm, a, s, lo, hi, bs_log2, page0, h, &tmk, &tmv, b_full, kTcTags);
+    }
+    __syncwarp();
+  } else if (warp < kTcDeqWarps) {
     if (tid < kTcRows) sm.lim[tid] = tid < R ? seq - qlen + tid / G + 1 : INT_MIN;
     // Q rows n < R, 16-dim word j: k-group 2j holds dims 16j + {0,2,1,3,4,6,5,7}, 2j+1 dims
     // 16j + {8,10,9,11,12,14,13,15} (the K column order); k-groups 32, 33 hold the bias
@@ -833,8 +853,10 @@ __global__ void __maxnreg__(72)
         bool need = false;
 #pragma unroll
         for (int i = 0; i < 16; ++i) need = need || (x[i] > mcur[i] + kTcHeadroom);
+        float alpha_l = 1.0f;  // lane i (and i + 16): the factor of row 16 hr + i
+        bool rescale = false;
         if (hr == 0 ? tc::bar_or(1, 128, need) : tc::bar_or(2, 128, need)) {
-          // new row maxima over the stage's 128 tokens; rescale O and L if they moved
+          // new row maxima over the stage's 128 tokens
 #pragma unroll
           for (int i = 0; i < 16; i += 4) {
             const int4 v4 = make_int4(__reduce_max_sync(0xffffffffu, tc_ord(x[i])),
@@ -844,12 +866,9 @@ __global__ void __maxnreg__(72)
             if (lane == 0) *reinterpret_cast<int4*>(&sm.red[lq][16 * hr + i]) = v4;
           }
           if (hr == 0) tc::bar_sync(1, 128); else tc::bar_sync(2, 128);
-          // (the scores and maxima are read again after the rescale: no registers held
-          // across it.  sm.red is rewritten only after the next vote, which every warp
-          // reaches after these reads)
-          // lane i (and i + 16) handles row 16 hr + i: its alpha (the O / L columns fetch
-          // it by shuffle) and this warp's copy of its new maximum
-          float alpha_l;
+          // lane i (and i + 16) handles row 16 hr + i: its factor alpha (the O / L columns
+          // fetch it by shuffle) and this warp's copy of its new maximum.  (sm.red is
+          // rewritten only after the next vote, which every warp reaches after these reads.)
           {
             const int rl = 16 * hr + (lane & 15);
             const float mold = sm.mrow[lq][rl];
@@ -862,41 +881,41 @@ __global__ void __maxnreg__(72)
             if (lane < 16) sm.mrow[lq][rl] = mnew;
             __syncwarp();
           }
-          if (st > 0 && __any_sync(0xffffffffu, alpha_l != 1.0f)) {
-            // O holds every PV before stage st once the PV of stage st - 1 is done
-            wait(b_pv + 8 * (b ^ 1), ((st - 1) >> 1) & 1);
-            tc::tc_fence_after();
-#pragma unroll
-            for (int hh = 0; hh < 3; ++hh) {
-              // O dims [0, 128), [128, 256), then L
-              const uint32_t col = tmem + lane_base + (hh < 2 ? kTcColO + 32 * hh : kTcColL) + 16 * hr;
-              uint32_t o[16];
-              tc::tmem_ld16(col, o);
-              tc::tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 16; ++i)
-                o[i] = __float_as_uint(__uint_as_float(o[i]) * __shfl_sync(0xffffffffu, alpha_l, i));
-              tc::tmem_st16(col, o);
-            }
-            tc::tmem_wait_st();
-          }
+          rescale = st > 0 && __any_sync(0xffffffffu, alpha_l != 1.0f);
           load_m(mcur);
-          load_x(x);
         }
-        // P^T[b] (fp16) rows 16 hr .. 16 hr + 15 and l
+        // P^T[b] (fp16) rows 16 hr .. 16 hr + 15
         uint32_t pk[8];
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
           const float mu0 = (mcur[i] == -INFINITY) ? 0.0f : mcur[i];
           const float mu1 = (mcur[i + 1] == -INFINITY) ? 0.0f : mcur[i + 1];
-          x[i] = tc_exp2(x[i] - mu0);
-          x[i + 1] = tc_exp2(x[i + 1] - mu1);
-          const __half2 ph = __floats2half2_rn(x[i], x[i + 1]);
+          const __half2 ph = __floats2half2_rn(tc_exp2(x[i] - mu0), tc_exp2(x[i + 1] - mu1));
           pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&ph);
         }
         uint8_t* pt = sm.pt[b] + pt_off + (2 * hr) * kTcVtSbo;
         *reinterpret_cast<uint4*>(pt) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         *reinterpret_cast<uint4*>(pt + kTcVtSbo) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        if (rescale) {
+          // O and L hold every PV before stage st once the PV of stage st - 1 is done;
+          // this stage's P is already written, so that wait overlaps its computation.
+          // The PV of stage st waits for this warp's arrival below.
+          wait(b_pv + 8 * (b ^ 1), ((st - 1) >> 1) & 1);
+          tc::tc_fence_after();
+#pragma unroll
+          for (int hh = 0; hh < 3; ++hh) {
+            // O dims [0, 128), [128, 256), then L
+            const uint32_t col = tmem + lane_base + (hh < 2 ? kTcColO + 32 * hh : kTcColL) + 16 * hr;
+            uint32_t o[16];
+            tc::tmem_ld16(col, o);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              o[i] = __float_as_uint(__uint_as_float(o[i]) * __shfl_sync(0xffffffffu, alpha_l, i));
+            tc::tmem_st16(col, o);
+          }
+          tc::tmem_wait_st();
+        }
       }
       // S[b] is read: free it for the QK of stage st + 2; P^T[b] is written
       tc::tc_fence_before();

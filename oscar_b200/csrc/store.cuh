@@ -179,11 +179,20 @@ OSCAR_DEVINL uint32_t quantize_vec(float (&x)[BPL][4], const bool (&act)[BPL], i
 // One warp per (token, kv head, K or V): the K and V halves of a vector are
 // quantized by two warps at once (warp 2 v + 0 writes the K codes and the K
 // scale/zero bytes [0:4] of the K slot, warp 2 v + 1 the V codes and [4:8]).
-// Warps warp0, warp0 + nwarps, ... of the task list.
-template <int BPL>
+// Warps warp0, warp0 + nwarps, ... of the task list.  `pre(tok, h, is_v, x,
+// act)` runs on every task with a slot >= 0 once the row is in registers (lane
+// holds floats 4 (lane + 32 j) .. + 3), before the block check and the
+// quantisation: the write step stages the same row from there.
+struct NoPre {
+  template <int BPL>
+  OSCAR_DEVINL void operator()(int64_t, int, bool, const float (&)[BPL][4], const bool (&)[BPL]) const {}
+};
+
+template <int BPL, typename Pre = NoPre>
 OSCAR_DEVINL void store_tasks(int64_t warp0, int64_t nwarps, const float* __restrict__ k_rot,
                               const float* __restrict__ v_rot, int64_t n, int hk, int D, int k_clip_idx,
-                              int v_clip_idx, const StoreGeom& g, const int64_t* __restrict__ slots) {
+                              int v_clip_idx, const StoreGeom& g, const int64_t* __restrict__ slots,
+                              const Pre& pre = Pre()) {
   const int NB = D / 4;  // code bytes per vector; BPL = code bytes per lane (1 or 2)
   const int lane = threadIdx.x & 31;
   const int bs_log2 = (g.block_size & (g.block_size - 1)) == 0 ? __ffs(g.block_size) - 1 : -1;
@@ -204,18 +213,6 @@ OSCAR_DEVINL void store_tasks(int64_t warp0, int64_t nwarps, const float* __rest
     }
     const int64_t slot = slots[tok];
     if (slot < 0) continue;
-    int64_t blk, off;
-    if (bs_log2 >= 0) {
-      blk = slot >> bs_log2;
-      off = slot & (g.block_size - 1);
-    } else {
-      blk = slot / g.block_size;
-      off = slot - blk * g.block_size;
-    }
-    if (blk >= g.num_blocks) {
-      if (lane == 0 && !is_v) flag_error(1u);
-      continue;
-    }
     const float* src = (is_v ? v_rot : k_rot) + vec * (int64_t)D;
     float x[BPL][4];
     bool act[BPL];
@@ -230,6 +227,19 @@ OSCAR_DEVINL void store_tasks(int64_t warp0, int64_t nwarps, const float* __rest
 #pragma unroll
         for (int e = 0; e < 4; ++e) x[j][e] = 0.0f;
       }
+    }
+    pre(tok, h, is_v, x, act);
+    int64_t blk, off;
+    if (bs_log2 >= 0) {
+      blk = slot >> bs_log2;
+      off = slot & (g.block_size - 1);
+    } else {
+      blk = slot / g.block_size;
+      off = slot - blk * g.block_size;
+    }
+    if (blk >= g.num_blocks) {
+      if (lane == 0 && !is_v) flag_error(1u);
+      continue;
     }
     uint8_t code[BPL];
     const uint32_t meta = quantize_vec<BPL>(x, act, is_v ? v_clip_idx : k_clip_idx, code);
@@ -399,45 +409,38 @@ __global__ void __launch_bounds__(128) write_step_kernel(const float* __restrict
 
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t task = warp; task < 2 * n * hk; task += nwarps) {
-    const int64_t vec = task >> 1;
-    const bool is_v = (task & 1) != 0;
-    const int tok = (int)(vec / hk), h = (int)(vec - (int64_t)tok * hk);
+  // staging, from the row the store just loaded: the seat's last writer among
+  // the step's tokens (later tokens with the same seat win) writes the row if
+  // its position is kept by the window, and head 0's K warp sets the owner tag
+  auto stage = [&](int64_t tok64, int h, bool is_v, const float (&x)[BPL][4], const bool (&act)[BPL]) {
+    const int tok = (int)tok64;
     const int seat = s_seat[tok];
-    if (seat < 0) continue;
-    // staging: the seat's last writer among the step's tokens (stable sort + last of run)
     bool later = false;
     for (int u0 = tok + 1; u0 < nt; u0 += 32) {
       const int u = u0 + lane;
       later = later || (u < nt && s_seat[u] == seat);
     }
-    if (!__any_sync(0xffffffffu, later)) {
-      int lo = 0, hi = st.num_req;  // the last r with qsl[r] <= tok
-      while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (s_qsl[mid] <= tok) lo = mid; else hi = mid;
-      }
-      bool keep = false;
-      if (st.num_req > 0 && s_qsl[lo] <= tok && tok < s_qsl[lo + 1]) {
-        const int64_t seq = s_seq[lo];
-        const int64_t pos = seq - s_qsl[lo + 1] + tok;
-        keep = (pos >= seq - st.recent) || (pos < st.sink_eff);
-      }
-      if (!is_v && h == 0 && lane == 0) st.owner[seat] = keep ? s_slot[tok] / st.bs : -1;
-      if (keep) {
-        const float4* src = reinterpret_cast<const float4*>((is_v ? v_rot : k_rot) + vec * (int64_t)D);
-        float4* dst = reinterpret_cast<float4*>((is_v ? st.stage_v : st.stage_k) + ((int64_t)seat * hk + h) * D);
-        float4 x[2];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) x[j] = (lane + 32 * j < D / 4) ? src[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-          if (lane + 32 * j < D / 4) dst[lane + 32 * j] = x[j];
-      }
+    if (__any_sync(0xffffffffu, later)) return;
+    int lo = 0, hi = st.num_req;  // the last r with qsl[r] <= tok
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_qsl[mid] <= tok) lo = mid; else hi = mid;
     }
-  }
-  // the INT2 store of the same vectors (after the staging reads of this warp's rows)
-  store_tasks<BPL>(warp, nwarps, k_rot, v_rot, n, hk, D, k_clip_idx, v_clip_idx, g, s_slot);
+    bool keep = false;
+    if (st.num_req > 0 && s_qsl[lo] <= tok && tok < s_qsl[lo + 1]) {
+      const int64_t seq = s_seq[lo];
+      const int64_t pos = seq - s_qsl[lo + 1] + tok;
+      keep = (pos >= seq - st.recent) || (pos < st.sink_eff);
+    }
+    if (!is_v && h == 0 && lane == 0) st.owner[seat] = keep ? s_slot[tok] / st.bs : -1;
+    if (keep) {
+      float4* dst = reinterpret_cast<float4*>((is_v ? st.stage_v : st.stage_k) + ((int64_t)seat * hk + h) * D);
+#pragma unroll
+      for (int j = 0; j < BPL; ++j)
+        if (act[j]) dst[lane + 32 * j] = make_float4(x[j][0], x[j][1], x[j][2], x[j][3]);
+    }
+  };
+  store_tasks<BPL>(warp, nwarps, k_rot, v_rot, n, hk, D, k_clip_idx, v_clip_idx, g, s_slot, stage);
 }
 
 }  // namespace oscar

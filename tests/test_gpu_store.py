@@ -57,6 +57,45 @@ def test_store_with_clip_bit_exact_vs_oracle(d, hk, kclip, vclip):
     assert np.array_equal(vc.cpu().numpy(), ev)
 
 
+@pytest.mark.parametrize("d", [256, 64])
+def test_store_clip_with_tied_magnitudes_at_the_top_vs_oracle(d):
+    """Clip thresholds near the top of |x| are selected by a warp tournament;
+    ties at the top (the same |x| in several lanes, and twice in one lane, of
+    either sign) must count with their multiplicity, at every rank around the
+    tied run."""
+    from oscar_b200 import kernels
+
+    dev = need_gpu()
+    rng = np.random.default_rng(90 + d)
+    rows = []
+    for t in range(24):
+        x = rng.standard_normal(d).astype(np.float32)
+        top = rng.choice(d, size=9, replace=False)
+        x[top[:5]] = 3.0
+        x[top[5:]] = -3.0
+        x[(top[0] // 4) * 4 + (top[0] + 1) % 4] = -3.0  # a second copy in the lane holding top[0]
+        if t % 3 == 1:
+            x[top[:2]] = 7.5  # a tied run above the first one
+        if t % 3 == 2:
+            x[:] = np.float32(-2.0)  # every |x| equal
+        rows.append(x)
+    k = np.stack(rows)[:, None, :]
+    v = -k
+    n, bs, nb = k.shape[0], 16, 4
+    slots = np.arange(n, dtype=np.int64)
+    for ratio in (0.96, 0.95, 0.962, 0.97, 0.99, 0.92, 0.88):
+        k8 = np.zeros((nb, bs, 1, d), dtype=np.uint8)
+        v8 = np.zeros_like(k8)
+        ek, ev = k8.copy(), v8.copy()
+        orc.store(orc.clip_only(k, ratio), orc.clip_only(v, ratio), ek, ev, slots)
+        kc = torch.from_numpy(k8).to(dev)
+        vc = torch.from_numpy(v8).to(dev)
+        kernels.oscar_store(torch.from_numpy(k).to(dev), torch.from_numpy(v).to(dev), kc, vc,
+                            torch.from_numpy(slots).to(dev), ratio, ratio)
+        assert np.array_equal(kc.cpu().numpy(), ek), ratio
+        assert np.array_equal(vc.cpu().numpy(), ev), ratio
+
+
 def test_store_clip_golden_rotate_clip(golden):
     """Rotated input from the reference's _rotate_clip: the kernel's in-kernel
     clip of the unclipped rotation equals storing the reference's clipped rows."""

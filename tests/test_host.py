@@ -204,3 +204,18 @@ def test_synthetic_case_shapes_follow_probe_make_case():
     assert set(BASELINE_CONFIGS) == {"cfg1_mtp_8k", "cfg2_mtp_24k", "cfg3_mtp_8x24k", "cfg4_continuation", "cfg5_mixed_64"}
     lengths = BASELINE_CONFIGS["cfg5_mixed_64"]["prefixes"]
     assert len(lengths) == 64 and min(lengths) >= 1024 and max(lengths) <= 32768
+
+
+def test_graph_wrappers_reject_host_tensors_and_empty_sequences():
+    """CUDA-graph wrappers need device tensors; a sequence needs a forward."""
+    import torch
+
+    from oscar_b200.graphs import GraphedForward, GraphedSequence
+
+    q = torch.zeros(1, 6, 256)
+    with pytest.raises(ValueError):
+        GraphedSequence([])
+    with pytest.raises(ValueError):
+        GraphedSequence([(None, None, q, q, q, None, None, q)])
+    with pytest.raises(ValueError):
+        GraphedForward(None, None, q, q, q, None, None, q)
