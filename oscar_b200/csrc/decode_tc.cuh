@@ -992,16 +992,19 @@ __global__ void __maxnreg__(72)
 // Merge of the splits (_merge_slab, slab_attention.py:156-194, joint form)
 // with the causal current chunk: one warp per query row, lane l owning dims
 // 8 l .. 8 l + 7, two rows per CTA, no block-wide barrier.  Launched as a
-// programmatic dependent of decode_tc_kernel: its CTAs fit beside an
-// attention CTA on an SM, score the current chunk while the attention grid
-// runs, then wait for it and read the splits' LSEs and fp16 partials (in
-// batches of eight 16-byte loads).
-constexpr int kTcCombineWarps = 2;  // 64 threads x <= 128 registers: fits beside an attention CTA
+// programmatic dependent of decode_tc_kernel: its CTAs start on SMs the
+// attention grid leaves free (or has left), score the current chunk while the
+// attention runs, then wait for it and read the splits' LSEs and fp16
+// partials (up to 24 splits in one round of 16-byte loads, later ones in
+// rounds of eight).
+constexpr int kTcCombineWarps = 2;  // 64 threads per CTA
 
 template <typename T>
 __global__ void __launch_bounds__(32 * kTcCombineWarps)
     tc_combine_kernel(const AttnArgs a, const __grid_constant__ AttnPlan p) {
-  constexpr int D = 256, kMaxKeys = 32, kBatch = 8;
+  // kFirst: partial rows loaded in the first round, enough for every split of a
+  // history spread over the whole GPU (144 CTAs over >= 6 requests); kBatch: later rounds
+  constexpr int D = 256, kMaxKeys = 32, kBatch = 8, kFirst = 24;
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * kTcCombineWarps + (threadIdx.x >> 5);
   const int per_req = a.hk * kTcRows;
@@ -1062,7 +1065,7 @@ __global__ void __launch_bounds__(32 * kTcCombineWarps)
   // (programmatic dependent launch: this grid may start while that one runs)
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
   // one round of loads: every split's LSE (lane i % 32) and the first
-  // kBatch * 2 partial rows, then the maximum (NaN propagates) and weights
+  // kFirst partial rows, then the maximum (NaN propagates) and weights
   float acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
@@ -1070,9 +1073,9 @@ __global__ void __launch_bounds__(32 * kTcCombineWarps)
   for (int i32 = 0; i32 < np; i32 += 32) {
     const int nb = min(32, np - i32);
     const float ls = (lane < nb) ? __ldcg(a.part_lse + prow_of(i32 + lane)) : -INFINITY;
-    uint4 ou[2 * kBatch];
+    uint4 ou[kFirst];
 #pragma unroll
-    for (int u = 0; u < 2 * kBatch; ++u)
+    for (int u = 0; u < kFirst; ++u)
       ou[u] = (u < nb) ? __ldcg(reinterpret_cast<const uint4*>(po + prow_of(i32 + u) * D + 8 * lane))
                        : make_uint4(0u, 0u, 0u, 0u);
     float mx = (i32 == 0) ? kscore : -INFINITY;
@@ -1093,14 +1096,14 @@ __global__ void __launch_bounds__(32 * kTcCombineWarps)
     const float w = (lane < nb && ls != -INFINITY) ? expf(ls - Mu) : 0.0f;
     lsum += w;
 #pragma unroll
-    for (int u = 0; u < 2 * kBatch; ++u) {
+    for (int u = 0; u < kFirst; ++u) {
       const float wu = __shfl_sync(0xffffffffu, w, u);
       if (u >= nb) break;
       const __half* hv = reinterpret_cast<const __half*>(&ou[u]);
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[e] = fmaf(wu, __half2float(hv[e]), acc[e]);
     }
-    for (int b0 = 2 * kBatch; b0 < nb; b0 += kBatch) {
+    for (int b0 = kFirst; b0 < nb; b0 += kBatch) {
       uint4 ob[kBatch];
 #pragma unroll
       for (int u = 0; u < kBatch; ++u)
