@@ -440,6 +440,21 @@ __global__ void __maxnreg__(72)
     for (int i = st_tid; i < (int)(sizeof(sm.pt) / 16); i += 32 * kTcSmWarps)
       reinterpret_cast<uint4*>(&sm.pt[0][0])[i] = make_uint4(0u, 0u, 0u, 0u);
   }
+  // dequant warps: the block-table entries of this CTA's staged-group scan (first
+  // batch: groups k = warp + 16 u), an engine input read before the wait
+  constexpr int kScanPer = 4;
+  int gblk[kScanPer];
+  bool ghit[kScanPer];
+#pragma unroll
+  for (int u = 0; u < kScanPer; ++u) {
+    gblk[u] = -1;
+    ghit[u] = false;
+    const int k = warp + u * kWarps, pos = (sp + k * nsplit) * 32 + lane;
+    if (warp < kTcDeqWarps && a.owner != nullptr && k < ngroups && pos < prefix) {
+      gblk[u] = a.bt[(int64_t)req * a.bt_stride + (pos >> bs_log2)];
+      if (gblk[u] >= a.num_blocks) gblk[u] = -1;
+    }
+  }
   pdl_wait();
   if (warp == kTcProdWarp) {
     if (a.owner != nullptr && tc::elect_one()) {
@@ -451,49 +466,27 @@ __global__ void __maxnreg__(72)
     if (tid < kTcRows) sm.lim[tid] = tid < R ? seq - qlen + tid / G + 1 : INT_MIN;
     // Q rows n < R, 16-dim word j: k-group 2j holds dims 16j + {0,2,1,3,4,6,5,7}, 2j+1 dims
     // 16j + {8,10,9,11,12,14,13,15} (the K column order); k-groups 32, 33 hold the bias
-    // column: 1 at k = 256, zeros after
-    for (int u = tid; u < kTcRows * 17; u += kTcCompute) {
-      const int n = u / 17, j = u - 17 * (u / 17);
-      uint4 ev = make_uint4(0, 0, 0, 0), od = ev;
-      if (j == 16) {
-        ev.x = (uint32_t)(std::is_same<T, __nv_bfloat16>::value ? 0x3F80u : 0x3C00u);  // 1.0 in T
-      } else if (n < R) {
+    // column: 1 at k = 256, zeros after.  Items u = tid, tid + 512: their loads and the
+    // owner tags of the scan's first batch go out in one round.
+    constexpr int kQItems = (kTcRows * 17 + kTcCompute - 1) / kTcCompute;
+    uint4 qraw[kQItems][2];
+#pragma unroll
+    for (int i = 0; i < kQItems; ++i) {
+      const int u = tid + i * kTcCompute, n = u / 17, j = u - 17 * (u / 17);
+      qraw[i][0] = qraw[i][1] = make_uint4(0, 0, 0, 0);
+      if (u < kTcRows * 17 && j < 16 && n < R) {
         const T* qrow =
             reinterpret_cast<const T*>(a.q) + ((int64_t)(q_start + n / G) * a.hq + (int64_t)h * G + n % G) * D;
-        const uint4 q0 = *reinterpret_cast<const uint4*>(qrow + 16 * j);
-        const uint4 q1 = *reinterpret_cast<const uint4*>(qrow + 16 * j + 8);
-        ev = make_uint4(prmt(q0.x, q0.y, 0x5410u), prmt(q0.x, q0.y, 0x7632u), prmt(q0.z, q0.w, 0x5410u),
-                        prmt(q0.z, q0.w, 0x7632u));
-        od = make_uint4(prmt(q1.x, q1.y, 0x5410u), prmt(q1.x, q1.y, 0x7632u), prmt(q1.z, q1.w, 0x5410u),
-                        prmt(q1.z, q1.w, 0x7632u));
+        qraw[i][0] = *reinterpret_cast<const uint4*>(qrow + 16 * j);
+        qraw[i][1] = *reinterpret_cast<const uint4*>(qrow + 16 * j + 8);
       }
-      uint8_t* dst = sm.qb + (n >> 3) * kTcQSbo + (2 * j) * 128 + (n & 7) * 16;
-      *reinterpret_cast<uint4*>(dst) = ev;
-      *reinterpret_cast<uint4*>(dst + 128) = od;
     }
     // this CTA's groups of the whole request, g = sp + k * nsplit: up to four per
-    // warp (block-table loads first, then the owner tags), kept in registers until
+    // warp (block-table entries first, then the owner tags), kept in registers until
     // the prefix counts give each staged position its index j; the first staged
     // stage's rows and positions (j < 128) then go to srow / spos
-    constexpr int kScanPer = 4;
     const bool scan_all = ngroups <= kScanPer * kWarps;
-    int gblk[kScanPer];
-    bool ghit[kScanPer];
-#pragma unroll
-    for (int u = 0; u < kScanPer; ++u) {
-      gblk[u] = -1;
-      ghit[u] = false;
-    }
-    for (int k0 = warp; k0 < ngroups; k0 += kScanPer * kWarps) {
-#pragma unroll
-      for (int u = 0; u < kScanPer; ++u) {
-        const int k = k0 + u * kWarps, pos = (sp + k * nsplit) * 32 + lane;
-        gblk[u] = -1;
-        if (a.owner != nullptr && k < ngroups && pos < prefix) {
-          gblk[u] = a.bt[(int64_t)req * a.bt_stride + (pos >> bs_log2)];
-          if (gblk[u] >= a.num_blocks) gblk[u] = -1;
-        }
-      }
+    auto scan_tags = [&](int k0) {
       int64_t tag[kScanPer];
 #pragma unroll
       for (int u = 0; u < kScanPer; ++u) {
@@ -507,6 +500,38 @@ __global__ void __maxnreg__(72)
         const uint32_t bits = __ballot_sync(0xffffffffu, ghit[u]);
         if (lane == 0 && k < ngroups) sm.gmask[k] = bits;
       }
+    };
+    if (warp < ngroups) scan_tags(warp);
+#pragma unroll
+    for (int i = 0; i < kQItems; ++i) {
+      const int u = tid + i * kTcCompute, n = u / 17, j = u - 17 * (u / 17);
+      if (u >= kTcRows * 17) break;
+      uint4 ev = make_uint4(0, 0, 0, 0), od = ev;
+      if (j == 16) {
+        ev.x = (uint32_t)(std::is_same<T, __nv_bfloat16>::value ? 0x3F80u : 0x3C00u);  // 1.0 in T
+      } else {
+        const uint4 q0 = qraw[i][0], q1 = qraw[i][1];
+        ev = make_uint4(prmt(q0.x, q0.y, 0x5410u), prmt(q0.x, q0.y, 0x7632u), prmt(q0.z, q0.w, 0x5410u),
+                        prmt(q0.z, q0.w, 0x7632u));
+        od = make_uint4(prmt(q1.x, q1.y, 0x5410u), prmt(q1.x, q1.y, 0x7632u), prmt(q1.z, q1.w, 0x5410u),
+                        prmt(q1.z, q1.w, 0x7632u));
+      }
+      uint8_t* dst = sm.qb + (n >> 3) * kTcQSbo + (2 * j) * 128 + (n & 7) * 16;
+      *reinterpret_cast<uint4*>(dst) = ev;
+      *reinterpret_cast<uint4*>(dst + 128) = od;
+    }
+    // later batches (histories with more groups than one pass holds)
+    for (int k0 = warp + kScanPer * kWarps; k0 < ngroups; k0 += kScanPer * kWarps) {
+#pragma unroll
+      for (int u = 0; u < kScanPer; ++u) {
+        const int k = k0 + u * kWarps, pos = (sp + k * nsplit) * 32 + lane;
+        gblk[u] = -1;
+        if (a.owner != nullptr && k < ngroups && pos < prefix) {
+          gblk[u] = a.bt[(int64_t)req * a.bt_stride + (pos >> bs_log2)];
+          if (gblk[u] >= a.num_blocks) gblk[u] = -1;
+        }
+      }
+      scan_tags(k0);
     }
     if (tid < kTcStage) {
       sm.srow[tid] = -1;
