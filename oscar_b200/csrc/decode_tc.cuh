@@ -973,6 +973,15 @@ __global__ void __maxnreg__(72)
 #pragma unroll
         for (int i = 0; i < 16; ++i) L[i] = __uint_as_float(lr[i]);
       }
+      // normalised O in fp16 (the merge reads it once; 2^-11 relative is far inside the
+      // output tolerance), zero for empty rows: one fast reciprocal per row (2 ulp of fp32,
+      // far below the fp16 rounding), the rows staged
+      // in shared memory (the P^T buffers, free once the last PV is done) so that they
+      // leave in 16-byte pieces below
+      float rinv[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) rinv[i] = (L[i] > 0.0f || L[i] != L[i]) ? __fdividef(1.0f, L[i]) : 0.0f;
+      __half* so = reinterpret_cast<__half*>(&sm.pt[0][0]);  // [32 rows][256 dims]
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         uint32_t o[16];
@@ -982,16 +991,10 @@ __global__ void __maxnreg__(72)
           tc::tmem_ld16(tmem + lane_base + kTcColO + 32 * hh + 16 * hr, o);
           tc::tmem_wait_ld();
         }
-        // normalised O in fp16 (the merge reads it once; 2^-11 relative is far inside the
-        // output tolerance), zero for empty rows
         const int dim = tc_dim(128 * hh + tok);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int r = 16 * hr + i;
-          if (r >= R) continue;
-          const bool keep = L[i] > 0.0f || L[i] != L[i];
-          po[(prow0 + r) * D + dim] = __float2half_rn(keep ? __uint_as_float(o[i]) / L[i] : 0.0f);
-        }
+        for (int i = 0; i < 16; ++i)
+          so[(16 * hr + i) * D + dim] = __float2half_rn(rinv[i] != 0.0f ? __uint_as_float(o[i]) * rinv[i] : 0.0f);
       }
       if (lq == 0 && lane < 16 && 16 * hr + lane < R) {
         float Li = 0.0f, mi = 0.0f;
@@ -1003,6 +1006,16 @@ __global__ void __maxnreg__(72)
           }
         a.part_lse[prow0 + 16 * hr + lane] =
             (Li > 0.0f || Li != Li) ? (mi + log2f(Li)) * 0.69314718055994531f : -INFINITY;
+      }
+    }
+    // the staged rows r < R, 512 contiguous bytes each, by all softmax threads
+    tc::bar_sync(3, 32 * kTcSmWarps);
+    {
+      const int st_tid = tid - kTcCompute;
+      const uint4* so4 = reinterpret_cast<const uint4*>(&sm.pt[0][0]);
+      for (int idx = st_tid; idx < R * (D / 8); idx += 32 * kTcSmWarps) {
+        const int r = idx / (D / 8), c = idx - r * (D / 8);
+        *reinterpret_cast<uint4*>(po + (prow0 + r) * D + 8 * c) = so4[idx];
       }
     }
   }
