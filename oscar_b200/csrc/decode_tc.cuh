@@ -1192,8 +1192,9 @@ __global__ void __launch_bounds__(32 * kTcCombineWarps)
   for (int o2 = 16; o2 > 0; o2 >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o2);
   const float den = (lsum > 0.0f || lsum != lsum) ? lsum : 1.0f;
   float4* dst = reinterpret_cast<float4*>(a.out + qrow * D + 8 * lane);
-  dst[0] = make_float4(acc[0] / den, acc[1] / den, acc[2] / den, acc[3] / den);
-  dst[1] = make_float4(acc[4] / den, acc[5] / den, acc[6] / den, acc[7] / den);
+  const float rden = __fdividef(1.0f, den);  // one fast reciprocal (2 ulp) for the row's 8 values
+  dst[0] = make_float4(acc[0] * rden, acc[1] * rden, acc[2] * rden, acc[3] * rden);
+  dst[1] = make_float4(acc[4] * rden, acc[5] * rden, acc[6] * rden, acc[7] * rden);
   if (lane == 0) a.lse[qrow] = (mx == -INFINITY) ? -INFINITY : Mu + logf(den);
 }
 
