@@ -325,14 +325,27 @@ Planned plan_batch(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1, int r
   return out;
 }
 
-int attn_target(int d, int nw) {
-  const int sms = device_info().sms;
-  if (d == 256) return sms * (nw == 2 ? attn_ctas_per_sm<256, __nv_bfloat16, 2>() : attn_ctas_per_sm<256, __nv_bfloat16, 4>());
-  if (d == 128) return sms * (nw == 2 ? attn_ctas_per_sm<128, __nv_bfloat16, 2>() : attn_ctas_per_sm<128, __nv_bfloat16, 4>());
-  return sms * (nw == 2 ? attn_ctas_per_sm<64, __nv_bfloat16, 2>() : attn_ctas_per_sm<64, __nv_bfloat16, 4>());
+template <int D>
+int attn_ctas_per_sm_nw(int nw) {
+  if (nw == 2) return attn_ctas_per_sm<D, __nv_bfloat16, 2>();
+  if (nw == 8) return attn_ctas_per_sm<D, __nv_bfloat16, 8>();
+  return attn_ctas_per_sm<D, __nv_bfloat16, 4>();
 }
 
-inline int rows_for(int max_q, int group) { return ((int64_t)max_q * group <= 32 && group <= 32) ? 32 : 64; }
+int attn_target(int d, int nw) {
+  const int sms = device_info().sms;
+  if (d == 256) return sms * attn_ctas_per_sm_nw<256>(nw);
+  if (d == 128) return sms * attn_ctas_per_sm_nw<128>(nw);
+  return sms * attn_ctas_per_sm_nw<64>(nw);
+}
+
+// query rows per tile-kernel CTA: 32 for decode-sized blocks, 128 (eight warps) for
+// continuation / prefill blocks of at least 512 rows, 64 otherwise
+inline int rows_for(int max_q, int group) {
+  const int64_t rows = (int64_t)max_q * group;
+  if (rows <= 32 && group <= 32) return 32;
+  return rows >= 512 ? 128 : 64;
+}
 
 template <int D, typename T, int NW>
 int run_attention(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs, void* workspace,
@@ -599,6 +612,7 @@ template <int D, typename T>
 int dispatch_rows(const oscar::AttnArgs& a, const std::vector<ReqInfo>& reqs, int max_q, void* ws, int64_t wsb,
                   cudaStream_t s) {
   if (rows_for(max_q, a.group) == 32) return run_attention<D, T, 2>(a, reqs, ws, wsb, s);
+  if (rows_for(max_q, a.group) == 128) return run_attention<D, T, 8>(a, reqs, ws, wsb, s);
   return run_attention<D, T, 4>(a, reqs, ws, wsb, s);
 }
 
