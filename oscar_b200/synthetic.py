@@ -132,3 +132,59 @@ BASELINE_CONFIGS = {
     "cfg5_mixed_64": dict(prefixes=lognormal_lengths(64, 5), lengths=[1 + (i * 7) % 4 for i in range(64)], hk=4,
                           group=6),
 }
+
+
+def attention_flops(prefixes, lengths, hq: int, d: int) -> float:
+    """Algorithmic FLOPs of one slab attention pass: 4 Hq D per (query, key)
+    pair, over each request's history (N x C) and causal current chunk
+    (N (N + 1) / 2)."""
+    pairs = sum(n * c + n * (n + 1) // 2 for c, n in zip(prefixes, lengths))
+    return 4.0 * hq * d * pairs
+
+
+def _run(name: str, calls: int, lengths_override: int | None) -> None:
+    """Time ``slab_attention`` on one BASELINE configuration on cuda:0 (CUDA
+    events around ``calls`` back-to-back calls after two warm-up calls) and
+    print one JSON line with the algorithmic TFLOP/s; the committed runner of
+    the continuation profiles."""
+    import json
+    from pathlib import Path
+
+    from . import kernels
+
+    spec = dict(BASELINE_CONFIGS[name])
+    if lengths_override:
+        spec["lengths"] = [lengths_override] * len(spec["lengths"])
+    dev = torch.device("cuda", 0)
+    case = make_case(spec["prefixes"], spec["lengths"], hk=spec["hk"], group=spec["group"], device=dev)
+    fill_caches(case)
+    args = (case.q, case.k_new, case.v_new, case.kc, case.vc, case.bt, case.qsl, case.seqs, case.scale, case.stage)
+    for _ in range(2):
+        kernels.slab_attention(*args)
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(calls):
+        kernels.slab_attention(*args)
+    end.record()
+    torch.cuda.synchronize(dev)
+    ms = start.elapsed_time(end) / calls
+    hq = spec["hk"] * spec["group"]
+    flops = attention_flops(spec["prefixes"], spec["lengths"], hq, case.q.shape[-1])
+    peaks = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
+    peak = json.loads(peaks.read_text()).get("bf16_tflops") if peaks.exists() else None
+    tflops = flops / (ms * 1e-3) / 1e12
+    print(json.dumps({"workload": name, "lengths": spec["lengths"][:4], "ms_per_call": ms, "tflops": tflops,
+                      "peak_bf16_tflops": peak, "frac": tflops / peak if peak else None,
+                      "device_error": kernels.device_error(dev)}), flush=True)
+
+
+if __name__ == "__main__":
+    import argparse
+
+    ap = argparse.ArgumentParser(description="time slab_attention on a BASELINE configuration")
+    ap.add_argument("--run", required=True, choices=sorted(BASELINE_CONFIGS))
+    ap.add_argument("--calls", type=int, default=5)
+    ap.add_argument("--lengths", type=int, default=None, help="override every request's new-token count")
+    a = ap.parse_args()
+    _run(a.run, a.calls, a.lengths)
