@@ -76,17 +76,6 @@ OSCAR_DEVINL int find_bucket(const int* begin, int n, int x) {
 
 // 8 INT2 codes (little-endian 16 bits) -> 8 values of T via the exact chain
 // fp32(code*scale + zero) -> fp16 -> T   (format.py:91-96 + streaming_attention.py:124)
-template <typename T>
-OSCAR_DEVINL uint4 dequant8(uint32_t codes, float s, float z) {
-  T lut[4];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) lut[c] = Elem<T>::from_f16(__float2half_rn(__fadd_rn(__fmul_rn((float)c, s), z)));
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    w[i] = pack2<T>(lut[(codes >> (4 * i)) & 3u], lut[(codes >> (4 * i + 2)) & 3u]);
-  return make_uint4(w[0], w[1], w[2], w[3]);
-}
 
 // bf16/fp16 value of the reference chain -> fp16 operand of the P.V product.
 // History and staged values went through fp16, so this is exact for them
@@ -121,53 +110,111 @@ OSCAR_DEVINL uint4 staged8(const float* src) {
 OSCAR_DEVINL uint16_t ld_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
 // Fill one 64-key tile of K (type T) and V (fp16) in shared memory (swizzled)
-// for keys [kt0, kt_end).
+// for keys [kt0, kt_end).  Phase 1 looks each key up once (block table,
+// staging owner tag) into s_info; phase 2 gives a thread one (key, 64-dim
+// group): a 16-byte load of K codes, one of V codes and one 8-byte load of the
+// slot's scale / zero words for an INT2 key, or the key's fp32 staged rows,
+// or its bf16/fp16 current-chunk rows.
+constexpr int64_t kTileNone = INT64_MIN;  // zero fill: past the tile end or a bad block
+constexpr int64_t kTileNew = -1;          // current-chunk key; <= -2: staged (-2 - seat); >= 0: INT2 slot
+
+template <typename T>
+OSCAR_DEVINL void tile_lut(uint32_t meta_sz, T (&lut)[4]) {
+  const float sc = f16_bits_to_f32(meta_sz & 0xffffu), zr = f16_bits_to_f32(meta_sz >> 16);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) lut[c] = Elem<T>::from_f16(__float2half_rn(__fadd_rn(__fmul_rn((float)c, sc), zr)));
+}
+
 template <int D, typename T, int NW>
 OSCAR_DEVINL void load_kv_tile(const AttnArgs& a, T* sK, __half* sV, int kt0, int kt_end, int req, int h,
-                               int q_start, int prefix) {
-  constexpr int NCH = D / 8;
-  constexpr int TPI = 32 / NCH;  // tokens per warp iteration
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int sub = lane / NCH, ch = lane % NCH;
-  for (int r = warp * TPI + sub; r < kKT; r += NW * TPI) {
+                               int q_start, int prefix, int64_t* s_info) {
+  constexpr int G64 = D / 64;  // 64-dim groups per key
+  const int tid = threadIdx.x;
+  for (int r = tid; r < kKT; r += NW * 32) {
     const int p = kt0 + r;
-    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+    int64_t info = kTileNone;
     if (p < kt_end) {
       if (p < prefix) {
         const int pg = p / a.bs, off = p - pg * a.bs;
         const int64_t blk = a.bt[(int64_t)req * a.bt_stride + pg];
         if (blk < 0 || blk >= a.num_blocks) {
-          if (ch == 0) flag_error(2u);
+          flag_error(2u);
         } else {
-          bool staged = false;
-          int64_t seat = 0;
+          info = blk * a.bs + off;
           if (a.owner != nullptr) {
-            seat = (blk % a.stage_rows) * a.bs + off;
-            staged = a.owner[seat] == blk;
-          }
-          if (staged) {
-            const int64_t base = (seat * a.hk + h) * (int64_t)D + ch * 8;
-            kv = staged8<T>(a.stage_k + base);
-            vv = staged8<T>(a.stage_v + base);
-          } else {
-            const uint8_t* ks = a.kc + blk * a.ksb + off * a.kst + (int64_t)h * a.ksh;
-            const uint8_t* vs = a.vc + blk * a.vsb + off * a.vst + (int64_t)h * a.vsh;
-            const uint32_t kcode = ld_u16(ks + 32 + ch * 2);
-            const uint32_t vcode = ld_u16(vs + ch * 2);
-            kv = dequant8<T>(kcode, f16_bits_to_f32(ld_u16(ks + 0)), f16_bits_to_f32(ld_u16(ks + 2)));
-            vv = dequant8<T>(vcode, f16_bits_to_f32(ld_u16(ks + 4)), f16_bits_to_f32(ld_u16(ks + 6)));
+            const int64_t seat = (blk % a.stage_rows) * a.bs + off;
+            if (a.owner[seat] == blk) info = -2 - seat;
           }
         }
       } else {
-        const int64_t t = (int64_t)q_start + (p - prefix);
-        const int64_t base = (t * a.hk + h) * (int64_t)D + ch * 8;
-        kv = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) + base);
-        vv = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v_new) + base);
+        info = kTileNew;
       }
     }
-    const int sw = (ch ^ (r & 7)) * 8;
-    *reinterpret_cast<uint4*>(sK + r * D + sw) = kv;
-    *reinterpret_cast<uint4*>(sV + r * D + sw) = to_f16x8<T>(vv);
+    s_info[r] = info;
+  }
+  __syncthreads();
+  for (int it = tid; it < kKT * G64; it += NW * 32) {
+    const int r = it / G64, g = it - (it / G64) * G64;
+    const int64_t info = s_info[r];
+    T* krow = sK + r * D;
+    __half* vrow = sV + r * D;
+    auto put = [&](int i, uint4 kw, uint4 vw) {  // 8-dim chunk 8 g + i
+      const int sw = ((8 * g + i) ^ (r & 7)) * 8;
+      *reinterpret_cast<uint4*>(krow + sw) = kw;
+      *reinterpret_cast<uint4*>(vrow + sw) = vw;
+    };
+    if (info == kTileNone) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) put(i, make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0));
+    } else if (info >= 0) {
+      const int64_t blk = info / a.bs, off = info - (info / a.bs) * a.bs;
+      const uint8_t* ks = a.kc + blk * a.ksb + off * a.kst + (int64_t)h * a.ksh;
+      const uint8_t* vs = a.vc + blk * a.vsb + off * a.vst + (int64_t)h * a.vsh;
+      uint2 meta;  // K scale, K zero, V scale, V zero
+      uint4 kc, vc;
+      if (((reinterpret_cast<uintptr_t>(ks) | reinterpret_cast<uintptr_t>(vs)) & 15) == 0) {
+        meta = *reinterpret_cast<const uint2*>(ks);
+        kc = *reinterpret_cast<const uint4*>(ks + 32 + 16 * g);
+        vc = *reinterpret_cast<const uint4*>(vs + 16 * g);
+      } else {
+        // caches at an address or stride that is not 16-byte aligned: 16-bit reads
+        auto w2 = [](const uint8_t* q) { return (uint32_t)ld_u16(q) | ((uint32_t)ld_u16(q + 2) << 16); };
+        meta = make_uint2(w2(ks), w2(ks + 4));
+        kc = make_uint4(w2(ks + 32 + 16 * g), w2(ks + 36 + 16 * g), w2(ks + 40 + 16 * g), w2(ks + 44 + 16 * g));
+        vc = make_uint4(w2(vs + 16 * g), w2(vs + 4 + 16 * g), w2(vs + 8 + 16 * g), w2(vs + 12 + 16 * g));
+      }
+      T klut[4], vlut[4];
+      tile_lut<T>(meta.x, klut);
+      tile_lut<T>(meta.y, vlut);
+      __half vl[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) vl[c] = __float2half_rn(fminf(fmaxf(Elem<T>::to_f32(vlut[c]), -65504.0f), 65504.0f));
+      const uint32_t kws[4] = {kc.x, kc.y, kc.z, kc.w}, vws[4] = {vc.x, vc.y, vc.z, vc.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t kcode = (kws[i >> 1] >> (16 * (i & 1))) & 0xffffu;
+        const uint32_t vcode = (vws[i >> 1] >> (16 * (i & 1))) & 0xffffu;
+        uint32_t kw[4], vw[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          kw[e] = pack2<T>(klut[(kcode >> (4 * e)) & 3u], klut[(kcode >> (4 * e + 2)) & 3u]);
+          vw[e] = pack2<__half>(vl[(vcode >> (4 * e)) & 3u], vl[(vcode >> (4 * e + 2)) & 3u]);
+        }
+        put(i, make_uint4(kw[0], kw[1], kw[2], kw[3]), make_uint4(vw[0], vw[1], vw[2], vw[3]));
+      }
+    } else if (info == kTileNew) {
+      const int64_t t = (int64_t)q_start + (kt0 + r - prefix);
+      const int64_t base = (t * a.hk + h) * (int64_t)D + 64 * g;
+      const uint4* kn = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) + base);
+      const uint4* vn = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v_new) + base);
+#pragma unroll 4
+      for (int i = 0; i < 8; ++i) put(i, kn[i], to_f16x8<T>(vn[i]));
+    } else {  // staged: info = -2 - seat
+      const int64_t base = ((-2 - info) * a.hk + h) * (int64_t)D + 64 * g;
+#pragma unroll 2
+      for (int i = 0; i < 8; ++i)
+        put(i, staged8<T>(a.stage_k + base + 8 * i), to_f16x8<T>(staged8<T>(a.stage_v + base + 8 * i)));
+    }
   }
 }
 
@@ -176,6 +223,7 @@ __global__ void __launch_bounds__(NW * 32) paged_attn_kernel(const AttnArgs a, c
   constexpr int ROWS = 16 * NW;
   constexpr int NCH = D / 8;
   extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int64_t s_info[kKT];  // per-key lookups of the tile being loaded
   T* sQ = reinterpret_cast<T*>(smem);
   T* sK = sQ + ROWS * D;
   __half* sV = reinterpret_cast<__half*>(sK + kKT * D);
@@ -231,7 +279,7 @@ __global__ void __launch_bounds__(NW * 32) paged_attn_kernel(const AttnArgs a, c
 
   for (int kt0 = lo; kt0 < hi; kt0 += kKT) {
     __syncthreads();
-    load_kv_tile<D, T, NW>(a, sK, sV, kt0, min(kt0 + kKT, hi), req, h, q_start, prefix);
+    load_kv_tile<D, T, NW>(a, sK, sV, kt0, min(kt0 + kKT, hi), req, h, q_start, prefix, s_info);
     __syncthreads();
 
     float s[kKT / 8][4];
