@@ -14,6 +14,7 @@
 
 #include "../../include/oscar_b200.h"
 #include "attention.cuh"
+#include "cont_tc.cuh"
 #include "decode.cuh"
 #include "decode_tc.cuh"
 #include "rotate.cuh"
@@ -608,9 +609,51 @@ int run_decode_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs,
   return OSCAR_OK;
 }
 
+// Continuation / prefill q-blocks of 128 rows at head dim 256 on the tensor cores
+// (cont_tc.cuh): the tile kernel's plan (same q-blocks, splits and workspace),
+// one CTA per SM.
+template <typename T>
+int run_cont_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs, void* workspace, int64_t ws_bytes,
+                cudaStream_t s) {
+  constexpr int D = 256;
+  constexpr size_t smem = sizeof(oscar::CtSmem);
+  static thread_local int set_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != set_dev) {
+    cudaFuncSetAttribute(oscar::cont_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    set_dev = dev;
+  }
+  const int target = attn_target(D, oscar::kCtRows / 16);  // the workspace bound assumes this plan
+  for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
+    const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
+    Planned pl = plan_batch(reqs, b0, b1, oscar::kCtRows, base.group, base.hk, D, target, ws_bytes);
+    oscar::AttnArgs a = base;
+    if (pl.part_bytes > 0) {
+      const int64_t parts = pl.plan.part_begin[pl.plan.num_req];
+      a.part_o = reinterpret_cast<float*>(workspace);
+      a.part_lse = a.part_o + parts * base.hk * oscar::kCtRows * D;
+    }
+    dim3 grid(pl.plan.total_items, base.hk);
+    oscar::cont_tc_kernel<T><<<grid, oscar::kCtThreads, smem, s>>>(a, pl.plan);
+    int st = cuda_status("cont_tc_kernel");
+    if (st) return st;
+    if (pl.plan.total_merge_rows > 0) {
+      dim3 mgrid(pl.plan.total_merge_rows, base.hk);
+      oscar::split_combine_kernel<D><<<mgrid, D / 4, 0, s>>>(a, pl.plan);
+      st = cuda_status("split_combine_kernel");
+      if (st) return st;
+    }
+  }
+  return OSCAR_OK;
+}
+
 template <int D, typename T>
 int dispatch_rows(const oscar::AttnArgs& a, const std::vector<ReqInfo>& reqs, int max_q, void* ws, int64_t wsb,
                   cudaStream_t s) {
+  const int path = g_attention_path.load();
+  if (D == 256 && rows_for(max_q, a.group) == oscar::kCtRows && (path == 0 || path == 3))
+    return run_cont_tc<T>(a, reqs, ws, wsb, s);
   if (rows_for(max_q, a.group) == 32) return run_attention<D, T, 2>(a, reqs, ws, wsb, s);
   if (rows_for(max_q, a.group) == 128) return run_attention<D, T, 8>(a, reqs, ws, wsb, s);
   return run_attention<D, T, 4>(a, reqs, ws, wsb, s);
