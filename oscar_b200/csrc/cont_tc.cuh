@@ -23,7 +23,7 @@
 //   mask, keep a running row maximum that moves only when a score exceeds it by
 //   more than 15 (log2 units; P = 2^(x - m) <= 2^15 stays in fp16 range, and O
 //   is rescaled in TMEM on those tiles only), write P (fp16) to shared memory,
-//   sum the fp16-rounded P into the row's l; finally O / l and the LSE.
+//   sum P (fp32) into the row's l; finally O / l and the LSE.
 // Warps 4-11 (loaders): a thread fills one (key, 64-dim group) of a 64-key tile
 //   per stage: INT2 codes through 4-entry value tables (PRMT look-ups), fp32
 //   staged rows, or bf16/fp16 current-chunk rows.  Three tile stages.
@@ -189,13 +189,21 @@ __global__ void __launch_bounds__(kCtThreads, 1) cont_tc_kernel(const AttnArgs a
       tc::tmem_ld32(tmem + lane_base + kCtColS + 64 * b + 32, sr + 32);
       tc::tmem_wait_ld();
       const int nvis = lim - (lo + t * kCtKeys);  // keys c < nvis of this tile are visible
-      float mx = -INFINITY;
+      // row maximum of the raw scores (four independent chains; scale > 0 commutes with max);
+      // masking only on tiles that reach past a row's last visible key
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (__any_sync(0xffffffffu, nvis < kCtKeys)) {
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float v = c < nvis ? __uint_as_float(sr[c]) * scale : -INFINITY;
-        sr[c] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
+        for (int c = 0; c < 64; ++c) {
+          const float v = c < nvis ? __uint_as_float(sr[c]) : -INFINITY;
+          sr[c] = __float_as_uint(v);
+          m4[c & 3] = fmaxf(m4[c & 3], v);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(sr[c]));
       }
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale;
       const bool grow = mx > m_run + kCtHeadroom;
       const bool rescale = grow && m_run != -INFINITY;
       const float alpha = rescale ? exp2f(m_run - mx) : 1.0f;
@@ -216,23 +224,24 @@ __global__ void __launch_bounds__(kCtThreads, 1) cont_tc_kernel(const AttnArgs a
         tc::tmem_wait_st();
         l_run *= alpha;
       }
-      const float muse = (m_run == -INFINITY) ? 0.0f : m_run;
+      const float nmuse = (m_run == -INFINITY) ? 0.0f : -m_run;
       uint8_t* prow = sm.p[b] + p_off;
-      float lsum = 0.0f;
+      // P = 2^(x scale - m) in fp16 (masked keys: 2^-inf = 0); l sums the fp32 values
+      float l4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int kc = 0; kc < 8; ++kc) {
         uint32_t w[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const __half2 h2 = __floats2half2_rn(exp2f(__uint_as_float(sr[8 * kc + 2 * i]) - muse),
-                                               exp2f(__uint_as_float(sr[8 * kc + 2 * i + 1]) - muse));
-          const float2 f2 = __half22float2(h2);
-          lsum += f2.x + f2.y;
+          const float p0 = tc_exp2(fmaf(__uint_as_float(sr[8 * kc + 2 * i]), scale, nmuse));
+          const float p1 = tc_exp2(fmaf(__uint_as_float(sr[8 * kc + 2 * i + 1]), scale, nmuse));
+          l4[i] += p0 + p1;
+          const __half2 h2 = __floats2half2_rn(p0, p1);
           w[i] = *reinterpret_cast<const uint32_t*>(&h2);
         }
         *reinterpret_cast<uint4*>(prow + kc * 128) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l_run += lsum;
+      l_run += (l4[0] + l4[1]) + (l4[2] + l4[3]);
       tc::fence_async_smem();
       tc::tc_fence_before();
       tc::mbar_arrive(b_p + 8 * b);
@@ -290,35 +299,67 @@ __global__ void __launch_bounds__(kCtThreads, 1) cont_tc_kernel(const AttnArgs a
       if (lse_dst != nullptr) *lse_dst = lse;
     }
   } else if (warp < kCtMmaWarp) {
-    // ============================ loaders: thread = (key r, 64-dim group g) of each tile
+    // ============================ loaders: thread = (key r, 64-dim group g) of each tile.
+    // The look-ups and global loads of tile t go out before the wait for its
+    // stage (PV of tile t - 3), so their latency hides behind that wait; the
+    // dequantisation and the shared-memory stores follow it.
     const int lt = tid - 32 * kCtSmWarps;
     const int r = (lt >> 5) * 8 + (lane & 7), g = lane >> 3;
     const int k_off = (r >> 3) * 4096 + (r & 7) * 16;
     const int v_off = (r >> 3) * 128 + (r & 7) * 16;
+    constexpr int kNone = 0, kInt2 = 1, kNew = 2, kStaged = 3;
 #pragma unroll 1
     for (int t = 0; t < ntiles; ++t) {
       const int st = t % kCtStages;
-      if (t >= kCtStages && !wait(b_empty + 8 * st, ((t / kCtStages) - 1) & 1)) break;
       const int kt0 = lo + t * kCtKeys;
       const int pos = kt0 + r;
-      int64_t info = kTileNone;
+      int kind = kNone;
+      int64_t blk = 0, seat = -1, own = -1;
+      int off = 0;
       if (pos < min(kt0 + kCtKeys, hi)) {
         if (pos < prefix) {
-          const int pg = pos / a.bs, off = pos - pg * a.bs;
-          const int64_t blk = a.bt[(int64_t)req * a.bt_stride + pg];
-          if (blk < 0 || blk >= a.num_blocks) {
-            flag_error(2u);
-          } else {
-            info = blk * a.bs + off;
-            if (a.owner != nullptr) {
-              const int64_t seat = (blk % a.stage_rows) * a.bs + off;
-              if (a.owner[seat] == blk) info = -2 - seat;
-            }
-          }
+          const int pg = pos / a.bs;
+          off = pos - pg * a.bs;
+          blk = a.bt[(int64_t)req * a.bt_stride + pg];
+          if (blk < 0 || blk >= a.num_blocks) flag_error(2u);
+          else kind = kInt2;
         } else {
-          info = kTileNew;
+          kind = kNew;
         }
       }
+      uint2 meta = make_uint2(0, 0);  // K scale, K zero, V scale, V zero
+      uint4 rk[8], rv[8];             // INT2: codes in [0]; current chunk: the raw 64-dim rows
+      if (kind == kInt2) {
+        const uint8_t* ks = a.kc + blk * a.ksb + off * a.kst + (int64_t)h * a.ksh;
+        const uint8_t* vs = a.vc + blk * a.vsb + off * a.vst + (int64_t)h * a.vsh;
+        if (a.owner != nullptr) {  // owner tag, loaded beside the codes
+          seat = (blk % a.stage_rows) * a.bs + off;
+          own = a.owner[seat];
+        }
+        if (((reinterpret_cast<uintptr_t>(ks) | reinterpret_cast<uintptr_t>(vs)) & 15) == 0) {
+          meta = *reinterpret_cast<const uint2*>(ks);
+          rk[0] = *reinterpret_cast<const uint4*>(ks + 32 + 16 * g);
+          rv[0] = *reinterpret_cast<const uint4*>(vs + 16 * g);
+        } else {
+          // caches at an address or stride that is not 16-byte aligned: 16-bit reads
+          auto w2 = [](const uint8_t* q) { return (uint32_t)ld_u16(q) | ((uint32_t)ld_u16(q + 2) << 16); };
+          meta = make_uint2(w2(ks), w2(ks + 4));
+          rk[0] = make_uint4(w2(ks + 32 + 16 * g), w2(ks + 36 + 16 * g), w2(ks + 40 + 16 * g), w2(ks + 44 + 16 * g));
+          rv[0] = make_uint4(w2(vs + 16 * g), w2(vs + 4 + 16 * g), w2(vs + 8 + 16 * g), w2(vs + 12 + 16 * g));
+        }
+      } else if (kind == kNew) {
+        const int64_t tk = (int64_t)q_start + (pos - prefix);
+        const int64_t base = (tk * a.hk + h) * (int64_t)D + 64 * g;
+        const uint4* kn = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) + base);
+        const uint4* vn = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v_new) + base);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          rk[i] = kn[i];
+          rv[i] = vn[i];
+        }
+      }
+      if (t >= kCtStages && !wait(b_empty + 8 * st, ((t / kCtStages) - 1) & 1)) break;
+      if (kind == kInt2 && own == blk) kind = kStaged;  // the staging arena holds this position
       uint8_t* kdst = sm.k[st] + k_off;
       uint8_t* vdst = sm.v[st] + v_off;
       // 16-dim group j = 4 g + jj: K chunks 2j, 2j + 1 of the key's row, V chunks 2j, 2j + 1
@@ -329,25 +370,9 @@ __global__ void __launch_bounds__(kCtThreads, 1) cont_tc_kernel(const AttnArgs a
         *reinterpret_cast<uint4*>(vdst + (2 * j) * kCtVSbo) = make_uint4(vr[0], vr[1], vr[2], vr[3]);
         *reinterpret_cast<uint4*>(vdst + (2 * j + 1) * kCtVSbo) = make_uint4(vr[4], vr[5], vr[6], vr[7]);
       };
-      if (info >= 0) {
-        const int64_t blk = info / a.bs, off = info - (info / a.bs) * a.bs;
-        const uint8_t* ks = a.kc + blk * a.ksb + off * a.kst + (int64_t)h * a.ksh;
-        const uint8_t* vs = a.vc + blk * a.vsb + off * a.vst + (int64_t)h * a.vsh;
-        uint2 meta;  // K scale, K zero, V scale, V zero
-        uint4 kc, vc;
-        if (((reinterpret_cast<uintptr_t>(ks) | reinterpret_cast<uintptr_t>(vs)) & 15) == 0) {
-          meta = *reinterpret_cast<const uint2*>(ks);
-          kc = *reinterpret_cast<const uint4*>(ks + 32 + 16 * g);
-          vc = *reinterpret_cast<const uint4*>(vs + 16 * g);
-        } else {
-          // caches at an address or stride that is not 16-byte aligned: 16-bit reads
-          auto w2 = [](const uint8_t* q) { return (uint32_t)ld_u16(q) | ((uint32_t)ld_u16(q + 2) << 16); };
-          meta = make_uint2(w2(ks), w2(ks + 4));
-          kc = make_uint4(w2(ks + 32 + 16 * g), w2(ks + 36 + 16 * g), w2(ks + 40 + 16 * g), w2(ks + 44 + 16 * g));
-          vc = make_uint4(w2(vs + 16 * g), w2(vs + 4 + 16 * g), w2(vs + 8 + 16 * g), w2(vs + 12 + 16 * g));
-        }
+      if (kind == kInt2) {
         const uint2 kl = tc_klut<T>(meta.x), vl = tc_vlut<T>(meta.y);
-        const uint32_t kw[4] = {kc.x, kc.y, kc.z, kc.w}, vw[4] = {vc.x, vc.y, vc.z, vc.w};
+        const uint32_t kw[4] = {rk[0].x, rk[0].y, rk[0].z, rk[0].w}, vw[4] = {rv[0].x, rv[0].y, rv[0].z, rv[0].w};
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
           uint32_t kr[8], vr[8];
@@ -355,28 +380,24 @@ __global__ void __launch_bounds__(kCtThreads, 1) cont_tc_kernel(const AttnArgs a
           tc_lut_word(vw[jj], vl.x, vl.y, vr);
           put(jj, kr, vr);
         }
-      } else if (info == kTileNew) {
-        const int64_t tk = (int64_t)q_start + (pos - prefix);
-        const int64_t base = (tk * a.hk + h) * (int64_t)D + 64 * g;
-        const uint4* kn = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) + base);
-        const uint4* vn = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v_new) + base);
+      } else if (kind == kNew) {
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
-          const uint4 k0 = kn[2 * jj], k1 = kn[2 * jj + 1];
-          const uint4 v0 = to_f16x8<T>(vn[2 * jj]), v1 = to_f16x8<T>(vn[2 * jj + 1]);
-          const uint32_t kw[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+          const uint4 v0 = to_f16x8<T>(rv[2 * jj]), v1 = to_f16x8<T>(rv[2 * jj + 1]);
+          const uint32_t kw[8] = {rk[2 * jj].x, rk[2 * jj].y, rk[2 * jj].z, rk[2 * jj].w,
+                                  rk[2 * jj + 1].x, rk[2 * jj + 1].y, rk[2 * jj + 1].z, rk[2 * jj + 1].w};
           const uint32_t vw[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
           uint32_t kr[8], vr[8];
           ct_permute16(kw, kr);
           ct_permute16(vw, vr);
           put(jj, kr, vr);
         }
-      } else if (info == kTileNone) {
+      } else if (kind == kNone) {
         const uint32_t z[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) put(jj, z, z);
-      } else {  // staged: info = -2 - seat
-        const int64_t base = ((-2 - info) * a.hk + h) * (int64_t)D + 64 * g;
+      } else {  // staged: the fp32 rows of the seat
+        const int64_t base = (seat * a.hk + h) * (int64_t)D + 64 * g;
 #pragma unroll 1
         for (int jj = 0; jj < 4; ++jj) {
           uint32_t kr[8], vr[8];
