@@ -142,16 +142,18 @@ def attention_flops(prefixes, lengths, hq: int, d: int) -> float:
     return 4.0 * hq * d * pairs
 
 
-def _run(name: str, calls: int, lengths_override: int | None) -> None:
+def _run(name: str, calls: int, lengths_override: int | None, path: str = "auto") -> None:
     """Time ``slab_attention`` on one BASELINE configuration on cuda:0 (CUDA
     events around ``calls`` back-to-back calls after two warm-up calls) and
     print one JSON line with the algorithmic TFLOP/s; the committed runner of
-    the continuation profiles."""
+    the continuation profiles.  ``path`` selects the kernel family
+    (:func:`kernels.set_attention_path`)."""
     import json
     from pathlib import Path
 
     from . import kernels
 
+    kernels.set_attention_path(path)
     spec = dict(BASELINE_CONFIGS[name])
     if lengths_override:
         spec["lengths"] = [lengths_override] * len(spec["lengths"])
@@ -174,7 +176,7 @@ def _run(name: str, calls: int, lengths_override: int | None) -> None:
     peaks = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
     peak = json.loads(peaks.read_text()).get("bf16_tflops") if peaks.exists() else None
     tflops = flops / (ms * 1e-3) / 1e12
-    print(json.dumps({"workload": name, "lengths": spec["lengths"][:4], "ms_per_call": ms, "tflops": tflops,
+    print(json.dumps({"workload": name, "path": path, "lengths": spec["lengths"][:4], "ms_per_call": ms, "tflops": tflops,
                       "peak_bf16_tflops": peak, "frac": tflops / peak if peak else None,
                       "device_error": kernels.device_error(dev)}), flush=True)
 
@@ -186,5 +188,6 @@ if __name__ == "__main__":
     ap.add_argument("--run", required=True, choices=sorted(BASELINE_CONFIGS))
     ap.add_argument("--calls", type=int, default=5)
     ap.add_argument("--lengths", type=int, default=None, help="override every request's new-token count")
+    ap.add_argument("--path", default="auto", choices=["auto", "tensor", "decode", "tile"])
     a = ap.parse_args()
-    _run(a.run, a.calls, a.lengths)
+    _run(a.run, a.calls, a.lengths, a.path)
