@@ -40,6 +40,7 @@ struct AttnPlan {
   int prefix[kPlanReqs];
   int splits[kPlanReqs];
   int chunk[kPlanReqs];
+  int eff_tile[kPlanReqs + 1];  // continuation pre-pass: first 64-key tile of each request in AttnArgs::eff
 };
 
 struct AttnArgs {
@@ -63,6 +64,7 @@ struct AttnArgs {
   float* lse;
   float* part_o;
   float* part_lse;
+  uint8_t* eff;  // continuation pre-pass output (tile layout of cont_tc.cuh), or nullptr
 };
 
 OSCAR_DEVINL int find_bucket(const int* begin, int n, int x) {

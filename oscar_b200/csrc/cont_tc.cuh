@@ -29,6 +29,9 @@
 //   staged rows, or bf16/fp16 current-chunk rows.  Three tile stages.
 // Warp 12: MMA issuer, an event loop over two queues (QK of the next loaded tile
 //   once its S buffer is free; PV of the tile whose P is written).
+// With a pre-pass (kEff: ct_expand_kernel wrote every tile of the request's keys
+//   once, in this layout, to the workspace) there are no loader warps: the MMA
+//   warp also fetches each tile with two 32 KB bulk copies (160 threads).
 // Every wait is bounded; a timeout flags the error, and the CTA drains.
 //
 // Dim order inside each 16-dim group (both operands of Q K^T, and the N index of
@@ -74,8 +77,147 @@ OSCAR_DEVINL void ct_permute16(const uint32_t* w, uint32_t* r) {
   }
 }
 
+// One (key, 64-dim group) of a 64-key tile: the key's kind and its global loads
+// (phase 1), then its K and V values in the tile layout (phase 2), so that a
+// caller can wait for the destination between the two.
+constexpr int kCtNone = 0, kCtInt2 = 1, kCtNew = 2, kCtStaged = 3;
+struct CtItem {
+  int kind;
+  int64_t blk, seat, own;
+  uint2 meta;        // INT2: K scale, K zero, V scale, V zero
+  uint4 rk[8], rv[8];  // INT2: codes in [0]; current chunk: the raw 64-dim K and V rows
+};
+
 template <typename T>
-__global__ void __launch_bounds__(kCtThreads, 1) cont_tc_kernel(const AttnArgs a, const __grid_constant__ AttnPlan p) {
+OSCAR_DEVINL void ct_item_load(const AttnArgs& a, int req, int h, int q_start, int prefix, int pos, int live_end,
+                               int g, CtItem& it) {
+  constexpr int D = 256;
+  it.kind = kCtNone;
+  it.blk = 0;
+  it.seat = -1;
+  it.own = -1;
+  it.meta = make_uint2(0, 0);
+  if (pos >= live_end) return;
+  if (pos >= prefix) {
+    it.kind = kCtNew;
+    const int64_t tk = (int64_t)q_start + (pos - prefix);
+    const int64_t base = (tk * a.hk + h) * (int64_t)D + 64 * g;
+    const uint4* kn = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) + base);
+    const uint4* vn = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v_new) + base);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      it.rk[i] = kn[i];
+      it.rv[i] = vn[i];
+    }
+    return;
+  }
+  const int pg = pos / a.bs, off = pos - pg * a.bs;
+  const int64_t blk = a.bt[(int64_t)req * a.bt_stride + pg];
+  if (blk < 0 || blk >= a.num_blocks) {
+    flag_error(2u);
+    return;
+  }
+  it.kind = kCtInt2;
+  it.blk = blk;
+  const uint8_t* ks = a.kc + blk * a.ksb + off * a.kst + (int64_t)h * a.ksh;
+  const uint8_t* vs = a.vc + blk * a.vsb + off * a.vst + (int64_t)h * a.vsh;
+  if (a.owner != nullptr) {  // owner tag, loaded beside the codes
+    // (a 32-bit remainder whenever both operands fit, as they do in practice)
+    const int64_t rem = (blk <= 0xffffffffll && a.stage_rows <= 0xffffffffll)
+                            ? (int64_t)((uint32_t)blk % (uint32_t)a.stage_rows)
+                            : blk % a.stage_rows;
+    it.seat = rem * a.bs + off;
+    it.own = a.owner[it.seat];
+  }
+  if (((reinterpret_cast<uintptr_t>(ks) | reinterpret_cast<uintptr_t>(vs)) & 15) == 0) {
+    it.meta = *reinterpret_cast<const uint2*>(ks);
+    it.rk[0] = *reinterpret_cast<const uint4*>(ks + 32 + 16 * g);
+    it.rv[0] = *reinterpret_cast<const uint4*>(vs + 16 * g);
+  } else {
+    // caches at an address or stride that is not 16-byte aligned: 16-bit reads
+    auto w2 = [](const uint8_t* q) { return (uint32_t)ld_u16(q) | ((uint32_t)ld_u16(q + 2) << 16); };
+    it.meta = make_uint2(w2(ks), w2(ks + 4));
+    it.rk[0] = make_uint4(w2(ks + 32 + 16 * g), w2(ks + 36 + 16 * g), w2(ks + 40 + 16 * g), w2(ks + 44 + 16 * g));
+    it.rv[0] = make_uint4(w2(vs + 16 * g), w2(vs + 4 + 16 * g), w2(vs + 8 + 16 * g), w2(vs + 12 + 16 * g));
+  }
+}
+
+// phase 2: kdst / vdst point at the key's row of the K tile and V tile (shared or
+// global memory; 16-dim group j = 4 g + jj goes to K chunks 2j, 2j + 1 and V chunks 2j, 2j + 1)
+template <typename T>
+OSCAR_DEVINL void ct_item_store(const AttnArgs& a, int h, int g, CtItem& it, uint8_t* kdst, uint8_t* vdst) {
+  constexpr int D = 256;
+  auto put = [&](int jj, const uint32_t* kr, const uint32_t* vr) {
+    const int j = 4 * g + jj;
+    *reinterpret_cast<uint4*>(kdst + (2 * j) * 128) = make_uint4(kr[0], kr[1], kr[2], kr[3]);
+    *reinterpret_cast<uint4*>(kdst + (2 * j + 1) * 128) = make_uint4(kr[4], kr[5], kr[6], kr[7]);
+    *reinterpret_cast<uint4*>(vdst + (2 * j) * kCtVSbo) = make_uint4(vr[0], vr[1], vr[2], vr[3]);
+    *reinterpret_cast<uint4*>(vdst + (2 * j + 1) * kCtVSbo) = make_uint4(vr[4], vr[5], vr[6], vr[7]);
+  };
+  int kind = it.kind;
+  if (kind == kCtInt2 && it.own == it.blk) kind = kCtStaged;  // the staging arena holds this position
+  if (kind == kCtInt2) {
+    const uint2 kl = tc_klut<T>(it.meta.x), vl = tc_vlut<T>(it.meta.y);
+    const uint32_t kw[4] = {it.rk[0].x, it.rk[0].y, it.rk[0].z, it.rk[0].w};
+    const uint32_t vw[4] = {it.rv[0].x, it.rv[0].y, it.rv[0].z, it.rv[0].w};
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      uint32_t kr[8], vr[8];
+      tc_lut_word(kw[jj], kl.x, kl.y, kr);
+      tc_lut_word(vw[jj], vl.x, vl.y, vr);
+      put(jj, kr, vr);
+    }
+  } else if (kind == kCtNew) {
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const uint4 v0 = to_f16x8<T>(it.rv[2 * jj]), v1 = to_f16x8<T>(it.rv[2 * jj + 1]);
+      const uint32_t kw[8] = {it.rk[2 * jj].x, it.rk[2 * jj].y, it.rk[2 * jj].z, it.rk[2 * jj].w,
+                              it.rk[2 * jj + 1].x, it.rk[2 * jj + 1].y, it.rk[2 * jj + 1].z, it.rk[2 * jj + 1].w};
+      const uint32_t vw[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      uint32_t kr[8], vr[8];
+      ct_permute16(kw, kr);
+      ct_permute16(vw, vr);
+      put(jj, kr, vr);
+    }
+  } else if (kind == kCtNone) {
+    const uint32_t z[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) put(jj, z, z);
+  } else {  // staged: the fp32 rows of the seat
+    const int64_t base = (it.seat * a.hk + h) * (int64_t)D + 64 * g;
+#pragma unroll 1
+    for (int jj = 0; jj < 4; ++jj) {
+      uint32_t kr[8], vr[8];
+      tc_pack_word<T, false>(a.stage_k + base + 16 * jj, true, kr);
+      tc_pack_word<T, true>(a.stage_v + base + 16 * jj, true, vr);
+      put(jj, kr, vr);
+    }
+  }
+}
+
+// Continuation pre-pass: every 64-key tile of each request's keys [0, seq) (and
+// zeros past seq), per kv head, written once in the shared-memory tile layout
+// (K tile 32 KB, then V tile 32 KB) to a.eff at tile p.eff_tile[request] + i, so
+// that the q-block CTAs of the request fetch each tile with two bulk copies
+// instead of each dequantising it.  Block = one tile x kv head, 256 threads =
+// (key, 64-dim group) as in the loader warps of cont_tc_kernel.
+template <typename T>
+__global__ void __launch_bounds__(256) ct_expand_kernel(const AttnArgs a, const __grid_constant__ AttnPlan p) {
+  const int tile = blockIdx.x, h = blockIdx.y;
+  const int ri = find_bucket(p.eff_tile, p.num_req, tile);
+  const int i = tile - p.eff_tile[ri];
+  const int lt = threadIdx.x;
+  const int r = (lt >> 5) * 8 + ((lt & 31) & 7), g = (lt & 31) >> 3;
+  const int pos = i * kCtKeys + r;
+  CtItem it;
+  ct_item_load<T>(a, p.req_id[ri], h, p.q_start[ri], p.prefix[ri], pos, p.seq[ri], g, it);
+  uint8_t* base = a.eff + ((int64_t)tile * a.hk + h) * (2 * kCtKeys * 256 * 2);
+  ct_item_store<T>(a, h, g, it, base + (r >> 3) * 4096 + (r & 7) * 16,
+                   base + kCtKeys * 256 * 2 + (r >> 3) * 128 + (r & 7) * 16);
+}
+
+template <typename T, bool kEff>
+__global__ void __launch_bounds__(kEff ? 32 * (kCtSmWarps + 1) : kCtThreads, 1) cont_tc_kernel(const AttnArgs a, const __grid_constant__ AttnPlan p) {
   extern __shared__ __align__(1024) uint8_t ct_raw[];
   CtSmem& sm = *reinterpret_cast<CtSmem*>(ct_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -102,11 +244,14 @@ __global__ void __launch_bounds__(kCtThreads, 1) cont_tc_kernel(const AttnArgs a
   const uint32_t b_full = smem_u32(&sm.bar_full[0]), b_empty = smem_u32(&sm.bar_empty[0]);
   const uint32_t b_s = smem_u32(&sm.bar_s[0]), b_p = smem_u32(&sm.bar_p[0]), b_o = smem_u32(&sm.bar_o[0]);
   const uint32_t b_end = smem_u32(&sm.bar_end);
+  // the MMA warp: after the loader warps, or right after the softmax warps when the
+  // tiles come from the pre-pass (kEff) by bulk copy
+  constexpr int kMma = kEff ? kCtSmWarps : kCtMmaWarp;
 
-  if (warp == kCtMmaWarp) {
+  if (warp == kMma) {
     if (lane == 0) {
       for (int i = 0; i < kCtStages; ++i) {
-        tc::mbar_init(b_full + 8 * i, 32 * kCtLdWarps);
+        tc::mbar_init(b_full + 8 * i, kEff ? 1 : 32 * kCtLdWarps);
         tc::mbar_init(b_empty + 8 * i, 1);
       }
       for (int i = 0; i < 2; ++i) {
@@ -298,7 +443,7 @@ __global__ void __launch_bounds__(kCtThreads, 1) cont_tc_kernel(const AttnArgs a
       }
       if (lse_dst != nullptr) *lse_dst = lse;
     }
-  } else if (warp < kCtMmaWarp) {
+  } else if (!kEff && warp < kMma) {
     // ============================ loaders: thread = (key r, 64-dim group g) of each tile.
     // The look-ups and global loads of tile t go out before the wait for its
     // stage (PV of tile t - 3), so their latency hides behind that wait; the
@@ -307,105 +452,14 @@ __global__ void __launch_bounds__(kCtThreads, 1) cont_tc_kernel(const AttnArgs a
     const int r = (lt >> 5) * 8 + (lane & 7), g = lane >> 3;
     const int k_off = (r >> 3) * 4096 + (r & 7) * 16;
     const int v_off = (r >> 3) * 128 + (r & 7) * 16;
-    constexpr int kNone = 0, kInt2 = 1, kNew = 2, kStaged = 3;
 #pragma unroll 1
     for (int t = 0; t < ntiles; ++t) {
       const int st = t % kCtStages;
       const int kt0 = lo + t * kCtKeys;
-      const int pos = kt0 + r;
-      int kind = kNone;
-      int64_t blk = 0, seat = -1, own = -1;
-      int off = 0;
-      if (pos < min(kt0 + kCtKeys, hi)) {
-        if (pos < prefix) {
-          const int pg = pos / a.bs;
-          off = pos - pg * a.bs;
-          blk = a.bt[(int64_t)req * a.bt_stride + pg];
-          if (blk < 0 || blk >= a.num_blocks) flag_error(2u);
-          else kind = kInt2;
-        } else {
-          kind = kNew;
-        }
-      }
-      uint2 meta = make_uint2(0, 0);  // K scale, K zero, V scale, V zero
-      uint4 rk[8], rv[8];             // INT2: codes in [0]; current chunk: the raw 64-dim rows
-      if (kind == kInt2) {
-        const uint8_t* ks = a.kc + blk * a.ksb + off * a.kst + (int64_t)h * a.ksh;
-        const uint8_t* vs = a.vc + blk * a.vsb + off * a.vst + (int64_t)h * a.vsh;
-        if (a.owner != nullptr) {  // owner tag, loaded beside the codes
-          seat = (blk % a.stage_rows) * a.bs + off;
-          own = a.owner[seat];
-        }
-        if (((reinterpret_cast<uintptr_t>(ks) | reinterpret_cast<uintptr_t>(vs)) & 15) == 0) {
-          meta = *reinterpret_cast<const uint2*>(ks);
-          rk[0] = *reinterpret_cast<const uint4*>(ks + 32 + 16 * g);
-          rv[0] = *reinterpret_cast<const uint4*>(vs + 16 * g);
-        } else {
-          // caches at an address or stride that is not 16-byte aligned: 16-bit reads
-          auto w2 = [](const uint8_t* q) { return (uint32_t)ld_u16(q) | ((uint32_t)ld_u16(q + 2) << 16); };
-          meta = make_uint2(w2(ks), w2(ks + 4));
-          rk[0] = make_uint4(w2(ks + 32 + 16 * g), w2(ks + 36 + 16 * g), w2(ks + 40 + 16 * g), w2(ks + 44 + 16 * g));
-          rv[0] = make_uint4(w2(vs + 16 * g), w2(vs + 4 + 16 * g), w2(vs + 8 + 16 * g), w2(vs + 12 + 16 * g));
-        }
-      } else if (kind == kNew) {
-        const int64_t tk = (int64_t)q_start + (pos - prefix);
-        const int64_t base = (tk * a.hk + h) * (int64_t)D + 64 * g;
-        const uint4* kn = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k_new) + base);
-        const uint4* vn = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v_new) + base);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          rk[i] = kn[i];
-          rv[i] = vn[i];
-        }
-      }
+      CtItem it;
+      ct_item_load<T>(a, req, h, q_start, prefix, kt0 + r, min(kt0 + kCtKeys, hi), g, it);
       if (t >= kCtStages && !wait(b_empty + 8 * st, ((t / kCtStages) - 1) & 1)) break;
-      if (kind == kInt2 && own == blk) kind = kStaged;  // the staging arena holds this position
-      uint8_t* kdst = sm.k[st] + k_off;
-      uint8_t* vdst = sm.v[st] + v_off;
-      // 16-dim group j = 4 g + jj: K chunks 2j, 2j + 1 of the key's row, V chunks 2j, 2j + 1
-      auto put = [&](int jj, const uint32_t* kr, const uint32_t* vr) {
-        const int j = 4 * g + jj;
-        *reinterpret_cast<uint4*>(kdst + (2 * j) * 128) = make_uint4(kr[0], kr[1], kr[2], kr[3]);
-        *reinterpret_cast<uint4*>(kdst + (2 * j + 1) * 128) = make_uint4(kr[4], kr[5], kr[6], kr[7]);
-        *reinterpret_cast<uint4*>(vdst + (2 * j) * kCtVSbo) = make_uint4(vr[0], vr[1], vr[2], vr[3]);
-        *reinterpret_cast<uint4*>(vdst + (2 * j + 1) * kCtVSbo) = make_uint4(vr[4], vr[5], vr[6], vr[7]);
-      };
-      if (kind == kInt2) {
-        const uint2 kl = tc_klut<T>(meta.x), vl = tc_vlut<T>(meta.y);
-        const uint32_t kw[4] = {rk[0].x, rk[0].y, rk[0].z, rk[0].w}, vw[4] = {rv[0].x, rv[0].y, rv[0].z, rv[0].w};
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          uint32_t kr[8], vr[8];
-          tc_lut_word(kw[jj], kl.x, kl.y, kr);
-          tc_lut_word(vw[jj], vl.x, vl.y, vr);
-          put(jj, kr, vr);
-        }
-      } else if (kind == kNew) {
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const uint4 v0 = to_f16x8<T>(rv[2 * jj]), v1 = to_f16x8<T>(rv[2 * jj + 1]);
-          const uint32_t kw[8] = {rk[2 * jj].x, rk[2 * jj].y, rk[2 * jj].z, rk[2 * jj].w,
-                                  rk[2 * jj + 1].x, rk[2 * jj + 1].y, rk[2 * jj + 1].z, rk[2 * jj + 1].w};
-          const uint32_t vw[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-          uint32_t kr[8], vr[8];
-          ct_permute16(kw, kr);
-          ct_permute16(vw, vr);
-          put(jj, kr, vr);
-        }
-      } else if (kind == kNone) {
-        const uint32_t z[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) put(jj, z, z);
-      } else {  // staged: the fp32 rows of the seat
-        const int64_t base = (seat * a.hk + h) * (int64_t)D + 64 * g;
-#pragma unroll 1
-        for (int jj = 0; jj < 4; ++jj) {
-          uint32_t kr[8], vr[8];
-          tc_pack_word<T, false>(a.stage_k + base + 16 * jj, true, kr);
-          tc_pack_word<T, true>(a.stage_v + base + 16 * jj, true, vr);
-          put(jj, kr, vr);
-        }
-      }
+      ct_item_store<T>(a, h, g, it, sm.k[st] + k_off, sm.v[st] + v_off);
       tc::fence_async_smem();
       tc::mbar_arrive(b_full + 8 * st);
     }
@@ -418,9 +472,28 @@ __global__ void __launch_bounds__(kCtThreads, 1) cont_tc_kernel(const AttnArgs a
     const uint64_t dk0 = tc::smem_desc(smem_u32(sm.k[0]), 128, kCtKSbo);
     const uint64_t dv0 = tc::smem_desc(smem_u32(sm.v[0]), 128, kCtVSbo);
     const uint64_t dp0 = tc::smem_desc(smem_u32(sm.p[0]), 128, kCtPSbo);
+    // kEff: tile t of this CTA is pre-pass tile eff_tile[request] + lo / 64 + t
+    constexpr uint32_t kTileBytes = kCtKeys * 256 * 2;
+    const uint8_t* eff0 = kEff ? a.eff + ((int64_t)(p.eff_tile[ri] + lo / kCtKeys) * a.hk + h) * (2 * kTileBytes)
+                               : nullptr;
+    auto refill = [&](int t) {  // K and V tiles of tile t into stage t % 3
+      const int st = t % kCtStages;
+      const uint8_t* src = eff0 + (int64_t)t * a.hk * (2 * kTileBytes);
+      tc::mbar_expect_tx(b_full + 8 * st, 2 * kTileBytes);
+      tc::bulk_load(smem_u32(sm.k[st]), src, kTileBytes, b_full + 8 * st);
+      tc::bulk_load(smem_u32(sm.v[st]), src + kTileBytes, kTileBytes, b_full + 8 * st);
+    };
+    int rf = 0;  // kEff: tiles requested so far
+    if (kEff) {
+      if (tc::elect_one())
+        for (int t = 0; t < min(kCtStages, ntiles); ++t) refill(t);
+      __syncwarp();
+      rf = min(kCtStages, ntiles);
+    }
     uint32_t idle = 0;
+    int qs = 0;
 #pragma unroll 1
-    for (int qs = 0, ps = 0; ps < ntiles;) {
+    for (int ps = 0; ps < ntiles;) {
       bool prog = false;
       if (ps < qs && __shfl_sync(0xffffffffu, (int)tc::mbar_test(b_p + 8 * (ps & 1), (ps >> 1) & 1), 0)) {
         // O += P V of tile ps; its commits release the tile's stage and mark O
@@ -453,6 +526,14 @@ __global__ void __launch_bounds__(kCtThreads, 1) cont_tc_kernel(const AttnArgs a
         ++qs;
         prog = true;
       }
+      if (kEff && rf < ntiles &&
+          __shfl_sync(0xffffffffu, (int)tc::mbar_test(b_empty + 8 * (rf % kCtStages), ((rf / kCtStages) - 1) & 1), 0)) {
+        // stage rf % 3 was read by PV(rf - 3)
+        if (tc::elect_one()) refill(rf);
+        __syncwarp();
+        ++rf;
+        prog = true;
+      }
       if (prog) {
         idle = 0;
       } else if (__shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&sm.abort), 0) != 0) {
@@ -462,6 +543,10 @@ __global__ void __launch_bounds__(kCtThreads, 1) cont_tc_kernel(const AttnArgs a
         break;
       }
     }
+    // no bulk copy may still be writing shared memory when the CTA ends (abort path:
+    // requested tiles that no QK consumed)
+    for (int t = qs; kEff && t < rf; ++t)
+      if (!tc::mbar_wait(b_full + 8 * (t % kCtStages), (t / kCtStages) & 1)) break;
     // no MMA may be in flight when the tensor memory is freed
     if (tc::elect_one()) tc::mma_commit(b_end);
     __syncwarp();
@@ -470,7 +555,7 @@ __global__ void __launch_bounds__(kCtThreads, 1) cont_tc_kernel(const AttnArgs a
 
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == kCtMmaWarp) {
+  if (warp == kMma) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
   }

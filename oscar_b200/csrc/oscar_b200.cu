@@ -613,17 +613,43 @@ int run_decode_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs,
 // (cont_tc.cuh): the tile kernel's plan (same q-blocks, splits and workspace),
 // one CTA per SM.
 template <typename T>
-int run_cont_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs, void* workspace, int64_t ws_bytes,
-                cudaStream_t s) {
-  constexpr int D = 256;
-  constexpr size_t smem = sizeof(oscar::CtSmem);
+void set_cont_tc_smem() {
   static thread_local int set_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev != set_dev) {
-    cudaFuncSetAttribute(oscar::cont_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(oscar::cont_tc_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sizeof(oscar::CtSmem));
+    cudaFuncSetAttribute(oscar::cont_tc_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sizeof(oscar::CtSmem));
     set_dev = dev;
   }
+}
+
+// pre-pass tiles of a batch: ceil(seq / 64) per request (fills plan.eff_tile)
+inline int64_t cont_tc_eff_tiles(oscar::AttnPlan& plan) {
+  int64_t tiles = 0;
+  for (int j = 0; j < plan.num_req; ++j) {
+    plan.eff_tile[j] = (int)tiles;
+    tiles += (plan.seq[j] + oscar::kCtKeys - 1) / oscar::kCtKeys;
+  }
+  plan.eff_tile[plan.num_req] = (int)tiles;
+  return tiles;
+}
+constexpr int64_t kCtEffTileBytes = 2LL * oscar::kCtKeys * 256 * 2;  // K and V tiles of 64 keys x 256 dims
+
+// Continuation / prefill q-blocks of 128 rows at head dim 256 on the tensor cores
+// (cont_tc.cuh): the tile kernel's plan (same q-blocks, splits and workspace),
+// one CTA per SM.  When the workspace also holds every tile of the batch's keys
+// after the split partials, a pre-pass writes them once in the tile layout and
+// the attention CTAs fetch them by bulk copy; otherwise each CTA dequantises its
+// own tiles.
+template <typename T>
+int run_cont_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs, void* workspace, int64_t ws_bytes,
+                cudaStream_t s) {
+  constexpr int D = 256;
+  constexpr size_t smem = sizeof(oscar::CtSmem);
+  set_cont_tc_smem<T>();
   const int target = attn_target(D, oscar::kCtRows / 16);  // the workspace bound assumes this plan
   for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
     const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
@@ -634,9 +660,23 @@ int run_cont_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs, v
       a.part_o = reinterpret_cast<float*>(workspace);
       a.part_lse = a.part_o + parts * base.hk * oscar::kCtRows * D;
     }
+    const int64_t tiles = cont_tc_eff_tiles(pl.plan);
+    const int64_t eff_off = (pl.part_bytes + 255) & ~(int64_t)255;
+    const bool pre = tiles > 0 && tiles < INT32_MAX && workspace != nullptr &&
+                     (reinterpret_cast<uintptr_t>(workspace) & 255) == 0 &&
+                     eff_off + tiles * base.hk * kCtEffTileBytes <= ws_bytes;
     dim3 grid(pl.plan.total_items, base.hk);
-    oscar::cont_tc_kernel<T><<<grid, oscar::kCtThreads, smem, s>>>(a, pl.plan);
-    int st = cuda_status("cont_tc_kernel");
+    int st;
+    if (pre) {
+      a.eff = reinterpret_cast<uint8_t*>(workspace) + eff_off;
+      oscar::ct_expand_kernel<T><<<dim3((unsigned)tiles, base.hk), 256, 0, s>>>(a, pl.plan);
+      st = cuda_status("ct_expand_kernel");
+      if (st) return st;
+      oscar::cont_tc_kernel<T, true><<<grid, 32 * (oscar::kCtSmWarps + 1), smem, s>>>(a, pl.plan);
+    } else {
+      oscar::cont_tc_kernel<T, false><<<grid, oscar::kCtThreads, smem, s>>>(a, pl.plan);
+    }
+    st = cuda_status("cont_tc_kernel");
     if (st) return st;
     if (pl.plan.total_merge_rows > 0) {
       dim3 mgrid(pl.plan.total_merge_rows, base.hk);
@@ -820,7 +860,13 @@ int64_t oscar_slab_attention_workspace(const int32_t* qsl, const int32_t* seqs, 
   for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
     const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
     Planned pl = plan_batch(reqs, b0, b1, rows, group, num_kv_heads, head_dim, target, INT64_MAX);
-    worst = std::max(worst, pl.part_bytes);
+    int64_t need = pl.part_bytes;
+    if (head_dim == 256 && rows == oscar::kCtRows && (path == 0 || path == 3)) {
+      // the tensor-core continuation kernel's pre-pass tiles follow the partials
+      const int64_t tiles = cont_tc_eff_tiles(pl.plan);
+      if (tiles > 0 && tiles < INT32_MAX) need = ((need + 255) & ~(int64_t)255) + tiles * num_kv_heads * kCtEffTileBytes;
+    }
+    worst = std::max(worst, need);
   }
   return worst;
 }

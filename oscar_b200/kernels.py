@@ -21,7 +21,9 @@ from . import _native
 from ._native import check
 from .format import check_d
 
-DEFAULT_WORKSPACE_BYTES = 32 * 1024 * 1024
+# bound on the attention workspace (split partials, then the continuation pre-pass tiles:
+# ceil(seq / 64) x Hk x 64 KiB per request); the allocation is what a call needs, up to this
+DEFAULT_WORKSPACE_BYTES = 512 * 1024 * 1024
 
 _DTYPES = {torch.float32: _native.DTYPE_F32, torch.bfloat16: _native.DTYPE_BF16, torch.float16: _native.DTYPE_F16}
 
@@ -230,8 +232,10 @@ def slab_attention(q, k_new, v_new, kc, vc, table, qsl, seqs, scale, stage=None,
     fp32 overrides) and the causal current chunk.  Returns (out [n, Hq, D]
     fp32, lse [n, Hq] fp32 natural log).  ``qsl``/``seqs`` are host lists.
 
-    ``workspace_bytes`` bounds the split-KV partial buffer (any value is valid;
-    smaller only lowers parallelism).  ``chunk_tokens`` is accepted for
+    ``workspace_bytes`` bounds the workspace: split-KV partials, then (head dim
+    256, q-blocks of 128 rows) the keys' tiles written once by a pre-pass.  Any
+    value is valid; a smaller one only lowers parallelism or makes each
+    attention CTA dequantise its own tiles.  ``chunk_tokens`` is accepted for
     signature compatibility: the fused kernel never materialises a slab."""
     del chunk_tokens
     qsl = [int(x) for x in qsl]

@@ -215,3 +215,26 @@ def test_scattered_staged_positions_match_oracle(frac, attn_path):
     out, lse = kernels.slab_attention(*case_to_device(case, args[3], args[4], dev))
     assert_attention_close(out, lse, want_out, want_lse)
     assert kernels.device_error(dev) == 0
+
+
+@pytest.mark.parametrize("prefixes,lengths", [([3000], [600]), ([2500, 0, 130], [120, 90, 200])])
+def test_continuation_prepass_and_per_cta_dequant_agree(prefixes, lengths):
+    """128-row q-blocks at head dim 256: with room in the workspace the keys'
+    tiles are written once by a pre-pass and fetched by bulk copy; without it
+    each CTA dequantises its own tiles.  Both give the oracle's answer."""
+    from oscar_b200 import kernels
+
+    dev = need_gpu()
+    case = make_case(prefixes, lengths, hk=2, group=6, seed=41)
+    args, dt = case_to_oracle(case)
+    want_out, want_lse = orc.streaming_attention(*args, dtype=dt)
+    dargs = case_to_device(case, args[3], args[4], dev)
+    full, full_lse = kernels.slab_attention(*dargs)
+    assert_attention_close(full, full_lse, want_out, want_lse)
+    own, own_lse = kernels.slab_attention(*dargs, workspace_bytes=0)
+    assert_attention_close(own, own_lse, want_out, want_lse)
+    # the two runs plan different KV splits: LSE agrees to fp32 rounding, outputs to the
+    # fp16 rounding of P within each split
+    torch.testing.assert_close(own_lse, full_lse, atol=2e-5, rtol=2e-5)
+    torch.testing.assert_close(own, full, **OUT_TOL)
+    assert kernels.device_error(dev) == 0
