@@ -31,7 +31,8 @@
 //   once its S buffer is free; PV of the tile whose P is written).
 // With a pre-pass (kEff: ct_expand_kernel wrote every tile of the request's keys
 //   once, in this layout, to the workspace) there are no loader warps: the MMA
-//   warp also fetches each tile with two 32 KB bulk copies (160 threads).
+//   issuer is warp 4, and a producer warp (warp 5) fetches each tile with two
+//   32 KB bulk copies (192 threads).
 // Every wait is bounded; a timeout flags the error, and the CTA drains.
 //
 // Dim order inside each 16-dim group (both operands of Q K^T, and the N index of
@@ -51,6 +52,7 @@ constexpr int kCtSmWarps = 4;
 constexpr int kCtLdWarps = 8;
 constexpr int kCtMmaWarp = kCtSmWarps + kCtLdWarps;
 constexpr int kCtThreads = 32 * (kCtMmaWarp + 1);  // 416
+constexpr int kCtEffThreads = 32 * (kCtSmWarps + 2);  // pre-pass variant: softmax, MMA, producer
 constexpr int kCtColQ = 0, kCtColS = 128, kCtColO = 256;
 constexpr uint32_t kCtKSbo = 4096;  // K tile: bytes between 8-key groups (32 k-groups x 128 B)
 constexpr uint32_t kCtVSbo = 1024;  // V tile: bytes between 8-dim groups (8 key groups x 128 B)
@@ -217,7 +219,7 @@ __global__ void __launch_bounds__(256) ct_expand_kernel(const AttnArgs a, const 
 }
 
 template <typename T, bool kEff>
-__global__ void __launch_bounds__(kEff ? 32 * (kCtSmWarps + 1) : kCtThreads, 1) cont_tc_kernel(const AttnArgs a, const __grid_constant__ AttnPlan p) {
+__global__ void __launch_bounds__(kEff ? kCtEffThreads : kCtThreads, 1) cont_tc_kernel(const AttnArgs a, const __grid_constant__ AttnPlan p) {
   extern __shared__ __align__(1024) uint8_t ct_raw[];
   CtSmem& sm = *reinterpret_cast<CtSmem*>(ct_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -463,6 +465,41 @@ __global__ void __launch_bounds__(kEff ? 32 * (kCtSmWarps + 1) : kCtThreads, 1) 
       tc::fence_async_smem();
       tc::mbar_arrive(b_full + 8 * st);
     }
+  } else if (kEff && warp == kMma + 1) {
+    // ============================ producer (kEff): tile t of this CTA is pre-pass tile
+    // eff_tile[request] + lo / 64 + t; its K and V tiles arrive by two bulk copies once
+    // PV(t - 3) has freed stage t % 3.  One elected lane issues.
+    constexpr uint32_t kTileBytes = kCtKeys * 256 * 2;
+    const uint8_t* eff0 = a.eff + ((int64_t)(p.eff_tile[ri] + lo / kCtKeys) * a.hk + h) * (2 * kTileBytes);
+    int rf = 0;
+#pragma unroll 1
+    for (; rf < ntiles; ++rf) {
+      const int st = rf % kCtStages;
+      if (rf >= kCtStages) {
+        bool ready = false;
+        for (uint32_t n = 0; !ready; ++n) {
+          ready = __shfl_sync(0xffffffffu, (int)tc::mbar_test(b_empty + 8 * st, ((rf / kCtStages) - 1) & 1), 0) != 0;
+          if (ready) break;
+          if (__shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&sm.abort), 0) != 0) break;
+          if (n > 4 * tc::kSpinLimit) {
+            if (lane == 0) give_up(16u);
+            break;
+          }
+        }
+        if (!ready) break;
+      }
+      if (tc::elect_one()) {
+        const uint8_t* src = eff0 + (int64_t)rf * a.hk * (2 * kTileBytes);
+        tc::mbar_expect_tx(b_full + 8 * st, 2 * kTileBytes);
+        tc::bulk_load(smem_u32(sm.k[st]), src, kTileBytes, b_full + 8 * st);
+        tc::bulk_load(smem_u32(sm.v[st]), src + kTileBytes, kTileBytes, b_full + 8 * st);
+      }
+      __syncwarp();
+    }
+    // no bulk copy may still be writing shared memory when the CTA ends (abort path):
+    // the last tile issued on each stage has landed
+    for (int t = max(0, rf - kCtStages); t < rf; ++t)
+      if (!tc::mbar_wait(b_full + 8 * (t % kCtStages), (t / kCtStages) & 1)) break;
   } else {
     // ============================ MMA issuer (one elected lane issues; the warp runs the loop)
     constexpr uint32_t idesc_qk =
@@ -472,28 +509,9 @@ __global__ void __launch_bounds__(kEff ? 32 * (kCtSmWarps + 1) : kCtThreads, 1) 
     const uint64_t dk0 = tc::smem_desc(smem_u32(sm.k[0]), 128, kCtKSbo);
     const uint64_t dv0 = tc::smem_desc(smem_u32(sm.v[0]), 128, kCtVSbo);
     const uint64_t dp0 = tc::smem_desc(smem_u32(sm.p[0]), 128, kCtPSbo);
-    // kEff: tile t of this CTA is pre-pass tile eff_tile[request] + lo / 64 + t
-    constexpr uint32_t kTileBytes = kCtKeys * 256 * 2;
-    const uint8_t* eff0 = kEff ? a.eff + ((int64_t)(p.eff_tile[ri] + lo / kCtKeys) * a.hk + h) * (2 * kTileBytes)
-                               : nullptr;
-    auto refill = [&](int t) {  // K and V tiles of tile t into stage t % 3
-      const int st = t % kCtStages;
-      const uint8_t* src = eff0 + (int64_t)t * a.hk * (2 * kTileBytes);
-      tc::mbar_expect_tx(b_full + 8 * st, 2 * kTileBytes);
-      tc::bulk_load(smem_u32(sm.k[st]), src, kTileBytes, b_full + 8 * st);
-      tc::bulk_load(smem_u32(sm.v[st]), src + kTileBytes, kTileBytes, b_full + 8 * st);
-    };
-    int rf = 0;  // kEff: tiles requested so far
-    if (kEff) {
-      if (tc::elect_one())
-        for (int t = 0; t < min(kCtStages, ntiles); ++t) refill(t);
-      __syncwarp();
-      rf = min(kCtStages, ntiles);
-    }
     uint32_t idle = 0;
-    int qs = 0;
 #pragma unroll 1
-    for (int ps = 0; ps < ntiles;) {
+    for (int qs = 0, ps = 0; ps < ntiles;) {
       bool prog = false;
       if (ps < qs && __shfl_sync(0xffffffffu, (int)tc::mbar_test(b_p + 8 * (ps & 1), (ps >> 1) & 1), 0)) {
         // O += P V of tile ps; its commits release the tile's stage and mark O
@@ -526,14 +544,6 @@ __global__ void __launch_bounds__(kEff ? 32 * (kCtSmWarps + 1) : kCtThreads, 1) 
         ++qs;
         prog = true;
       }
-      if (kEff && rf < ntiles &&
-          __shfl_sync(0xffffffffu, (int)tc::mbar_test(b_empty + 8 * (rf % kCtStages), ((rf / kCtStages) - 1) & 1), 0)) {
-        // stage rf % 3 was read by PV(rf - 3)
-        if (tc::elect_one()) refill(rf);
-        __syncwarp();
-        ++rf;
-        prog = true;
-      }
       if (prog) {
         idle = 0;
       } else if (__shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&sm.abort), 0) != 0) {
@@ -543,10 +553,6 @@ __global__ void __launch_bounds__(kEff ? 32 * (kCtSmWarps + 1) : kCtThreads, 1) 
         break;
       }
     }
-    // no bulk copy may still be writing shared memory when the CTA ends (abort path:
-    // requested tiles that no QK consumed)
-    for (int t = qs; kEff && t < rf; ++t)
-      if (!tc::mbar_wait(b_full + 8 * (t % kCtStages), (t / kCtStages) & 1)) break;
     // no MMA may be in flight when the tensor memory is freed
     if (tc::elect_one()) tc::mma_commit(b_end);
     __syncwarp();

@@ -672,7 +672,7 @@ int run_cont_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs, v
       oscar::ct_expand_kernel<T><<<dim3((unsigned)tiles, base.hk), 256, 0, s>>>(a, pl.plan);
       st = cuda_status("ct_expand_kernel");
       if (st) return st;
-      oscar::cont_tc_kernel<T, true><<<grid, 32 * (oscar::kCtSmWarps + 1), smem, s>>>(a, pl.plan);
+      oscar::cont_tc_kernel<T, true><<<grid, oscar::kCtEffThreads, smem, s>>>(a, pl.plan);
     } else {
       oscar::cont_tc_kernel<T, false><<<grid, oscar::kCtThreads, smem, s>>>(a, pl.plan);
     }
