@@ -166,9 +166,12 @@ int oscar_staging_write_noalloc(const float* k_rot, const float* v_rot, int64_t 
  * stage_k/stage_v/owner: staging arena or all NULL (stage_rows = 0)
  * out      [n_tokens, num_q_heads, head_dim] fp32 (rotated space)
  * lse      [n_tokens, num_q_heads] fp32, natural log, scale included
- * workspace: device scratch for split-KV partials; any size (0 included)
- *   is valid -- a small workspace only lowers parallelism.  The planned
- *   size for full parallelism is oscar_slab_attention_workspace().
+ * workspace: device scratch for split-KV partials and, at head dim 256
+ *   with q-blocks of 128 rows, the keys' tiles written once by a pre-pass
+ *   (ceil(seq / 64) * num_kv_heads * 64 KiB per request, after the partials,
+ *   256-byte aligned workspace).  Any size (0 included) is valid -- a small
+ *   workspace only lowers parallelism or makes each attention CTA dequantise
+ *   its own tiles.  The planned size is oscar_slab_attention_workspace().
  */
 int oscar_slab_attention(const void* q, const void* k_new, const void* v_new, int32_t dtype,
                          int64_t n_tokens, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
@@ -183,7 +186,8 @@ int oscar_slab_attention(const void* q, const void* k_new, const void* v_new, in
                          void* workspace, int64_t workspace_bytes,
                          void* stream);
 
-/* Workspace bytes the planner would use for full split-KV parallelism. */
+/* Workspace bytes the planner would use: full split-KV parallelism, plus
+ * the continuation pre-pass tiles where that path applies. */
 int64_t oscar_slab_attention_workspace(const int32_t* qsl, const int32_t* seqs, int32_t num_requests,
                                        int32_t has_new, int32_t num_q_heads, int32_t num_kv_heads,
                                        int32_t head_dim);
