@@ -637,6 +637,18 @@ inline int64_t cont_tc_eff_tiles(oscar::AttnPlan& plan) {
   return tiles;
 }
 constexpr int64_t kCtEffTileBytes = 2LL * oscar::kCtKeys * 256 * 2;  // K and V tiles of 64 keys x 256 dims
+// the pre-pass pays when each request's tiles are read by several q-blocks (at least
+// four on average); with fewer, writing and re-reading the expanded tiles costs
+// more than each CTA dequantising its own
+inline bool cont_tc_prepass_pays(const oscar::AttnPlan& plan) {
+  int64_t qblocks = 0;
+  for (int j = 0; j < plan.num_req; ++j) qblocks += (plan.item_begin[j + 1] - plan.item_begin[j]) / plan.splits[j];
+  return plan.num_req > 0 && qblocks >= 4LL * plan.num_req;
+}
+// head dim 256, more than 32 rows per KV group: the tensor-core continuation kernel
+inline bool cont_tc_route(int head_dim, int max_q, int group, int path) {
+  return head_dim == 256 && rows_for(max_q, group) != 32 && (path == 0 || path == 3);
+}
 
 // Continuation / prefill q-blocks of 128 rows at head dim 256 on the tensor cores
 // (cont_tc.cuh): the tile kernel's plan (same q-blocks, splits and workspace),
@@ -662,7 +674,7 @@ int run_cont_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs, v
     }
     const int64_t tiles = cont_tc_eff_tiles(pl.plan);
     const int64_t eff_off = (pl.part_bytes + 255) & ~(int64_t)255;
-    const bool pre = tiles > 0 && tiles < INT32_MAX && workspace != nullptr &&
+    const bool pre = tiles > 0 && tiles < INT32_MAX && workspace != nullptr && cont_tc_prepass_pays(pl.plan) &&
                      (reinterpret_cast<uintptr_t>(workspace) & 255) == 0 &&
                      eff_off + tiles * base.hk * kCtEffTileBytes <= ws_bytes;
     dim3 grid(pl.plan.total_items, base.hk);
@@ -691,9 +703,7 @@ int run_cont_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs, v
 template <int D, typename T>
 int dispatch_rows(const oscar::AttnArgs& a, const std::vector<ReqInfo>& reqs, int max_q, void* ws, int64_t wsb,
                   cudaStream_t s) {
-  const int path = g_attention_path.load();
-  if (D == 256 && rows_for(max_q, a.group) == oscar::kCtRows && (path == 0 || path == 3))
-    return run_cont_tc<T>(a, reqs, ws, wsb, s);
+  if (cont_tc_route(D, max_q, a.group, g_attention_path.load())) return run_cont_tc<T>(a, reqs, ws, wsb, s);
   if (rows_for(max_q, a.group) == 32) return run_attention<D, T, 2>(a, reqs, ws, wsb, s);
   if (rows_for(max_q, a.group) == 128) return run_attention<D, T, 8>(a, reqs, ws, wsb, s);
   return run_attention<D, T, 4>(a, reqs, ws, wsb, s);
@@ -855,13 +865,14 @@ int64_t oscar_slab_attention_workspace(const int32_t* qsl, const int32_t* seqs, 
       worst = std::max(worst, pl.part_bytes);
     }
   }
-  const int rows = rows_for(max_q, group);
+  const bool ct = cont_tc_route(head_dim, max_q, group, path);
+  const int rows = ct ? oscar::kCtRows : rows_for(max_q, group);
   const int target = attn_target(head_dim, rows / 16);
   for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
     const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
     Planned pl = plan_batch(reqs, b0, b1, rows, group, num_kv_heads, head_dim, target, INT64_MAX);
     int64_t need = pl.part_bytes;
-    if (head_dim == 256 && rows == oscar::kCtRows && (path == 0 || path == 3)) {
+    if (ct && cont_tc_prepass_pays(pl.plan)) {
       // the tensor-core continuation kernel's pre-pass tiles follow the partials
       const int64_t tiles = cont_tc_eff_tiles(pl.plan);
       if (tiles > 0 && tiles < INT32_MAX) need = ((need + 255) & ~(int64_t)255) + tiles * num_kv_heads * kCtEffTileBytes;
