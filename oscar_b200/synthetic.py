@@ -142,12 +142,15 @@ def attention_flops(prefixes, lengths, hq: int, d: int) -> float:
     return 4.0 * hq * d * pairs
 
 
-def _run(name: str, calls: int, lengths_override: int | None, path: str = "auto") -> None:
+def _run(name: str, calls: int, lengths_override: int | None, path: str = "auto", prefixes_override: int | None = None,
+         sdpa: bool = False) -> None:
     """Time ``slab_attention`` on one BASELINE configuration on cuda:0 (CUDA
     events around ``calls`` back-to-back calls after two warm-up calls) and
     print one JSON line with the algorithmic TFLOP/s; the committed runner of
     the continuation profiles.  ``path`` selects the kernel family
-    (:func:`kernels.set_attention_path`)."""
+    (:func:`kernels.set_attention_path`).  With ``sdpa`` and no history (prefix-free
+    prefill), torch's scaled_dot_product_attention on the same causal q/k/v is timed
+    beside it, as the library attention a prefix-free prefill could otherwise use."""
     import json
     from pathlib import Path
 
@@ -157,6 +160,8 @@ def _run(name: str, calls: int, lengths_override: int | None, path: str = "auto"
     spec = dict(BASELINE_CONFIGS[name])
     if lengths_override:
         spec["lengths"] = [lengths_override] * len(spec["lengths"])
+    if prefixes_override is not None:
+        spec["prefixes"] = [prefixes_override] * len(spec["prefixes"])
     dev = torch.device("cuda", 0)
     case = make_case(spec["prefixes"], spec["lengths"], hk=spec["hk"], group=spec["group"], device=dev)
     fill_caches(case)
@@ -176,9 +181,29 @@ def _run(name: str, calls: int, lengths_override: int | None, path: str = "auto"
     peaks = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
     peak = json.loads(peaks.read_text()).get("bf16_tflops") if peaks.exists() else None
     tflops = flops / (ms * 1e-3) / 1e12
-    print(json.dumps({"workload": name, "path": path, "lengths": spec["lengths"][:4], "ms_per_call": ms, "tflops": tflops,
-                      "peak_bf16_tflops": peak, "frac": tflops / peak if peak else None,
-                      "device_error": kernels.device_error(dev)}), flush=True)
+    line = {"workload": name, "path": path, "prefixes": spec["prefixes"][:4], "lengths": spec["lengths"][:4],
+            "ms_per_call": ms, "tflops": tflops, "peak_bf16_tflops": peak, "frac": tflops / peak if peak else None,
+            "device_error": kernels.device_error(dev)}
+    if sdpa and not any(spec["prefixes"]) and len(spec["lengths"]) == 1:
+        import torch.nn.functional as F
+
+        q = case.q.transpose(0, 1).unsqueeze(0)  # [1, Hq, n, D]
+        k = case.k_new.transpose(0, 1).unsqueeze(0)
+        v = case.v_new.transpose(0, 1).unsqueeze(0)
+        run = lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=case.scale,  # noqa: E731
+                                                     enable_gqa=True)
+        for _ in range(2):
+            run()
+        torch.cuda.synchronize(dev)
+        start.record()
+        for _ in range(calls):
+            run()
+        end.record()
+        torch.cuda.synchronize(dev)
+        ms_lib = start.elapsed_time(end) / calls
+        line["sdpa_ms_per_call"] = ms_lib
+        line["sdpa_tflops"] = flops / (ms_lib * 1e-3) / 1e12
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":
@@ -189,5 +214,7 @@ if __name__ == "__main__":
     ap.add_argument("--calls", type=int, default=5)
     ap.add_argument("--lengths", type=int, default=None, help="override every request's new-token count")
     ap.add_argument("--path", default="auto", choices=["auto", "tensor", "decode", "tile"])
+    ap.add_argument("--prefixes", type=int, default=None, help="override every request's history length")
+    ap.add_argument("--sdpa", action="store_true", help="prefix-free prefill: also time torch SDPA on the same q/k/v")
     a = ap.parse_args()
-    _run(a.run, a.calls, a.lengths, a.path)
+    _run(a.run, a.calls, a.lengths, a.path, a.prefixes, a.sdpa)
