@@ -294,21 +294,23 @@ __global__ void __launch_bounds__(kEff ? kCtEffThreads : kCtThreads, 1) cont_tc_
       const int tl = row / G, hg = row - (row / G) * G;
       qsrc += ((int64_t)(q_start + tok0 + tl) * a.hq + (int64_t)h * G + hg) * D;
     }
+    // two rounds of 128 dims (16 loads in flight per thread), 32 columns per store
 #pragma unroll 1
-    for (int c0 = 0; c0 < 4; ++c0) {  // 64 dims = 32 columns per store
-      uint32_t r[32];
+    for (int c0 = 0; c0 < 4; c0 += 2) {
+      uint4 w[16];
 #pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const int j = 4 * c0 + jj;
-        uint4 w0 = make_uint4(0, 0, 0, 0), w1 = make_uint4(0, 0, 0, 0);
-        if (live) {
-          w0 = *reinterpret_cast<const uint4*>(qsrc + 16 * j);
-          w1 = *reinterpret_cast<const uint4*>(qsrc + 16 * j + 8);
+      for (int i = 0; i < 16; ++i) w[i] = live ? *reinterpret_cast<const uint4*>(qsrc + 64 * c0 + 8 * i) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t r[32];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const uint4 w0 = w[8 * half + 2 * jj], w1 = w[8 * half + 2 * jj + 1];
+          const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          ct_permute16(ww, r + 8 * jj);
         }
-        const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        ct_permute16(w, r + 8 * jj);
+        tc::tmem_st32(tmem + lane_base + kCtColQ + 32 * (c0 + half), r);
       }
-      tc::tmem_st32(tmem + lane_base + kCtColQ + 32 * c0, r);
     }
     tc::tmem_wait_st();
   }
