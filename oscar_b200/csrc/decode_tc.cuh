@@ -368,7 +368,9 @@ __global__ void __maxnreg__(72)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   TcSmem& sm = *reinterpret_cast<TcSmem*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int item = blockIdx.x, h = blockIdx.y;
+  // grid (kv heads, items): the hardware starts CTAs x-fastest, so every head of the
+  // heaviest requests (planned first) starts before the light ones
+  const int item = blockIdx.y, h = blockIdx.x;
   const int ri = find_bucket(p.item_begin, p.num_req, item);
   const int sp = item - p.item_begin[ri];
   const int req = p.req_id[ri];

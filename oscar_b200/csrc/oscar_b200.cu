@@ -595,7 +595,7 @@ int run_decode_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs,
     oscar::AttnArgs a = base;
     a.part_o = reinterpret_cast<float*>(workspace);  // fp16 partials in the fp32-sized slots
     a.part_lse = a.part_o + (int64_t)pl.plan.total_items * base.hk * oscar::kTcRows * 256;
-    launch_pdl(oscar::decode_tc_kernel<T>, dim3(pl.plan.total_items, base.hk), dim3(oscar::kTcThreads),
+    launch_pdl(oscar::decode_tc_kernel<T>, dim3(base.hk, pl.plan.total_items), dim3(oscar::kTcThreads),
                sizeof(oscar::TcSmem), s, a, pl.plan, tmk, tmv);
     int st = cuda_status("decode_tc_kernel");
     if (st) return st;
@@ -748,6 +748,10 @@ int collect_requests(const int32_t* qsl, const int32_t* seqs, int32_t num_reques
       any_history = any_history || prefix > 0;
     }
   }
+  // longest first: the planners lay CTAs out in request order and the hardware starts
+  // them in that order, so the heaviest requests start first and short ones fill the
+  // tail (a request's own plan and splits do not depend on its place)
+  std::stable_sort(reqs.begin(), reqs.end(), [](const ReqInfo& x, const ReqInfo& y) { return x.seq > y.seq; });
   return OSCAR_OK;
 }
 

@@ -143,14 +143,16 @@ def attention_flops(prefixes, lengths, hq: int, d: int) -> float:
 
 
 def _run(name: str, calls: int, lengths_override: int | None, path: str = "auto", prefixes_override: int | None = None,
-         sdpa: bool = False) -> None:
+         sdpa: bool = False, flush: bool = False) -> None:
     """Time ``slab_attention`` on one BASELINE configuration on cuda:0 (CUDA
     events around ``calls`` back-to-back calls after two warm-up calls) and
     print one JSON line with the algorithmic TFLOP/s; the committed runner of
     the continuation profiles.  ``path`` selects the kernel family
     (:func:`kernels.set_attention_path`).  With ``sdpa`` and no history (prefix-free
     prefill), torch's scaled_dot_product_attention on the same causal q/k/v is timed
-    beside it, as the library attention a prefix-free prefill could otherwise use."""
+    beside it, as the library attention a prefix-free prefill could otherwise use.  With
+    ``flush`` every call is timed alone after an L2 eviction (decode-shaped configs, whose
+    caches would otherwise stay in L2 between calls)."""
     import json
     from pathlib import Path
 
@@ -170,20 +172,40 @@ def _run(name: str, calls: int, lengths_override: int | None, path: str = "auto"
         kernels.slab_attention(*args)
     torch.cuda.synchronize(dev)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(calls):
-        kernels.slab_attention(*args)
-    end.record()
-    torch.cuda.synchronize(dev)
-    ms = start.elapsed_time(end) / calls
+    if flush:
+        # each call timed alone, after a 512 MiB write that evicts the 126 MB L2
+        scrub = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+        ms = 0.0
+        for _ in range(calls):
+            scrub.zero_()
+            start.record()
+            kernels.slab_attention(*args)
+            end.record()
+            torch.cuda.synchronize(dev)
+            ms += start.elapsed_time(end)
+        ms /= calls
+        del scrub
+    else:
+        start.record()
+        for _ in range(calls):
+            kernels.slab_attention(*args)
+        end.record()
+        torch.cuda.synchronize(dev)
+        ms = start.elapsed_time(end) / calls
     hq = spec["hk"] * spec["group"]
     flops = attention_flops(spec["prefixes"], spec["lengths"], hq, case.q.shape[-1])
     peaks = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
     peak = json.loads(peaks.read_text()).get("bf16_tflops") if peaks.exists() else None
     tflops = flops / (ms * 1e-3) / 1e12
-    line = {"workload": name, "path": path, "prefixes": spec["prefixes"][:4], "lengths": spec["lengths"][:4],
+    line = {"workload": name, "path": path, "l2_flushed": flush, "prefixes": spec["prefixes"][:4], "lengths": spec["lengths"][:4],
             "ms_per_call": ms, "tflops": tflops, "peak_bf16_tflops": peak, "frac": tflops / peak if peak else None,
             "device_error": kernels.device_error(dev)}
+    # decode-shaped steps are HBM-bound: 136 B per history token and kv head (64 B of K codes,
+    # 64 B of V codes, 8 B of scale / zero), against the measured copy bandwidth
+    hist_bytes = 136.0 * sum(spec["prefixes"]) * spec["hk"]
+    hbm = json.loads(peaks.read_text()).get("hbm_gbs") if peaks.exists() else None
+    line["history_gbs"] = hist_bytes / (ms * 1e-3) / 1e9
+    line["history_frac_of_hbm"] = line["history_gbs"] / hbm if hbm else None
     if sdpa and not any(spec["prefixes"]) and len(spec["lengths"]) == 1:
         import torch.nn.functional as F
 
@@ -216,5 +238,6 @@ if __name__ == "__main__":
     ap.add_argument("--path", default="auto", choices=["auto", "tensor", "decode", "tile"])
     ap.add_argument("--prefixes", type=int, default=None, help="override every request's history length")
     ap.add_argument("--sdpa", action="store_true", help="prefix-free prefill: also time torch SDPA on the same q/k/v")
+    ap.add_argument("--flush", action="store_true", help="time each call alone after evicting L2")
     a = ap.parse_args()
-    _run(a.run, a.calls, a.lengths, a.path, a.prefixes, a.sdpa)
+    _run(a.run, a.calls, a.lengths, a.path, a.prefixes, a.sdpa, a.flush)
