@@ -585,6 +585,7 @@ int run_decode_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs,
     plans.push_back(plan_decode(reqs, b0, b1, oscar::kTcRows, base.hk, base.bs, target, ws_bytes, false,
                                 oscar::kTcStage, oscar::kTcMaxPages, oscar::kTcMaxStages));
     if (!plans.back().fits) return kDecodeNoFit;
+    if (plans.back().plan.total_items > 65535) return kDecodeNoFit;  // the grid's y extent holds the items
   }
   CUtensorMap tmk, tmv;
   const int box_y = std::min(base.bs, oscar::kTcStage);
