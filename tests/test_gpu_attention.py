@@ -71,6 +71,7 @@ SYNTH = [
     ([2500, 0, 130], [120, 90, 200], dict(hk=2, group=6, dtype=torch.float16)),  # 128-row q-blocks, fp16
     ([3000], [600], dict(hk=2, group=6, seed=5)),            # 128-row q-blocks, staged sink/recent
     ([700, 90], [120, 40], dict(hk=1, group=6, bs=32)),    # 128-row q-blocks over 32-token pages
+    ([2000], [300], dict(hk=2, group=6, fresh=False)),      # cache-only, 128-row q-blocks (pre-pass tiles)
     ([777], [5], dict(dtype=torch.float16, d=64, bs=16)),
     ([513], [4], dict(cache_dtype=torch.bfloat16, hk=2)),    # legacy bf16 geometry
     ([300, 200], [2, 3], dict(group=8, hk=2, d=64, bs=8)),
