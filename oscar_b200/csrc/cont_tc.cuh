@@ -32,7 +32,8 @@
 // With a pre-pass (kEff: ct_expand_kernel wrote every tile of the request's keys
 //   once, in this layout, to the workspace) there are no loader warps: the MMA
 //   issuer is warp 4, and a producer warp (warp 5) fetches each tile with two
-//   32 KB bulk copies (192 threads).
+//   32 KB bulk copies (192 threads); both run straight-line loops on suspending
+//   waits, leaving the issue slots of their SM sub-partitions to the softmax.
 // Every wait is bounded; a timeout flags the error, and the CTA drains.
 //
 // Dim order inside each 16-dim group (both operands of Q K^T, and the N index of
@@ -477,19 +478,9 @@ __global__ void __launch_bounds__(kEff ? kCtEffThreads : kCtThreads, 1) cont_tc_
 #pragma unroll 1
     for (; rf < ntiles; ++rf) {
       const int st = rf % kCtStages;
-      if (rf >= kCtStages) {
-        bool ready = false;
-        for (uint32_t n = 0; !ready; ++n) {
-          ready = __shfl_sync(0xffffffffu, (int)tc::mbar_test(b_empty + 8 * st, ((rf / kCtStages) - 1) & 1), 0) != 0;
-          if (ready) break;
-          if (__shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&sm.abort), 0) != 0) break;
-          if (n > 4 * tc::kSpinLimit) {
-            if (lane == 0) give_up(16u);
-            break;
-          }
-        }
-        if (!ready) break;
-      }
+      // (a suspending, bounded wait: the warp takes no issue slots from the softmax warps
+      // of its SM sub-partition meanwhile)
+      if (rf >= kCtStages && !__all_sync(0xffffffffu, wait(b_empty + 8 * st, ((rf / kCtStages) - 1) & 1))) break;
       if (tc::elect_one()) {
         const uint8_t* src = eff0 + (int64_t)rf * a.hk * (2 * kTileBytes);
         tc::mbar_expect_tx(b_full + 8 * st, 2 * kTileBytes);
@@ -511,9 +502,54 @@ __global__ void __launch_bounds__(kEff ? kCtEffThreads : kCtThreads, 1) cont_tc_
     const uint64_t dk0 = tc::smem_desc(smem_u32(sm.k[0]), 128, kCtKSbo);
     const uint64_t dv0 = tc::smem_desc(smem_u32(sm.v[0]), 128, kCtVSbo);
     const uint64_t dp0 = tc::smem_desc(smem_u32(sm.p[0]), 128, kCtPSbo);
+    auto issue_qk = [&](int qs) {  // S[qs & 1] = Q K^T of tile qs
+      tc::tc_fence_after();
+      const uint64_t dka = dk0 + (uint64_t)((qs % kCtStages) * (sizeof(sm.k[0]) >> 4));
+      const uint32_t d_s = tmem + kCtColS + 64 * (qs & 1);
+      if (tc::elect_one()) {
+#pragma unroll
+        for (int j = 0; j < D / 16; ++j) tc::mma_ts(d_s, tmem + kCtColQ + 8 * j, dka + 16 * j, idesc_qk, j > 0 ? 1u : 0u);
+        tc::mma_commit(b_s + 8 * (qs & 1));
+      }
+      __syncwarp();
+    };
+    auto issue_pv = [&](int ps) {  // O += P V of tile ps; its commits release the stage and mark O
+      tc::tc_fence_after();
+      const uint64_t dva = dv0 + (uint64_t)((ps % kCtStages) * (sizeof(sm.v[0]) >> 4));
+      const uint64_t dpa = dp0 + (uint64_t)((ps & 1) * (sizeof(sm.p[0]) >> 4));
+      if (tc::elect_one()) {
+#pragma unroll
+        for (int j = 0; j < kCtKeys / 16; ++j)
+          tc::mma_ss(tmem + kCtColO, dpa + 16 * j, dva + 16 * j, idesc_pv, (ps > 0 || j > 0) ? 1u : 0u);
+        tc::mma_commit(b_empty + 8 * (ps % kCtStages));
+        tc::mma_commit(b_o + 8 * (ps & 1));
+      }
+      __syncwarp();
+    };
+    if (kEff) {
+      // tiles arrive by bulk copy well ahead, so the order is fixed: QK(0), QK(1), then per
+      // tile PV(t) and QK(t + 2).  Suspending, bounded waits leave the issue slots of this
+      // SM sub-partition to its softmax warp.
+#pragma unroll 1
+      for (int t = 0; t < min(2, ntiles); ++t) {
+        if (!__all_sync(0xffffffffu, wait(b_full + 8 * (t % kCtStages), (t / kCtStages) & 1))) break;
+        issue_qk(t);
+      }
+#pragma unroll 1
+      for (int t = 0; t < ntiles; ++t) {
+        if (*reinterpret_cast<volatile int*>(&sm.abort) != 0) break;
+        if (!__all_sync(0xffffffffu, wait(b_p + 8 * (t & 1), (t >> 1) & 1))) break;
+        issue_pv(t);
+        const int q2 = t + 2;
+        if (q2 < ntiles) {
+          if (!__all_sync(0xffffffffu, wait(b_full + 8 * (q2 % kCtStages), (q2 / kCtStages) & 1))) break;
+          issue_qk(q2);
+        }
+      }
+    }
     uint32_t idle = 0;
 #pragma unroll 1
-    for (int qs = 0, ps = 0; ps < ntiles;) {
+    for (int qs = 0, ps = 0; !kEff && ps < ntiles;) {
       bool prog = false;
       if (ps < qs && __shfl_sync(0xffffffffu, (int)tc::mbar_test(b_p + 8 * (ps & 1), (ps >> 1) & 1), 0)) {
         // O += P V of tile ps; its commits release the tile's stage and mark O
