@@ -27,13 +27,12 @@
 // Warps 4-11 (loaders): a thread fills one (key, 64-dim group) of a 64-key tile
 //   per stage: INT2 codes through 4-entry value tables (PRMT look-ups), fp32
 //   staged rows, or bf16/fp16 current-chunk rows.  Three tile stages.
-// Warp 12: MMA issuer, an event loop over two queues (QK of the next loaded tile
-//   once its S buffer is free; PV of the tile whose P is written).
+// Warp 12: MMA issuer, in the fixed order QK(0), QK(1), then per tile PV(t) once
+//   its P is written and QK(t + 2) once its tile is loaded, on suspending waits.
 // With a pre-pass (kEff: ct_expand_kernel wrote every tile of the request's keys
 //   once, in this layout, to the workspace) there are no loader warps: the MMA
 //   issuer is warp 4, and a producer warp (warp 5) fetches each tile with two
-//   32 KB bulk copies (192 threads); both run straight-line loops on suspending
-//   waits, leaving the issue slots of their SM sub-partitions to the softmax.
+//   32 KB bulk copies (192 threads), also on suspending waits.
 // Every wait is bounded; a timeout flags the error, and the CTA drains.
 //
 // Dim order inside each 16-dim group (both operands of Q K^T, and the N index of
@@ -526,10 +525,10 @@ __global__ void __launch_bounds__(kEff ? kCtEffThreads : kCtThreads, 1) cont_tc_
       }
       __syncwarp();
     };
-    if (kEff) {
-      // tiles arrive by bulk copy well ahead, so the order is fixed: QK(0), QK(1), then per
-      // tile PV(t) and QK(t + 2).  Suspending, bounded waits leave the issue slots of this
-      // SM sub-partition to its softmax warp.
+    {
+      // a fixed order: QK(0), QK(1), then per tile PV(t) and QK(t + 2) (S[t & 1] is free once
+      // PV(t) is issued: the softmax of tile t has read it).  Suspending, bounded waits leave
+      // the issue slots of this SM sub-partition to its softmax warp.
 #pragma unroll 1
       for (int t = 0; t < min(2, ntiles); ++t) {
         if (!__all_sync(0xffffffffu, wait(b_full + 8 * (t % kCtStages), (t / kCtStages) & 1))) break;
@@ -545,50 +544,6 @@ __global__ void __launch_bounds__(kEff ? kCtEffThreads : kCtThreads, 1) cont_tc_
           if (!__all_sync(0xffffffffu, wait(b_full + 8 * (q2 % kCtStages), (q2 / kCtStages) & 1))) break;
           issue_qk(q2);
         }
-      }
-    }
-    uint32_t idle = 0;
-#pragma unroll 1
-    for (int qs = 0, ps = 0; !kEff && ps < ntiles;) {
-      bool prog = false;
-      if (ps < qs && __shfl_sync(0xffffffffu, (int)tc::mbar_test(b_p + 8 * (ps & 1), (ps >> 1) & 1), 0)) {
-        // O += P V of tile ps; its commits release the tile's stage and mark O
-        tc::tc_fence_after();
-        const uint64_t dva = dv0 + (uint64_t)((ps % kCtStages) * (sizeof(sm.v[0]) >> 4));
-        const uint64_t dpa = dp0 + (uint64_t)((ps & 1) * (sizeof(sm.p[0]) >> 4));
-        if (tc::elect_one()) {
-#pragma unroll
-          for (int j = 0; j < kCtKeys / 16; ++j)
-            tc::mma_ss(tmem + kCtColO, dpa + 16 * j, dva + 16 * j, idesc_pv, (ps > 0 || j > 0) ? 1u : 0u);
-          tc::mma_commit(b_empty + 8 * (ps % kCtStages));
-          tc::mma_commit(b_o + 8 * (ps & 1));
-        }
-        __syncwarp();
-        ++ps;
-        prog = true;
-      }
-      if (qs < ntiles && qs < ps + 2 &&
-          __shfl_sync(0xffffffffu, (int)tc::mbar_test(b_full + 8 * (qs % kCtStages), (qs / kCtStages) & 1), 0)) {
-        // S[qs & 1] = Q K^T of tile qs (S[qs & 1] was read by the softmax of tile qs - 2)
-        tc::tc_fence_after();
-        const uint64_t dka = dk0 + (uint64_t)((qs % kCtStages) * (sizeof(sm.k[0]) >> 4));
-        const uint32_t d_s = tmem + kCtColS + 64 * (qs & 1);
-        if (tc::elect_one()) {
-#pragma unroll
-          for (int j = 0; j < D / 16; ++j) tc::mma_ts(d_s, tmem + kCtColQ + 8 * j, dka + 16 * j, idesc_qk, j > 0 ? 1u : 0u);
-          tc::mma_commit(b_s + 8 * (qs & 1));
-        }
-        __syncwarp();
-        ++qs;
-        prog = true;
-      }
-      if (prog) {
-        idle = 0;
-      } else if (__shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&sm.abort), 0) != 0) {
-        break;  // another warp timed out: drain
-      } else if (++idle > 4 * tc::kSpinLimit) {
-        if (lane == 0) give_up(16u);
-        break;
       }
     }
     // no MMA may be in flight when the tensor memory is freed
