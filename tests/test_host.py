@@ -21,7 +21,18 @@ def test_config_defaults_and_validation(monkeypatch):
     cfg = config.OscarConfig.from_env()
     assert (cfg.sink_tokens, cfg.recent_tokens, cfg.staging_tokens) == (64, 256, 8192)
     assert cfg.attention_mode == "streaming" and cfg.window_enabled
-    assert cfg.stream_workspace_bytes == 32 * 1024 * 1024
+    # 128 MiB (the reference's 32 would push long continuations off the pre-pass path)
+    assert cfg.stream_workspace_bytes == 128 * 1024 * 1024
+    assert config.OscarConfig.from_env(environ={"OSCAR_ASCEND_STREAM_WORKSPACE_MIB": "32"}).stream_workspace_bytes \
+        == 32 * 1024 * 1024
+    # blank / unparsable numbers keep the default, negative counts clamp to 0
+    odd = config.OscarConfig.from_env(environ={"OSCAR_ASCEND_SINK_TOKENS": " ", "OSCAR_ASCEND_RECENT_TOKENS": "x",
+                                               "OSCAR_ASCEND_STAGING_TOKENS": "-5"})
+    assert (odd.sink_tokens, odd.recent_tokens, odd.staging_tokens, odd.window_enabled) == (64, 256, 0, False)
+    with pytest.raises(ValueError, match="native"):
+        config.OscarConfig.from_env(environ={"OSCAR_ASCEND_ATTENTION_MODE": "native"})
+    with pytest.raises(ValueError, match="streaming or native"):
+        config.OscarConfig.from_env(environ={"OSCAR_ASCEND_ATTENTION_MODE": "dense"})
     monkeypatch.setenv("OSCAR_ASCEND_K_CLIP_RATIO", "1.5")
     with pytest.raises(ValueError, match="clip ratios"):
         config.OscarConfig.from_env()
