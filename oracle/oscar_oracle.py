@@ -327,13 +327,15 @@ def validate_layout(q, k_new, kc_shape, bt, qsl, seqs, stage):
 
 
 def streaming_attention(q, k_new, v_new, k8, v8, bt, qsl, seqs, scale, stage=None, *,
-                        dtype="bf16", kv_tile=128, query_tile=32):
+                        dtype="bf16", kv_tile=128, query_tile=32, rows=None):
     """kernels/streaming_attention.streaming_attention_ref (streaming_attention.py:134-196).
 
     Exact fp32 online softmax over [paged INT2 history with staged overrides]
     followed by the causal current chunk.  Returns rotated-space output
     [n, Hq, D] fp32 and natural-log LSE [n, Hq] (scale included).  Queries that
-    see no key produce 0 and -inf."""
+    see no key produce 0 and -inf.  ``rows`` (economy for large test cases): a
+    list of [start, end) query-row ranges; only query tiles meeting one are
+    computed, the other rows stay 0 / -inf."""
     q = np.asarray(q, F32)
     n, hq, d = q.shape
     hk = k8.shape[2]
@@ -349,6 +351,8 @@ def streaming_attention(q, k_new, v_new, k8, v8, bt, qsl, seqs, scale, stage=Non
         newv = None if v_new is None else np.asarray(v_new, F32)[a:b]
         for qa in range(a, b, query_tile):
             qb = min(qa + query_tile, b)
+            if rows is not None and not any(r0 < qb and qa < r1 for r0, r1 in rows):
+                continue
             qpart = q[qa:qb].transpose(1, 0, 2)  # [hq, nq, d]
             ends = seq - (b - a) + np.arange(qa - a, qb - a) + 1
             maximum = np.full((hq, qb - qa), -np.inf, F32)

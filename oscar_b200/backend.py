@@ -5,8 +5,9 @@ the plugin swaps ``layer.impl.__class__`` to a subclass of the impl's own
 class with :class:`OscarAttentionImplMixin` in front (see plugin.py), so only
 ``forward`` / ``do_kv_cache_update`` and the OSCAR store / staging / read
 paths change.  Everything on the device runs in the CUDA kernels of
-``csrc/`` through :mod:`oscar_b200.kernels`; the rotations are plain cuBLAS
-GEMMs.  There is no dense-history path and no CPU fallback.
+``csrc/`` through :mod:`oscar_b200.kernels`, the per-layer rotations
+included (``csrc/rotate.cuh``).  There is no dense-history path and no CPU
+fallback.
 """
 from __future__ import annotations
 

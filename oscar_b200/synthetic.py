@@ -52,16 +52,29 @@ def _outliers(x: torch.Tensor, factor: float = 20.0) -> torch.Tensor:
 
 def make_case(prefixes, lengths, *, hk=1, group=6, d=256, dtype=torch.bfloat16, cache_dtype=torch.int8, bs=128,
               window=True, fresh=True, seed=117, outliers=True, sink=128, recent=256, staging_tokens=8192,
-              device="cpu", extra_blocks=0) -> Case:
+              device="cpu", extra_blocks=0, compact=False, headroom=0) -> Case:
     """Build one case.  Caches are allocated zeroed; fill them with
-    :func:`fill_caches` (device kernel) or with the CPU oracle in tests."""
+    :func:`fill_caches` (device kernel) or with the CPU oracle in tests.
+    ``compact`` allocates only the pages the requests use (plus ``headroom``
+    tokens of growth each) instead of a full-width block table per request;
+    unused block-table entries are 0."""
     gen = torch.Generator(device=device).manual_seed(seed)
     hq = hk * group
     seqs = [p + n if fresh else p for p, n in zip(prefixes, lengths)]
-    width = max(16, math.ceil(max(seqs, default=0) / bs / 16) * 16)
-    blocks = len(seqs) * width + extra_blocks
-    perm = torch.randperm(blocks, generator=gen, device=device)
-    bt = perm[: len(seqs) * width].reshape(len(seqs), width).to(torch.int32)
+    width = max(16, math.ceil((max(seqs, default=0) + headroom) / bs / 16) * 16)
+    if compact:
+        need = [math.ceil((s_ + headroom) / bs) for s_ in seqs]
+        blocks = sum(need) + extra_blocks
+        perm = torch.randperm(blocks, generator=gen, device=device).to(torch.int32)
+        bt = torch.zeros(len(seqs), width, dtype=torch.int32, device=device)
+        off = 0
+        for r, n_ in enumerate(need):
+            bt[r, :n_] = perm[off:off + n_]
+            off += n_
+    else:
+        blocks = len(seqs) * width + extra_blocks
+        perm = torch.randperm(blocks, generator=gen, device=device)
+        bt = perm[: len(seqs) * width].reshape(len(seqs), width).to(torch.int32)
     kc = torch.zeros(blocks, bs, hk, d, dtype=cache_dtype, device=device)
     vc = torch.zeros_like(kc)
     qsl, slots = [0], []
@@ -140,104 +153,3 @@ def attention_flops(prefixes, lengths, hq: int, d: int) -> float:
     (N (N + 1) / 2)."""
     pairs = sum(n * c + n * (n + 1) // 2 for c, n in zip(prefixes, lengths))
     return 4.0 * hq * d * pairs
-
-
-def _run(name: str, calls: int, lengths_override: int | None, path: str = "auto", prefixes_override: int | None = None,
-         sdpa: bool = False, flush: bool = False) -> None:
-    """Time ``slab_attention`` on one BASELINE configuration on cuda:0 (CUDA
-    events around ``calls`` back-to-back calls after two warm-up calls) and
-    print one JSON line with the algorithmic TFLOP/s; the committed runner of
-    the continuation profiles.  ``path`` selects the kernel family
-    (:func:`kernels.set_attention_path`).  With ``sdpa`` and no history (prefix-free
-    prefill), torch's scaled_dot_product_attention on the same causal q/k/v is timed
-    beside it, as the library attention a prefix-free prefill could otherwise use.  With
-    ``flush`` every call is timed alone after an L2 eviction (decode-shaped configs, whose
-    caches would otherwise stay in L2 between calls)."""
-    import json
-    from pathlib import Path
-
-    from . import kernels
-
-    kernels.set_attention_path(path)
-    spec = dict(BASELINE_CONFIGS[name])
-    if lengths_override:
-        spec["lengths"] = [lengths_override] * len(spec["lengths"])
-    if prefixes_override is not None:
-        spec["prefixes"] = [prefixes_override] * len(spec["prefixes"])
-    dev = torch.device("cuda", 0)
-    case = make_case(spec["prefixes"], spec["lengths"], hk=spec["hk"], group=spec["group"], device=dev)
-    fill_caches(case)
-    args = (case.q, case.k_new, case.v_new, case.kc, case.vc, case.bt, case.qsl, case.seqs, case.scale, case.stage)
-    for _ in range(2):
-        kernels.slab_attention(*args)
-    torch.cuda.synchronize(dev)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if flush:
-        # each call timed alone, after a 512 MiB write that evicts the 126 MB L2
-        scrub = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
-        ms = 0.0
-        for _ in range(calls):
-            scrub.zero_()
-            start.record()
-            kernels.slab_attention(*args)
-            end.record()
-            torch.cuda.synchronize(dev)
-            ms += start.elapsed_time(end)
-        ms /= calls
-        del scrub
-    else:
-        start.record()
-        for _ in range(calls):
-            kernels.slab_attention(*args)
-        end.record()
-        torch.cuda.synchronize(dev)
-        ms = start.elapsed_time(end) / calls
-    hq = spec["hk"] * spec["group"]
-    flops = attention_flops(spec["prefixes"], spec["lengths"], hq, case.q.shape[-1])
-    peaks = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
-    peak = json.loads(peaks.read_text()).get("bf16_tflops") if peaks.exists() else None
-    tflops = flops / (ms * 1e-3) / 1e12
-    line = {"workload": name, "path": path, "l2_flushed": flush, "prefixes": spec["prefixes"][:4], "lengths": spec["lengths"][:4],
-            "ms_per_call": ms, "tflops": tflops, "peak_bf16_tflops": peak, "frac": tflops / peak if peak else None,
-            "device_error": kernels.device_error(dev)}
-    # decode-shaped steps are HBM-bound: 136 B per history token and kv head (64 B of K codes,
-    # 64 B of V codes, 8 B of scale / zero), against the measured copy bandwidth
-    hist_bytes = 136.0 * sum(spec["prefixes"]) * spec["hk"]
-    hbm = json.loads(peaks.read_text()).get("hbm_gbs") if peaks.exists() else None
-    line["history_gbs"] = hist_bytes / (ms * 1e-3) / 1e9
-    line["history_frac_of_hbm"] = line["history_gbs"] / hbm if hbm else None
-    if sdpa and not any(spec["prefixes"]) and len(spec["lengths"]) == 1:
-        import torch.nn.functional as F
-
-        q = case.q.transpose(0, 1).unsqueeze(0)  # [1, Hq, n, D]
-        k = case.k_new.transpose(0, 1).unsqueeze(0)
-        v = case.v_new.transpose(0, 1).unsqueeze(0)
-        run = lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=case.scale,  # noqa: E731
-                                                     enable_gqa=True)
-        for _ in range(2):
-            run()
-        torch.cuda.synchronize(dev)
-        start.record()
-        for _ in range(calls):
-            run()
-        end.record()
-        torch.cuda.synchronize(dev)
-        ms_lib = start.elapsed_time(end) / calls
-        line["sdpa_ms_per_call"] = ms_lib
-        line["sdpa_tflops"] = flops / (ms_lib * 1e-3) / 1e12
-    print(json.dumps(line), flush=True)
-
-
-if __name__ == "__main__":
-    import argparse
-
-    ap = argparse.ArgumentParser(description="time slab_attention on a BASELINE configuration")
-    ap.add_argument("--run", required=True, choices=sorted(BASELINE_CONFIGS))
-    ap.add_argument("--calls", type=int, default=5)
-    ap.add_argument("--lengths", type=int, default=None, help="override every request's new-token count")
-    ap.add_argument("--path", default="auto", choices=["auto", "tensor", "decode", "tile"])
-    ap.add_argument("--prefixes", type=int, default=None, help="override every request's history length")
-    ap.add_argument("--sdpa", action="store_true", help="prefix-free prefill: also time torch SDPA on the same q/k/v")
-    ap.add_argument("--flush", action="store_true", help="time each call alone after evicting L2")
-    a = ap.parse_args()
-    _run(a.run, a.calls, a.lengths, a.path, a.prefixes, a.sdpa, a.flush)

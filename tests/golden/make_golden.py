@@ -6,7 +6,7 @@ CPU path (``OSCAR_ASCEND_USE_TRITON=0``) is the parity oracle for this build.
 ``vllm``, ``vllm_ascend`` and ``torch_npu`` are masked in ``sys.modules`` so the
 reference selects its CPU placeholders (oscar_ascend/backend.py:68-85).
 
-Usage:  python tests/golden/make_golden.py [REFERENCE_ROOT]
+Usage:  python tests/golden/make_golden.py REFERENCE_ROOT   (or OSCAR_REFERENCE=...)
 Writes ``tests/golden/*.npz``; the committed fixtures are what the tests read.
 """
 from __future__ import annotations
@@ -363,7 +363,9 @@ def gen_backend(ref, torch):
 
 
 def main():
-    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("OSCAR_REFERENCE", "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("OSCAR_REFERENCE")
+    if not root:
+        sys.exit("usage: python tests/golden/make_golden.py REFERENCE_ROOT (or set OSCAR_REFERENCE)")
     ref = _import_reference(root)
     import torch
 
