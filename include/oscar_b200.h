@@ -186,6 +186,33 @@ int oscar_slab_attention(const void* q, const void* k_new, const void* v_new, in
                          void* workspace, int64_t workspace_bytes,
                          void* stream);
 
+/* History-shard attention: the partial (O, LSE) of q over one shard of the
+ * paged history, for split-KV across GPUs (each rank holds a page-aligned
+ * range of every request's history; the ranks' partials are combined with
+ * oscar_merge_slab).  No counterpart entry in the reference: it is the
+ * slab loop of kernels/slab_attention.py:458-475 with the slabs of one
+ * shard only.  Every key of [0, history_lens[r]) (through block_table row
+ * r) is visible to every query row of request r -- the shard holds no keys
+ * of the current chunk, which the owner adds in its own pass.  Arguments as
+ * oscar_slab_attention without k_new / v_new; history_lens is a HOST int32
+ * array.  Runs on the decode kernels only: head_dim 256 and at most 32
+ * query rows (q_len x query heads per KV head) per request and KV head,
+ * else ERR_UNSUPPORTED. */
+int oscar_slab_attention_shard(const void* q, int32_t dtype,
+                               int64_t n_tokens, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                               const uint8_t* k_cache, const uint8_t* v_cache, int64_t num_blocks,
+                               int32_t block_size,
+                               int64_t k_stride_block, int64_t k_stride_token, int64_t k_stride_head,
+                               int64_t v_stride_block, int64_t v_stride_token, int64_t v_stride_head,
+                               const int32_t* block_table, int64_t bt_rows, int64_t bt_stride,
+                               const int32_t* qsl, const int32_t* history_lens, int32_t num_requests,
+                               float scale,
+                               const float* stage_k, const float* stage_v, const int64_t* owner,
+                               int64_t stage_rows,
+                               float* out, float* lse,
+                               void* workspace, int64_t workspace_bytes,
+                               void* stream);
+
 /* Workspace bytes the planner would use: full split-KV parallelism, plus
  * the continuation pre-pass tiles where that path applies. */
 int64_t oscar_slab_attention_workspace(const int32_t* qsl, const int32_t* seqs, int32_t num_requests,

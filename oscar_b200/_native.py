@@ -49,6 +49,9 @@ SIGNATURES = {
     "oscar_slab_attention": (ctypes.c_int, [_P, _P, _P, _I32, _I64, _I32, _I32, _I32, _P, _P, _I64, _I32,
                                             _I64, _I64, _I64, _I64, _I64, _I64, _P, _I64, _I64,
                                             _P, _P, _I32, _F32, _P, _P, _P, _I64, _P, _P, _P, _I64, _P]),
+    "oscar_slab_attention_shard": (ctypes.c_int, [_P, _I32, _I64, _I32, _I32, _I32, _P, _P, _I64, _I32,
+                                                  _I64, _I64, _I64, _I64, _I64, _I64, _P, _I64, _I64,
+                                                  _P, _P, _I32, _F32, _P, _P, _P, _I64, _P, _P, _P, _I64, _P]),
     "oscar_slab_attention_workspace": (ctypes.c_int64, [_P, _P, _I32, _I32, _I32, _I32, _I32]),
     "oscar_merge_slab": (ctypes.c_int, [_P, _P, _I64, _P, _I32, _P, _I64, _I32, _I32, _I64, _P, _P]),
     "oscar_rotate_rows": (ctypes.c_int, [_P, _I32, _I64, _I64, _I32, _P, _I32, _P, _I32, _I64, _P, _I64, _P]),

@@ -758,17 +758,21 @@ int collect_requests(const int32_t* qsl, const int32_t* seqs, int32_t num_reques
 
 }  // namespace
 
-extern "C" {
-
-int oscar_slab_attention(const void* q, const void* k_new, const void* v_new, int32_t dtype, int64_t n_tokens,
-                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, const uint8_t* k_cache,
-                         const uint8_t* v_cache, int64_t num_blocks, int32_t block_size, int64_t k_stride_block,
-                         int64_t k_stride_token, int64_t k_stride_head, int64_t v_stride_block,
-                         int64_t v_stride_token, int64_t v_stride_head, const int32_t* block_table, int64_t bt_rows,
-                         int64_t bt_stride, const int32_t* qsl, const int32_t* seqs, int32_t num_requests,
-                         float scale, const float* stage_k, const float* stage_v, const int64_t* owner,
-                         int64_t stage_rows, float* out, float* lse, void* workspace, int64_t workspace_bytes,
-                         void* stream) {
+// The body of oscar_slab_attention and oscar_slab_attention_shard.  A history
+// shard has no current chunk and every key of [0, seqs[r]) visible to every
+// query row: its plan carries seq = prefix + q_len (the causal limit
+// seq - q_len + t + 1 never falls below the prefix) and it runs on the decode
+// kernels, which read history only below the prefix and chunk keys only from
+// k_new.
+static int slab_attention_impl(const void* q, const void* k_new, const void* v_new, int32_t dtype, int64_t n_tokens,
+                               int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, const uint8_t* k_cache,
+                               const uint8_t* v_cache, int64_t num_blocks, int32_t block_size, int64_t k_stride_block,
+                               int64_t k_stride_token, int64_t k_stride_head, int64_t v_stride_block,
+                               int64_t v_stride_token, int64_t v_stride_head, const int32_t* block_table,
+                               int64_t bt_rows, int64_t bt_stride, const int32_t* qsl, const int32_t* seqs,
+                               int32_t num_requests, float scale, const float* stage_k, const float* stage_v,
+                               const int64_t* owner, int64_t stage_rows, float* out, float* lse, void* workspace,
+                               int64_t workspace_bytes, void* stream, bool shard) {
   if (num_q_heads < 1 || num_kv_heads < 1 || num_q_heads % num_kv_heads || n_tokens < 0 || block_size < 1)
     return fail(OSCAR_ERR_INVALID, "Invalid slab query layout");
   if ((k_new == nullptr) != (v_new == nullptr)) return fail(OSCAR_ERR_INVALID, "Both new K and V must be supplied together");
@@ -788,6 +792,12 @@ int oscar_slab_attention(const void* q, const void* k_new, const void* v_new, in
   int st = collect_requests(qsl, seqs, num_requests, n_tokens, has_new, bt_rows, bt_stride, block_size, reqs, max_q,
                             any_history);
   if (st) return st;
+  if (shard) {
+    if (head_dim != 256 || max_q * group > oscar::kTcRows)
+      return fail(OSCAR_ERR_UNSUPPORTED, "history shards run the decode kernels: head_dim 256 and at most %d query "
+                  "rows per KV group", oscar::kTcRows);
+    for (ReqInfo& r : reqs) r.seq = r.prefix + r.q_len;
+  }
   if (any_history) {
     if (!k_cache || !v_cache || !block_table) return fail(OSCAR_ERR_INVALID, "history requires caches and a block table");
     if (k_stride_head < 32 + head_dim / 4 || v_stride_head < head_dim / 4)
@@ -830,9 +840,57 @@ int oscar_slab_attention(const void* q, const void* k_new, const void* v_new, in
   a.out = out;
   a.lse = lse;
   if (reqs.empty()) return OSCAR_OK;
+  if (shard) {
+    const bool bf = dtype == OSCAR_DTYPE_BF16;
+    // family selector: 2 keeps the shard on the mma.sync decode kernel
+    if (g_attention_path.load() != 2 && tc_eligible(256, max_q * group, a)) {
+      st = bf ? run_decode_tc<__nv_bfloat16>(a, reqs, workspace, workspace_bytes, s)
+              : run_decode_tc<__half>(a, reqs, workspace, workspace_bytes, s);
+      if (st != kDecodeNoFit) return st;
+    }
+    if (decode_eligible(256, max_q * group, a)) {
+      st = bf ? run_decode_rows<__nv_bfloat16>(a, reqs, max_q * group, workspace, workspace_bytes, s)
+              : run_decode_rows<__half>(a, reqs, max_q * group, workspace, workspace_bytes, s);
+      if (st != kDecodeNoFit) return st;
+    }
+    return fail(OSCAR_ERR_UNSUPPORTED, "history shard: the decode kernels do not fit this layout");
+  }
   if (head_dim == 256) return dispatch_dtype<256>(dtype, a, reqs, max_q, workspace, workspace_bytes, s);
   if (head_dim == 128) return dispatch_dtype<128>(dtype, a, reqs, max_q, workspace, workspace_bytes, s);
   return dispatch_dtype<64>(dtype, a, reqs, max_q, workspace, workspace_bytes, s);
+}
+
+extern "C" {
+
+int oscar_slab_attention(const void* q, const void* k_new, const void* v_new, int32_t dtype, int64_t n_tokens,
+                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, const uint8_t* k_cache,
+                         const uint8_t* v_cache, int64_t num_blocks, int32_t block_size, int64_t k_stride_block,
+                         int64_t k_stride_token, int64_t k_stride_head, int64_t v_stride_block,
+                         int64_t v_stride_token, int64_t v_stride_head, const int32_t* block_table, int64_t bt_rows,
+                         int64_t bt_stride, const int32_t* qsl, const int32_t* seqs, int32_t num_requests,
+                         float scale, const float* stage_k, const float* stage_v, const int64_t* owner,
+                         int64_t stage_rows, float* out, float* lse, void* workspace, int64_t workspace_bytes,
+                         void* stream) {
+  return slab_attention_impl(q, k_new, v_new, dtype, n_tokens, num_q_heads, num_kv_heads, head_dim, k_cache, v_cache,
+                             num_blocks, block_size, k_stride_block, k_stride_token, k_stride_head, v_stride_block,
+                             v_stride_token, v_stride_head, block_table, bt_rows, bt_stride, qsl, seqs, num_requests,
+                             scale, stage_k, stage_v, owner, stage_rows, out, lse, workspace, workspace_bytes, stream,
+                             false);
+}
+
+int oscar_slab_attention_shard(const void* q, int32_t dtype, int64_t n_tokens, int32_t num_q_heads,
+                               int32_t num_kv_heads, int32_t head_dim, const uint8_t* k_cache, const uint8_t* v_cache,
+                               int64_t num_blocks, int32_t block_size, int64_t k_stride_block, int64_t k_stride_token,
+                               int64_t k_stride_head, int64_t v_stride_block, int64_t v_stride_token,
+                               int64_t v_stride_head, const int32_t* block_table, int64_t bt_rows, int64_t bt_stride,
+                               const int32_t* qsl, const int32_t* history_lens, int32_t num_requests, float scale,
+                               const float* stage_k, const float* stage_v, const int64_t* owner, int64_t stage_rows,
+                               float* out, float* lse, void* workspace, int64_t workspace_bytes, void* stream) {
+  return slab_attention_impl(q, nullptr, nullptr, dtype, n_tokens, num_q_heads, num_kv_heads, head_dim, k_cache,
+                             v_cache, num_blocks, block_size, k_stride_block, k_stride_token, k_stride_head,
+                             v_stride_block, v_stride_token, v_stride_head, block_table, bt_rows, bt_stride, qsl,
+                             history_lens, num_requests, scale, stage_k, stage_v, owner, stage_rows, out, lse,
+                             workspace, workspace_bytes, stream, true);
 }
 
 int64_t oscar_slab_attention_workspace(const int32_t* qsl, const int32_t* seqs, int32_t num_requests, int32_t has_new,

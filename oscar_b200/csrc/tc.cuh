@@ -71,6 +71,10 @@ OSCAR_DEVINL void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint3
                "l"(src), "r"(bytes), "r"(bar)
                : "memory");
 }
+// bring `bytes` (a multiple of 16, 16-byte aligned) of global memory into L2
+OSCAR_DEVINL void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(src), "r"(bytes) : "memory");
+}
 OSCAR_DEVINL void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
 // ---------------------------------------------------------------- named barriers
@@ -117,6 +121,13 @@ OSCAR_DEVINL void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
+}
+// one 32-bit column of 32 lanes: thread i writes / reads lane (taddr.lane + i)
+OSCAR_DEVINL void tmem_st1(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};\n" ::"r"(taddr), "r"(v) : "memory");
+}
+OSCAR_DEVINL void tmem_ld1(uint32_t taddr, uint32_t& v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n" : "=r"(v) : "r"(taddr) : "memory");
 }
 OSCAR_DEVINL void tmem_st8(uint32_t taddr, const uint32_t* r) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"r"(taddr),

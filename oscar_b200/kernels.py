@@ -6,6 +6,8 @@ Mirrors the reference's kernel entry points for the hot path:
   * ``staging_write``     backend.py:513-555
   * ``slab_attention``    kernels/slab_attention.py:376-476 (semantics of
                           kernels/streaming_attention.py:134-196)
+  * ``slab_attention_shard`` one history shard of slab_attention.py:458-475
+                          (split-KV across GPUs)
   * ``merge_slab``        kernels/slab_attention.py:341-373
 
 Layout problems raise ValueError with the reference's messages; every call
@@ -286,6 +288,60 @@ def slab_attention(q, k_new, v_new, kc, vc, table, qsl, seqs, scale, stage=None,
         k8.data_ptr(), v8.data_ptr(), k8.shape[0], k8.shape[1], *k8.stride()[:3], *v8.stride()[:3],
         table.data_ptr(), table.shape[0], table.stride(0), qsl_p, seqs_p, len(seqs), float(scale),
         _ptr(sk), _ptr(sv), _ptr(owner), rows, out.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws_bytes,
+        _stream(dev)))
+    return out, lse
+
+
+def slab_attention_shard(q, kc, vc, table, qsl, history_lens, scale, stage=None, *,
+                         workspace_bytes: int = DEFAULT_WORKSPACE_BYTES):
+    """Partial attention of rotated queries over one shard of the paged
+    history: request r's keys [0, history_lens[r]) through table row r, all of
+    them visible to all of its queries, no current chunk.  Returns (out, lse)
+    like ``slab_attention``; shards of one history are combined with
+    ``merge_slab`` (the split-KV merge of slab_attention.py:458-475 across
+    GPUs).  Decode-sized steps at head dim 256 only (the tensor-core decode
+    kernel or the CUDA-core decode kernel); other layouts raise ValueError."""
+    qsl = [int(x) for x in qsl]
+    hist = [int(x) for x in history_lens]
+    if (q.ndim != 3 or kc.ndim != 4 or q.shape[1] < 1 or kc.shape[2] < 1 or len(qsl) != len(hist) + 1
+            or not qsl or qsl[0] != 0 or qsl[-1] != q.shape[0] or q.shape[1] % kc.shape[2]):
+        raise ValueError("Invalid slab query layout")
+    if any(a > b or h < 0 for a, b, h in zip(qsl, qsl[1:], hist)):
+        raise ValueError("Sequence length must cover its query chunk")
+    _validate_tensors(q, None, None, kc, vc, table, qsl, hist, stage)
+    dev = _require_cuda(q, kc, vc, table, *(stage or ()))
+    if q.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"unsupported query dtype {q.dtype}")
+    n, hq, d = q.shape
+    hk = kc.shape[2]
+    q = q.contiguous()
+    table = table.to(device=dev, dtype=torch.int32).contiguous()
+    k8, v8 = _byte_view(kc), _byte_view(vc)
+    sk = sv = owner = None
+    rows = 0
+    if stage is not None:
+        sk, sv, owner = stage
+        if sk.dtype != torch.float32 or sv.dtype != torch.float32 or owner.dtype != torch.int64:
+            raise ValueError("staging arena must be fp32 K/V and int64 owner tags")
+        rows = owner.shape[0]
+    out = torch.empty(n, hq, d, dtype=torch.float32, device=dev)
+    lse = torch.empty(n, hq, dtype=torch.float32, device=dev)
+    if n == 0:
+        return out, lse
+    lib = _native.lib()
+    qsl_a = np.ascontiguousarray(qsl, dtype=np.int32)
+    hist_a = np.ascontiguousarray(hist, dtype=np.int32)
+    # the shard's plan is the one of a step with the history as prefix and the
+    # queries as its chunk
+    seqs_a = np.ascontiguousarray([h + b - a for h, a, b in zip(hist, qsl, qsl[1:])], dtype=np.int32)
+    need = lib.oscar_slab_attention_workspace(qsl_a.ctypes.data, seqs_a.ctypes.data, len(hist), 1, hq, hk, d)
+    ws_bytes = max(0, min(int(need), int(workspace_bytes)))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    check(lib.oscar_slab_attention_shard(
+        q.data_ptr(), _DTYPES[q.dtype], n, hq, hk, d,
+        k8.data_ptr(), v8.data_ptr(), k8.shape[0], k8.shape[1], *k8.stride()[:3], *v8.stride()[:3],
+        table.data_ptr(), table.shape[0], table.stride(0), qsl_a.ctypes.data, hist_a.ctypes.data, len(hist),
+        float(scale), _ptr(sk), _ptr(sv), _ptr(owner), rows, out.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws_bytes,
         _stream(dev)))
     return out, lse
 
