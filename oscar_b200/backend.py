@@ -11,6 +11,7 @@ fallback.
 """
 from __future__ import annotations
 
+import abc
 from itertools import pairwise
 
 import numpy as np
@@ -84,7 +85,7 @@ def _device_batch(attn_metadata, qsl: list, seqs: list, device) -> tuple:
     return _device_ints(qsl, device), _device_ints(seqs[:b], device)
 
 
-class OscarAttentionImplMixin:
+class OscarAttentionImplMixin(metaclass=abc.ABCMeta):
     """The OSCAR read/write/window paths.  Placed first in the MRO of a
     subclass of the running vLLM attention impl (plugin.install_impl)."""
 

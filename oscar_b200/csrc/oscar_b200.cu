@@ -413,7 +413,7 @@ struct DecodePlanned {
 // hold all of them.
 DecodePlanned plan_decode(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1, int rows, int hk, int bs,
                           int target, int64_t ws_bytes, bool staged, int stage = oscar::kDecStage,
-                          int max_pages = oscar::kDecMaxPages, int max_stages = 1 << 20) {
+                          int max_pages = oscar::kDecMaxPages, int max_stages = 1 << 20, bool one_wave = false) {
   DecodePlanned out{};
   oscar::AttnPlan& p = out.plan;
   p.num_req = (int)(b1 - b0);
@@ -457,8 +457,17 @@ DecodePlanned plan_decode(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1
     p.total_merge_rows = 0;
     out.part_bytes = part_bytes;
     out.fits = part_bytes <= ws_bytes;
-    if (out.fits || (all_single && budget >= max_chunk_stages)) break;
-    budget *= 2;
+    if (!out.fits && !(all_single && budget >= max_chunk_stages)) {
+      budget *= 2;
+      continue;
+    }
+    // one CTA per SM: a grid larger than the target runs a second wave behind the
+    // first, so the step takes two chunk times; longer chunks in one wave are faster
+    if (one_wave && out.fits && !all_single && (int64_t)items * hk > target && per < max_chunk_stages) {
+      ++budget;
+      continue;
+    }
+    break;
   }
   return out;
 }
@@ -583,7 +592,7 @@ int run_decode_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs,
   for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
     const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
     plans.push_back(plan_decode(reqs, b0, b1, oscar::kTcRows, base.hk, base.bs, target, ws_bytes, false,
-                                oscar::kTcStage, oscar::kTcMaxPages, oscar::kTcMaxStages));
+                                oscar::kTcStage, oscar::kTcMaxPages, oscar::kTcMaxStages, true));
     if (!plans.back().fits) return kDecodeNoFit;
     if (plans.back().plan.total_items > 65535) return kDecodeNoFit;  // the grid's y extent holds the items
   }

@@ -9,12 +9,16 @@ A shadow-pool failure raises (never silently writes bf16 into an int8 pool).
 """
 from __future__ import annotations
 
+import abc
+
 import torch
+
+from .surgery import compose
 
 _CLASSES: dict = {}
 
 
-class MTPShadowMixin:
+class MTPShadowMixin(metaclass=abc.ABCMeta):
     def _shadow_kv(self, kv_cache):
         sh = getattr(self, "_oscar_shadow_kv", None)
         if sh is not None:
@@ -37,12 +41,12 @@ class MTPShadowMixin:
     def do_kv_cache_update(self, layer, key, value, kv_cache, slot_mapping):
         if self._needs_shadow(kv_cache):
             kv_cache = self._shadow_kv(kv_cache)
-        return super().do_kv_cache_update(layer, key, value, kv_cache, slot_mapping)
+        return self._oscar_base.do_kv_cache_update(self, layer, key, value, kv_cache, slot_mapping)
 
     def forward(self, layer, query, key, value, kv_cache, attn_metadata, *args, **kwargs):
         if self._needs_shadow(kv_cache):
             kv_cache = self._shadow_kv(kv_cache)
-        return super().forward(layer, query, key, value, kv_cache, attn_metadata, *args, **kwargs)
+        return self._oscar_base.forward(self, layer, query, key, value, kv_cache, attn_metadata, *args, **kwargs)
 
 
 def shadow_impl_class(base: type) -> type:
@@ -50,6 +54,6 @@ def shadow_impl_class(base: type) -> type:
         return base
     cls = _CLASSES.get(base)
     if cls is None:
-        cls = type(f"MTPShadow{base.__name__}", (MTPShadowMixin, base), {"__module__": __name__})
+        cls = compose(MTPShadowMixin, base, f"MTPShadow{base.__name__}", __name__)
         _CLASSES[base] = cls
     return cls

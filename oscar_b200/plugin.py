@@ -3,9 +3,9 @@
 Drop-in for oscar_ascend/plugin.py:60-267.  ``load_plugin()`` (no arguments,
 idempotent) wraps ``Attention.__init__`` with an after-hook.  For decoder
 FULL-attention layers of hybrid models the hook swaps ``layer.impl.__class__``
-to ``OscarImpl[<original impl class>]`` (OscarAttentionImplMixin in front of
-the original class), runs ``_oscar_setup()`` and rolls the instance back if
-setup fails.  MTP draft layers keep bf16 KV (optionally in a shadow pool,
+to ``OscarImpl[<original impl class>]`` (a subclass of the original class
+with the methods of OscarAttentionImplMixin in front, oscar_b200.surgery),
+runs ``_oscar_setup()`` and rolls the instance back if setup fails.  MTP draft layers keep bf16 KV (optionally in a shadow pool,
 OSCAR_ASCEND_PACKED=1); sliding-window, sink and non-decoder layers are
 skipped.  The Ascend platform bootstrap (plugin.py:27-57) has no CUDA
 counterpart and is not part of this package.
@@ -26,12 +26,13 @@ _IMPL_CLASSES: dict = {}
 def oscar_impl_class(base: type) -> type:
     """Subclass of the running impl class with the OSCAR paths in front (cached)."""
     from .backend import OscarAttentionImplMixin
+    from .surgery import compose
 
     if issubclass(base, OscarAttentionImplMixin):
         return base
     cls = _IMPL_CLASSES.get(base)
     if cls is None:
-        cls = type(f"Oscar{base.__name__}", (OscarAttentionImplMixin, base), {"__module__": __name__})
+        cls = compose(OscarAttentionImplMixin, base, f"Oscar{base.__name__}", __name__)
         _IMPL_CLASSES[base] = cls
     return cls
 
@@ -62,6 +63,16 @@ def _is_mtp_layer(layer_name: str) -> bool:
     return ".mtp." in layer_name or layer_name.startswith("mtp.")
 
 
+def _has_sliding_window(impl) -> bool:
+    """vLLM-CUDA impls encode "no window" as (-1, -1) (the Ascend impl as None)."""
+    window = getattr(impl, "sliding_window", None)
+    if window is None:
+        return False
+    if isinstance(window, (tuple, list)):
+        return any(w is not None and w >= 0 for w in window)
+    return True
+
+
 def _skip_reasons(impl, model_config) -> list[str]:
     reasons = []
     if not _is_hybrid_config(model_config):
@@ -70,7 +81,7 @@ def _skip_reasons(impl, model_config) -> list[str]:
     at_value = getattr(at, "value", at)
     if str(at_value) != "decoder":
         reasons.append(f"attn_type={at!r}")
-    if getattr(impl, "sliding_window", None) is not None:
+    if _has_sliding_window(impl):
         reasons.append("sliding-window")
     if getattr(impl, "sinks", None) is not None:
         reasons.append("sinks")
@@ -100,6 +111,24 @@ def _should_oscar(layer, impl, model_config=None) -> bool:
     return True
 
 
+def _install_worker_hooks() -> None:
+    """The worker seams (oscar_b200.integration) once an OSCAR layer exists
+    (plugin.py:150-151 of the reference); an engine without vLLM-CUDA's worker
+    classes runs without them."""
+    try:
+        from vllm.v1.worker.gpu_model_runner import GPUModelRunner
+        from vllm.v1.worker.gpu_worker import Worker
+    except ImportError as exc:  # pragma: no cover - depends on the engine build
+        if "worker-hooks" not in _SKIP_REASONS_LOGGED:
+            _SKIP_REASONS_LOGGED.add("worker-hooks")
+            _HEARTBEAT["errors"].append(f"worker hooks: {exc}")
+            print(f"[oscar-b200] vLLM-CUDA worker classes unavailable, memory seams not installed: {exc}")
+        return
+    from .integration import install_runner_hooks
+
+    install_runner_hooks(Worker, GPUModelRunner)
+
+
 def attach(attention_layer) -> bool:
     """The after-hook body for one constructed ``Attention`` layer."""
     impl = getattr(attention_layer, "impl", None)
@@ -114,6 +143,7 @@ def attach(attention_layer) -> bool:
     if not _should_oscar(attention_layer, impl):
         return False
     install_impl(impl, oscar_impl_class(impl.__class__))
+    _install_worker_hooks()
     _HEARTBEAT["loaded"] += 1
     _HEARTBEAT["layers"].append(f"{layer_name}:heads={impl.num_heads}/kv={impl.num_kv_heads}/d={impl.head_size}")
     return True
