@@ -274,6 +274,45 @@ typedef struct oscar_rotate_seg {
 int oscar_rotate_rows_batch(const oscar_rotate_seg* segs, int32_t n_segs, int32_t x_dtype, int32_t head_dim,
                             int32_t out_dtype, void* stream);
 
+/* ------------------------------------------------------------------------
+ * One FULL-attention layer step of a decode-sized batch in one call: the
+ * backend forward of backend.py:249-282 (streaming mode, staging window on)
+ * when every request has cached history, n_tokens <= 256 and
+ * num_requests <= 256.  No counterpart entry in the reference, where the
+ * forward is Python around its kernels; here the host cost of a decode step
+ * is one call.  In order, on `stream`:
+ *   1. k @ R_k and v @ R_v (fp32 rows for the store and the window, query
+ *      dtype rows for the attention) and q @ R_k (query dtype), one launch;
+ *   2. oscar_write_step of the step's tokens (clip + INT2 store + staging);
+ *   3. oscar_slab_attention over the history and the causal chunk, rotated;
+ *   4. o @ R_v^T into `out` in the query dtype.
+ * q [n, Hq, D], k / v [n, Hk, D]: heads contiguous, token rows q_stride /
+ * k_stride / v_stride elements apart (multiples of 8; e.g. views of a fused
+ * QKV projection); out [n, Hq * D] rows out_stride elements apart.  R_k, R_v
+ * and R_v^T are fp32 [D, D] row-major.  slot_mapping / qsl_dev / seqs_dev
+ * are device arrays (oscar_write_step), qsl / seqs the same on the HOST.
+ * scratch: device memory, 256-byte aligned, at least
+ * oscar_decode_layer_step_scratch() bytes for the step's rotated rows and
+ * attention output; bytes beyond that are the attention workspace
+ * (oscar_slab_attention's `workspace`).  A request without cached history
+ * returns ERR_UNSUPPORTED (its chunk attends in the model's domain). */
+int oscar_decode_layer_step(const void* q, const void* k, const void* v, int32_t dtype, int64_t q_stride,
+                            int64_t k_stride, int64_t v_stride, int64_t n_tokens, int32_t num_q_heads,
+                            int32_t num_kv_heads, int32_t head_dim, const float* rot_k, const float* rot_v,
+                            const float* rot_vt, float k_clip_ratio, float v_clip_ratio, uint8_t* k_cache,
+                            uint8_t* v_cache, int64_t num_blocks, int32_t block_size, int64_t k_stride_block,
+                            int64_t k_stride_token, int64_t k_stride_head, int64_t v_stride_block,
+                            int64_t v_stride_token, int64_t v_stride_head, const int64_t* slot_mapping,
+                            const int32_t* qsl_dev, const int32_t* seqs_dev, const int32_t* block_table,
+                            int64_t bt_rows, int64_t bt_stride, const int32_t* qsl, const int32_t* seqs,
+                            int32_t num_requests, int32_t sink_eff, int32_t recent_tokens, float scale,
+                            float* stage_k, float* stage_v, int64_t* owner, int64_t stage_rows, void* out,
+                            int64_t out_stride, void* scratch, int64_t scratch_bytes, void* stream);
+
+/* Bytes of oscar_decode_layer_step's scratch before the attention workspace. */
+int64_t oscar_decode_layer_step_scratch(int64_t n_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                                        int32_t head_dim, int32_t dtype);
+
 #ifdef __cplusplus
 }
 #endif

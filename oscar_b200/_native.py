@@ -56,6 +56,12 @@ SIGNATURES = {
     "oscar_merge_slab": (ctypes.c_int, [_P, _P, _I64, _P, _I32, _P, _I64, _I32, _I32, _I64, _P, _P]),
     "oscar_rotate_rows": (ctypes.c_int, [_P, _I32, _I64, _I64, _I32, _P, _I32, _P, _I32, _I64, _P, _I64, _P]),
     "oscar_rotate_rows_batch": (ctypes.c_int, [ctypes.POINTER(RotateSeg), _I32, _I32, _I32, _I32, _P]),
+    "oscar_decode_layer_step": (ctypes.c_int, [_P, _P, _P, _I32, _I64, _I64, _I64, _I64, _I32, _I32, _I32,
+                                               _P, _P, _P, _F32, _F32, _P, _P, _I64, _I32,
+                                               _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _I64,
+                                               _P, _P, _I32, _I32, _I32, _F32, _P, _P, _P, _I64, _P, _I64,
+                                               _P, _I64, _P]),
+    "oscar_decode_layer_step_scratch": (ctypes.c_int64, [_I64, _I32, _I32, _I32, _I32]),
 }
 
 ABI_VERSION = 1

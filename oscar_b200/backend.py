@@ -63,6 +63,23 @@ def block_table_of(attn_metadata) -> torch.Tensor:
     return bt
 
 
+_STEP_DTYPES = (torch.bfloat16, torch.float16)
+
+
+def _token_stride(t: torch.Tensor, heads: int, d: int):
+    """Elements between token rows of a [n, heads * D] or [n, heads, D] tensor
+    whose heads are contiguous within a token; None for any other layout."""
+    if t.dim() == 2 and t.shape[1] == heads * d and t.stride(1) == 1:
+        ts = t.stride(0)
+    elif t.dim() == 3 and t.shape[1] == heads and t.shape[2] == d and t.stride(2) == 1 and t.stride(1) == d:
+        ts = t.stride(0)
+    else:
+        return None
+    if (t.shape[0] > 1 and ts % 8) or t.data_ptr() % 16:
+        return None
+    return ts
+
+
 def _device_ints(values, device) -> torch.Tensor:
     t = torch.from_numpy(np.asarray(values, dtype=np.int32))
     if device.type == "cuda":
@@ -86,8 +103,13 @@ def _device_batch(attn_metadata, qsl: list, seqs: list, device) -> tuple:
 
 
 class OscarAttentionImplMixin(metaclass=abc.ABCMeta):
-    """The OSCAR read/write/window paths.  Placed first in the MRO of a
-    subclass of the running vLLM attention impl (plugin.install_impl)."""
+    """The OSCAR read/write/window paths.  The plugin builds a subclass of the
+    running vLLM attention impl with these methods in front of its own
+    (plugin.oscar_impl_class, oscar_b200.surgery)."""
+
+    # decode-sized steps run as one native call (_native_step); False keeps them
+    # on the per-kernel path (the two are bit-identical)
+    _oscar_native_step = True
 
     # ------------------------------------------------------------------ setup
     def _oscar_setup(self) -> None:
@@ -278,6 +300,9 @@ class OscarAttentionImplMixin(metaclass=abc.ABCMeta):
         if attn_metadata is None:
             return output.fill_(0)
         self._set_caches(kv_cache)
+        if key is not None and value is not None and self._oscar_native_step and \
+                self._native_step(layer, query, key, value, attn_metadata, output):
+            return output
         if key is not None and value is not None:
             n = attn_metadata.num_actual_tokens
             slots = attn_metadata.slot_mapping[:n].to(device=key.device, dtype=torch.int64)
@@ -307,6 +332,66 @@ class OscarAttentionImplMixin(metaclass=abc.ABCMeta):
             return self._streaming_attention(layer, query, key, value, kv_cache, attn_metadata, output,
                                              rotated_lo=None if rotated is None else rotated[2:])
         return self._streaming_attention(layer, query, key, value, kv_cache, attn_metadata, output)
+
+    def _native_step(self, layer, query, key, value, md, output) -> bool:
+        """A decode-sized step (window on, <= 256 tokens and requests, every
+        request with cached history, 16-bit activations whose heads are
+        contiguous per token) as one native call: rotations, write step,
+        attention and output rotation (kernels.decode_layer_step).  Returns
+        False, having done nothing, for any other step."""
+        cfg = self._oscar
+        n = md.num_actual_tokens
+        dt = query.dtype
+        if (not cfg.window_enabled or n <= 0 or n > kernels.WRITE_STEP_MAX_TOKENS or dt not in _STEP_DTYPES
+                or key.dtype != dt or value.dtype != dt or output.dtype != dt):
+            return False
+        qsl, seqs = metadata_batch_lists(md)
+        b = len(qsl) - 1
+        if b < 1 or b > kernels.WRITE_STEP_MAX_REQUESTS or qsl[-1] != n or len(seqs) < b:
+            return False
+        if any(bq - aq >= s_ for aq, bq, s_ in zip(qsl, qsl[1:], seqs) if bq > aq):
+            return False  # a prefix-free request attends in the model's domain
+        hq, hk, d = self.num_heads, self.num_kv_heads, self.head_size
+        rows = []
+        for t, heads in ((query, hq), (key, hk), (value, hk), (output, hq)):
+            ts = _token_stride(t, heads, d)
+            if ts is None:
+                return False
+            rows.append(ts)
+        slots = md.slot_mapping
+        if slots.dtype != torch.int64 or slots.device != query.device or slots.shape[0] < n or \
+                (slots.dim() == 1 and slots.stride(0) != 1):
+            return False
+        self._ensure_staging(layer, None)
+        qsl_d, seqs_d = _device_batch(md, qsl, seqs, query.device)
+        table = block_table_of(md)
+        if table.dtype != torch.int32 or not table.is_contiguous():
+            table = table.to(torch.int32).contiguous()
+        rk, rv = self._layer_rots(layer, query.device)
+        rvt = self._layer_rvt(layer, query.device)
+        if output.shape[0] > n:
+            output[n:].zero_()
+        kernels.decode_layer_step(query, key, value, rows, n, hq, hk, d, rk, rv, rvt, cfg.k_clip_ratio,
+                                  cfg.v_clip_ratio, self.key_cache, self.value_cache, slots, qsl_d, seqs_d, table,
+                                  qsl, seqs[:b], self.sink_eff, cfg.recent_tokens, self.scale, layer._oscar_stage_k,
+                                  layer._oscar_stage_v, layer._oscar_slot_owner, output,
+                                  self._step_scratch(query.device))
+        self._oscar_stats["writes"] += 1
+        self._oscar_stats["kv_bytes_written"] += n * hk * 160
+        return True
+
+    def _step_scratch(self, device) -> torch.Tensor:
+        """The impl's scratch for native steps (rotated rows, attention output
+        and the attention workspace up to the configured bound), grown on
+        demand and shared by the impl's layers (their steps run in stream order)."""
+        buf = getattr(self, "_oscar_scratch", None)
+        if buf is None or buf.device != device:
+            # sized once for the largest native step plus the configured workspace bound
+            need = kernels.decode_step_scratch_bytes(kernels.WRITE_STEP_MAX_TOKENS, self.num_heads, self.num_kv_heads,
+                                                     self.head_size, self._oscar.stream_workspace_bytes)
+            buf = torch.empty(need, dtype=torch.uint8, device=device)
+            self._oscar_scratch = buf
+        return buf
 
     def _whole_batch_rotated_queries(self, query, key, metadata):
         """The query rows [covered, Hq, D] when every active request takes the

@@ -10,6 +10,7 @@
 #include <mutex>
 #include <string>
 #include <utility>
+#include <queue>
 #include <vector>
 
 #include "../../include/oscar_b200.h"
@@ -411,9 +412,43 @@ struct DecodePlanned {
 // stages so that about `target` CTAs run; every split writes a partial (two
 // when staging is on: the INT2 one and the staged one), so the workspace must
 // hold all of them.
+// Estimated makespan, in stages, of splitting each request's history into
+// chunks of at most `per` stages on `target` SMs that hold one CTA each: the
+// CTAs start in grid order (kv heads fastest, then the items: requests longest
+// first, their splits in order) on the SM that frees first, and each takes
+// `overhead` (prologue, epilogue) plus its stages.
+double decode_makespan(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1, int hk, int stage, int64_t per,
+                       int target, double overhead) {
+  std::priority_queue<double, std::vector<double>, std::greater<double>> free_at;
+  for (int i = 0; i < target; ++i) free_at.push(0.0);
+  double makespan = 0.0;
+  for (size_t i = b0; i < b1; ++i) {
+    const int ns = std::max(1, (reqs[i].prefix + stage - 1) / stage);
+    int sp = (int)((ns + per - 1) / per);
+    const int chunk_st = (ns + sp - 1) / sp;
+    sp = (ns + chunk_st - 1) / chunk_st;
+    for (int s = 0; s < sp; ++s) {
+      const double len = overhead + std::min(chunk_st, ns - s * chunk_st);
+      for (int h = 0; h < hk; ++h) {
+        const double t = free_at.top() + len;
+        free_at.pop();
+        free_at.push(t);
+        makespan = std::max(makespan, t);
+      }
+    }
+  }
+  return makespan;
+}
+
+// Splits of each request's history [0, prefix) into chunks of whole stages so
+// that about `target` CTAs run; every split writes a partial (two when staging
+// is on: the INT2 one and the staged one), so the workspace must hold all of
+// them.  With `overhead` > 0 (kernels holding one CTA per SM), the chunk bound
+// is the candidate with the smallest decode_makespan: equal chunks a little
+// over one wave would otherwise run a second wave behind the first.
 DecodePlanned plan_decode(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1, int rows, int hk, int bs,
                           int target, int64_t ws_bytes, bool staged, int stage = oscar::kDecStage,
-                          int max_pages = oscar::kDecMaxPages, int max_stages = 1 << 20, bool one_wave = false) {
+                          int max_pages = oscar::kDecMaxPages, int max_stages = 1 << 20, double overhead = 0.0) {
   DecodePlanned out{};
   oscar::AttnPlan& p = out.plan;
   p.num_req = (int)(b1 - b0);
@@ -424,6 +459,19 @@ DecodePlanned plan_decode(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1
   int64_t work = 0;
   for (size_t i = b0; i < b1; ++i) work += std::max(1, (reqs[i].prefix + stage - 1) / stage);
   int64_t budget = std::max<int64_t>(1, (work * hk + target - 1) / std::max(target, 1));
+  if (overhead > 0.0) {
+    const int64_t base = std::min(budget, max_chunk_stages);
+    const int64_t cands[] = {base, (base * 5 + 3) / 4, (base * 3 + 1) / 2, base * 2, base * 3, max_chunk_stages};
+    double best = -1.0;
+    for (int64_t c : cands) {
+      c = std::max<int64_t>(1, std::min(c, max_chunk_stages));
+      const double m = decode_makespan(reqs, b0, b1, hk, stage, c, target, overhead);
+      if (best < 0.0 || m < best - 1e-9 || (m <= best + 1e-9 && c > budget)) {
+        best = m;
+        budget = c;
+      }
+    }
+  }
   for (;;) {
     int items = 0;
     int64_t part_bytes = 0;
@@ -457,17 +505,8 @@ DecodePlanned plan_decode(const std::vector<ReqInfo>& reqs, size_t b0, size_t b1
     p.total_merge_rows = 0;
     out.part_bytes = part_bytes;
     out.fits = part_bytes <= ws_bytes;
-    if (!out.fits && !(all_single && budget >= max_chunk_stages)) {
-      budget *= 2;
-      continue;
-    }
-    // one CTA per SM: a grid larger than the target runs a second wave behind the
-    // first, so the step takes two chunk times; longer chunks in one wave are faster
-    if (one_wave && out.fits && !all_single && (int64_t)items * hk > target && per < max_chunk_stages) {
-      ++budget;
-      continue;
-    }
-    break;
+    if (out.fits || (all_single && budget >= max_chunk_stages)) break;
+    budget *= 2;
   }
   return out;
 }
@@ -575,6 +614,11 @@ bool tc_eligible(int head_dim, int max_rows, const oscar::AttnArgs& a) {
   return encode_tiled() != nullptr;
 }
 
+// per-CTA cost of the tensor-core decode kernel beyond its stages, in stages
+// (prologue with the first TMA round trip, epilogue, share of the merge:
+// about 5 us against about 2 us per 128-token stage, from clock64 traces)
+constexpr double kTcCtaOverhead = 2.5;
+
 template <typename T>
 int run_decode_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs, void* workspace, int64_t ws_bytes,
                   cudaStream_t s) {
@@ -592,7 +636,7 @@ int run_decode_tc(const oscar::AttnArgs& base, const std::vector<ReqInfo>& reqs,
   for (size_t b0 = 0; b0 < reqs.size(); b0 += oscar::kPlanReqs) {
     const size_t b1 = std::min(reqs.size(), b0 + (size_t)oscar::kPlanReqs);
     plans.push_back(plan_decode(reqs, b0, b1, oscar::kTcRows, base.hk, base.bs, target, ws_bytes, false,
-                                oscar::kTcStage, oscar::kTcMaxPages, oscar::kTcMaxStages, true));
+                                oscar::kTcStage, oscar::kTcMaxPages, oscar::kTcMaxStages, kTcCtaOverhead));
     if (!plans.back().fits) return kDecodeNoFit;
     if (plans.back().plan.total_items > 65535) return kDecodeNoFit;  // the grid's y extent holds the items
   }
@@ -1099,6 +1143,39 @@ int launch_rotate(const oscar::RotBatch& b, int d, cudaStream_t s) {
   return launch_rotate_d<InT, OutT, 64>(b, s);
 }
 
+// The kernel reads the rotation matrices before it waits for the launch in
+// front of it, unless that launch may have written one: the outputs of this
+// thread's previous rotation launch are remembered and checked for overlap.
+// (No other library kernel writes anything a caller could pass as a rotation.)
+void mark_rot_early(oscar::RotBatch& b, int out_dtype, int head_dim) {
+  struct Range {
+    uintptr_t lo, hi;
+  };
+  static thread_local Range prev[2 * oscar::kRotMaxSegs];
+  static thread_local int n_prev = 0;
+  const size_t out_es = out_dtype == OSCAR_DTYPE_F32 ? 4 : 2;
+  const size_t rot_bytes = (size_t)head_dim * head_dim * sizeof(float);
+  b.rot_early = 1;
+  for (int i = 0; i < b.n; ++i) {
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(b.seg[i].rot), hi = lo + rot_bytes;
+    for (int j = 0; j < n_prev; ++j)
+      if (lo < prev[j].hi && prev[j].lo < hi) b.rot_early = 0;
+  }
+  n_prev = 0;
+  for (int i = 0; i < b.n; ++i) {
+    const oscar::RotSeg& d = b.seg[i];
+    const int64_t last = (d.rows - 1) / d.heads;  // last token
+    if (d.out != nullptr) {
+      const uintptr_t lo = reinterpret_cast<uintptr_t>(d.out);
+      prev[n_prev++] = {lo, lo + ((size_t)last * d.out_stride + (size_t)d.heads * head_dim) * out_es};
+    }
+    if (d.out_f32 != nullptr) {
+      const uintptr_t lo = reinterpret_cast<uintptr_t>(d.out_f32);
+      prev[n_prev++] = {lo, lo + ((size_t)last * d.out_f32_stride + (size_t)d.heads * head_dim) * 4};
+    }
+  }
+}
+
 template <typename InT>
 int rotate_out(int out_dtype, const oscar::RotBatch& b, int d, cudaStream_t s) {
   if (out_dtype == OSCAR_DTYPE_F32) return launch_rotate<InT, float>(b, d, s);
@@ -1135,6 +1212,7 @@ extern "C" int oscar_rotate_rows_batch(const oscar_rotate_seg* segs, int32_t n_s
     d.out_stride = g.out_stride;
     d.out_f32 = g.out_f32;
     d.out_f32_stride = g.out_f32_stride;
+    d.heads = 1;
     b.tile_begin[b.n] = (int)tiles;
     tiles += (g.rows + oscar::kRotRows - 1) / oscar::kRotRows;
     if (tiles > INT_MAX / 2) return fail(OSCAR_ERR_INVALID, "rotate: too many rows");
@@ -1142,37 +1220,7 @@ extern "C" int oscar_rotate_rows_batch(const oscar_rotate_seg* segs, int32_t n_s
   }
   if (b.n == 0) return OSCAR_OK;
   b.tile_begin[b.n] = (int)tiles;
-  // The kernel reads the rotation matrices before it waits for the launch in
-  // front of it, unless that launch may have written one: the outputs of this
-  // thread's previous rotation launch are remembered and checked for overlap.
-  // (No other library kernel writes anything a caller could pass as a rotation.)
-  {
-    struct Range {
-      uintptr_t lo, hi;
-    };
-    static thread_local Range prev[2 * oscar::kRotMaxSegs];
-    static thread_local int n_prev = 0;
-    const size_t out_es = out_dtype == OSCAR_DTYPE_F32 ? 4 : 2;
-    const size_t rot_bytes = (size_t)head_dim * head_dim * sizeof(float);
-    b.rot_early = 1;
-    for (int i = 0; i < b.n; ++i) {
-      const uintptr_t lo = reinterpret_cast<uintptr_t>(b.seg[i].rot), hi = lo + rot_bytes;
-      for (int j = 0; j < n_prev; ++j)
-        if (lo < prev[j].hi && prev[j].lo < hi) b.rot_early = 0;
-    }
-    n_prev = 0;
-    for (int i = 0; i < b.n; ++i) {
-      const oscar::RotSeg& d = b.seg[i];
-      if (d.out != nullptr) {
-        const uintptr_t lo = reinterpret_cast<uintptr_t>(d.out);
-        prev[n_prev++] = {lo, lo + ((size_t)(d.rows - 1) * d.out_stride + head_dim) * out_es};
-      }
-      if (d.out_f32 != nullptr) {
-        const uintptr_t lo = reinterpret_cast<uintptr_t>(d.out_f32);
-        prev[n_prev++] = {lo, lo + ((size_t)(d.rows - 1) * d.out_f32_stride + head_dim) * 4};
-      }
-    }
-  }
+  mark_rot_early(b, out_dtype, head_dim);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (x_dtype == OSCAR_DTYPE_F32) return rotate_out<float>(out_dtype, b, head_dim, s);
   if (x_dtype == OSCAR_DTYPE_BF16) return rotate_out<__nv_bfloat16>(out_dtype, b, head_dim, s);
@@ -1184,4 +1232,159 @@ extern "C" int oscar_rotate_rows(const void* x, int32_t x_dtype, int64_t rows, i
                                  float* out_f32, int64_t out_f32_stride, void* stream) {
   oscar_rotate_seg g{x, rows, x_stride, rot, transpose, out, out_stride, out_f32, out_f32_stride};
   return oscar_rotate_rows_batch(&g, 1, x_dtype, head_dim, out == nullptr ? OSCAR_DTYPE_F32 : out_dtype, stream);
+}
+
+// ---------------------------------------------------------------------------
+// One decode-sized layer step in one call (oscar_decode_layer_step).
+namespace {
+
+constexpr int64_t kStepAlign = 256;
+inline int64_t step_align(int64_t x) { return (x + kStepAlign - 1) / kStepAlign * kStepAlign; }
+
+struct StepScratch {
+  int64_t k_rot, v_rot, k_lo, v_lo, q_lo, att, lse, ws;  // byte offsets
+};
+
+inline StepScratch step_scratch(int64_t n, int hq, int hk, int d, int es) {
+  StepScratch s{};
+  int64_t off = 0;
+  auto take = [&](int64_t bytes) {
+    const int64_t at = off;
+    off += step_align(bytes);
+    return at;
+  };
+  s.k_rot = take(n * hk * d * 4);
+  s.v_rot = take(n * hk * d * 4);
+  s.k_lo = take(n * hk * d * es);
+  s.v_lo = take(n * hk * d * es);
+  s.q_lo = take(n * hq * d * es);
+  s.att = take(n * hq * d * 4);
+  s.lse = take(n * hq * 4);
+  s.ws = off;
+  return s;
+}
+
+template <typename T>
+int step_rotations(const oscar::RotBatch& b, int out_dtype, int d, cudaStream_t s) {
+  return rotate_out<T>(out_dtype, b, d, s);
+}
+
+}  // namespace
+
+extern "C" int64_t oscar_decode_layer_step_scratch(int64_t n_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                                                   int32_t head_dim, int32_t dtype) {
+  if (n_tokens < 0 || num_q_heads < 1 || num_kv_heads < 1 || (dtype != OSCAR_DTYPE_BF16 && dtype != OSCAR_DTYPE_F16))
+    return -1;
+  return step_scratch(n_tokens, num_q_heads, num_kv_heads, head_dim, 2).ws;
+}
+
+extern "C" int oscar_decode_layer_step(
+    const void* q, const void* k, const void* v, int32_t dtype, int64_t q_stride, int64_t k_stride, int64_t v_stride,
+    int64_t n_tokens, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, const float* rot_k,
+    const float* rot_v, const float* rot_vt, float k_clip_ratio, float v_clip_ratio, uint8_t* k_cache,
+    uint8_t* v_cache, int64_t num_blocks, int32_t block_size, int64_t k_stride_block, int64_t k_stride_token,
+    int64_t k_stride_head, int64_t v_stride_block, int64_t v_stride_token, int64_t v_stride_head,
+    const int64_t* slot_mapping, const int32_t* qsl_dev, const int32_t* seqs_dev, const int32_t* block_table,
+    int64_t bt_rows, int64_t bt_stride, const int32_t* qsl, const int32_t* seqs, int32_t num_requests,
+    int32_t sink_eff, int32_t recent_tokens, float scale, float* stage_k, float* stage_v, int64_t* owner,
+    int64_t stage_rows, void* out, int64_t out_stride, void* scratch, int64_t scratch_bytes, void* stream) {
+  if (dtype != OSCAR_DTYPE_BF16 && dtype != OSCAR_DTYPE_F16)
+    return fail(OSCAR_ERR_UNSUPPORTED, "layer step: query dtype must be bf16 or fp16");
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+    return fail(OSCAR_ERR_INVALID, "layer step: D=%d must be 64, 128 or 256", head_dim);
+  if (n_tokens < 1 || num_q_heads < 1 || num_kv_heads < 1 || num_q_heads % num_kv_heads || !q || !k || !v || !out ||
+      !scratch || !rot_k || !rot_v || !rot_vt || !qsl || !seqs)
+    return fail(OSCAR_ERR_INVALID, "layer step: invalid arguments");
+  if (q_stride < (int64_t)num_q_heads * head_dim || k_stride < (int64_t)num_kv_heads * head_dim ||
+      v_stride < (int64_t)num_kv_heads * head_dim || out_stride < (int64_t)num_q_heads * head_dim ||
+      (q_stride | k_stride | v_stride | out_stride) % 8)
+    return fail(OSCAR_ERR_INVALID, "layer step: token strides must cover the heads and be multiples of 8 elements");
+  if (num_requests < 1 || qsl[0] != 0 || qsl[num_requests] != n_tokens)
+    return fail(OSCAR_ERR_INVALID, "Invalid slab query layout");
+  for (int r = 0; r < num_requests; ++r)
+    if (qsl[r + 1] - qsl[r] >= seqs[r] && qsl[r + 1] > qsl[r])
+      return fail(OSCAR_ERR_UNSUPPORTED, "layer step: request %d has no cached history (prefix-free chunks take "
+                  "the model-domain path)", r);
+  const StepScratch sc = step_scratch(n_tokens, num_q_heads, num_kv_heads, head_dim, 2);
+  if (scratch_bytes < sc.ws) return fail(OSCAR_ERR_INVALID, "layer step: scratch smaller than %lld bytes",
+                                         (long long)sc.ws);
+  if (reinterpret_cast<uintptr_t>(scratch) % kStepAlign)
+    return fail(OSCAR_ERR_INVALID, "layer step: scratch must be %lld-byte aligned", (long long)kStepAlign);
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  float* k_rot = reinterpret_cast<float*>(base + sc.k_rot);
+  float* v_rot = reinterpret_cast<float*>(base + sc.v_rot);
+  void* k_lo = base + sc.k_lo;
+  void* v_lo = base + sc.v_lo;
+  void* q_lo = base + sc.q_lo;
+  float* att = reinterpret_cast<float*>(base + sc.att);
+  float* lse = reinterpret_cast<float*>(base + sc.lse);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int hq = num_q_heads, hk = num_kv_heads, d = head_dim;
+  // 1. k @ R_k, v @ R_v (fp32 for the store and the window, query dtype for the
+  //    attention) and q @ R_k (query dtype), one launch
+  {
+    oscar::RotBatch b{};
+    auto seg = [&](const void* x, int64_t stride, int heads, const float* rot, void* o, float* of) {
+      oscar::RotSeg& g = b.seg[b.n];
+      g.x = x;
+      g.rows = n_tokens * heads;
+      g.x_stride = stride;
+      g.heads = heads;
+      g.rot = rot;
+      g.transpose = 0;
+      g.out = o;
+      g.out_stride = (int64_t)heads * d;
+      g.out_f32 = of;
+      g.out_f32_stride = (int64_t)heads * d;
+      b.tile_begin[b.n] = b.n == 0 ? 0 : b.tile_begin[b.n - 1] + (int)((b.seg[b.n - 1].rows + oscar::kRotRows - 1) /
+                                                                      oscar::kRotRows);
+      ++b.n;
+    };
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+         reinterpret_cast<uintptr_t>(rot_k) | reinterpret_cast<uintptr_t>(rot_v) |
+         reinterpret_cast<uintptr_t>(rot_vt)) & 15)
+      return fail(OSCAR_ERR_INVALID, "layer step: q / k / v and the rotations must be 16-byte aligned");
+    seg(k, k_stride, hk, rot_k, k_lo, k_rot);
+    seg(v, v_stride, hk, rot_v, v_lo, v_rot);
+    seg(q, q_stride, hq, rot_k, q_lo, nullptr);
+    b.tile_begin[b.n] = b.tile_begin[b.n - 1] + (int)((b.seg[b.n - 1].rows + oscar::kRotRows - 1) / oscar::kRotRows);
+    mark_rot_early(b, dtype, d);
+    const int st = dtype == OSCAR_DTYPE_BF16 ? step_rotations<__nv_bfloat16>(b, dtype, d, s)
+                                             : step_rotations<__half>(b, dtype, d, s);
+    if (st) return st;
+  }
+  // 2. clip + INT2 store and the staging write of the step's tokens
+  int st = oscar_write_step(k_rot, v_rot, n_tokens, hk, d, k_clip_ratio, v_clip_ratio, k_cache, v_cache, num_blocks,
+                            block_size, k_stride_block, k_stride_token, k_stride_head, v_stride_block,
+                            v_stride_token, v_stride_head, slot_mapping, qsl_dev, seqs_dev, num_requests, sink_eff,
+                            recent_tokens, stage_k, stage_v, owner, stage_rows, stream);
+  if (st) return st;
+  // 3. attention in the rotated space
+  st = slab_attention_impl(q_lo, k_lo, v_lo, dtype, n_tokens, hq, hk, d, k_cache, v_cache, num_blocks, block_size,
+                           k_stride_block, k_stride_token, k_stride_head, v_stride_block, v_stride_token,
+                           v_stride_head, block_table, bt_rows, bt_stride, qsl, seqs, num_requests, scale, stage_k,
+                           stage_v, owner, stage_rows, att, lse, base + sc.ws, scratch_bytes - sc.ws, stream, false);
+  if (st) return st;
+  // 4. o @ R_v^T into the output rows, in the query dtype
+  {
+    oscar::RotBatch b{};
+    oscar::RotSeg& g = b.seg[0];
+    g.x = att;
+    g.rows = n_tokens * hq;
+    g.x_stride = (int64_t)hq * d;
+    g.heads = hq;
+    g.rot = rot_vt;
+    g.transpose = 0;
+    g.out = out;
+    g.out_stride = out_stride;
+    g.out_f32 = nullptr;
+    g.out_f32_stride = 0;
+    b.n = 1;
+    b.tile_begin[0] = 0;
+    b.tile_begin[1] = (int)((g.rows + oscar::kRotRows - 1) / oscar::kRotRows);
+    if (reinterpret_cast<uintptr_t>(out) & 15) return fail(OSCAR_ERR_INVALID, "layer step: out must be 16-byte aligned");
+    mark_rot_early(b, dtype, d);
+    st = rotate_out<float>(dtype, b, d, s);
+  }
+  return st;
 }

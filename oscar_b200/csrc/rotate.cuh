@@ -27,6 +27,7 @@ constexpr int kRotMaxSegs = 4;
 struct RotSeg {
   const void* x;
   int64_t rows, x_stride;
+  int heads;  // rows r = token * heads + head: x at token * x_stride + head * D (outputs likewise)
   const float* rot;
   int transpose;
   void* out;
@@ -47,6 +48,13 @@ constexpr size_t rotate_smem_bytes() {
   return (size_t)(D * kRotCols + D * kRotRows) * sizeof(float) > (size_t)8 * kRotRows * kRotCols * sizeof(float)
              ? (size_t)(D * kRotCols + D * kRotRows) * sizeof(float)
              : (size_t)8 * kRotRows * kRotCols * sizeof(float);
+}
+
+// element offset of row r (token r / heads, head r % heads)
+OSCAR_DEVINL int64_t rot_row(int64_t r, int heads, int64_t stride, int d) {
+  if (heads == 1) return r * stride;
+  const int64_t t = r / heads;
+  return t * stride + (r - t * heads) * d;
 }
 
 template <typename T>
@@ -126,7 +134,7 @@ __global__ void __launch_bounds__(256) rotate_rows_kernel(const __grid_constant_
     const int r = i & (kRotRows - 1), kc = i >> 4;
     xbuf[u] = make_uint4(0u, 0u, 0u, 0u);
     if (i < kXChunks && r0 + r < sg.rows)
-      xbuf[u] = *reinterpret_cast<const uint4*>(x + (r0 + r) * sg.x_stride + kP * kc);
+      xbuf[u] = *reinterpret_cast<const uint4*>(x + rot_row(r0 + r, sg.heads, sg.x_stride, D) + kP * kc);
   }
 #pragma unroll
   for (int u = 0; u < kRLoads; ++u) {
@@ -196,8 +204,8 @@ __global__ void __launch_bounds__(256) rotate_rows_kernel(const __grid_constant_
     OutT* out = static_cast<OutT*>(sg.out);
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      if (out != nullptr) rot_store<OutT>(out + (r0 + r) * sg.out_stride + c0 + cq + j, v[j]);
-      if (sg.out_f32 != nullptr) sg.out_f32[(r0 + r) * sg.out_f32_stride + c0 + cq + j] = v[j];
+      if (out != nullptr) rot_store<OutT>(out + rot_row(r0 + r, sg.heads, sg.out_stride, D) + c0 + cq + j, v[j]);
+      if (sg.out_f32 != nullptr) sg.out_f32[rot_row(r0 + r, sg.heads, sg.out_f32_stride, D) + c0 + cq + j] = v[j];
     }
   }
 }

@@ -346,6 +346,40 @@ def slab_attention_shard(q, kc, vc, table, qsl, history_lens, scale, stage=None,
     return out, lse
 
 
+def decode_step_scratch_bytes(n: int, hq: int, hk: int, d: int, workspace_bytes: int) -> int:
+    """Scratch of decode_layer_step for up to n tokens: the rotated rows and
+    the attention output, then `workspace_bytes` of attention workspace."""
+    fixed = int(_native.lib().oscar_decode_layer_step_scratch(n, hq, hk, d, _native.DTYPE_BF16))
+    if fixed < 0:
+        raise ValueError("decode_layer_step: invalid geometry")
+    return fixed + max(0, int(workspace_bytes))
+
+
+def decode_layer_step(q, k, v, token_strides, n, hq, hk, d, rot_k, rot_v, rot_vt, k_clip_ratio, v_clip_ratio,
+                      k_cache, v_cache, slot_mapping, qsl_dev, seqs_dev, table, qsl, seqs, sink_eff, recent_tokens,
+                      scale, stage_k, stage_v, owner, out, scratch) -> None:
+    """One decode-sized layer step in one native call (oscar_decode_layer_step):
+    rotations, clip + INT2 store + staging write, rotated attention, output
+    rotation into ``out``.  The backend's fast path: the caller has checked
+    the layouts (heads contiguous per token, ``token_strides`` = the token
+    row strides of q, k, v, out in elements; int64 slots, int32 device qsl /
+    seqs and block table, host lists ``qsl`` / ``seqs``); the C side checks
+    sizes and alignment and raises through ``check``."""
+    lib = _native.lib()
+    k8, v8 = k_cache.view(torch.uint8), v_cache.view(torch.uint8)
+    qsl_a = np.asarray(qsl, dtype=np.int32)
+    seqs_a = np.asarray(seqs, dtype=np.int32)
+    kst, vst = k8.stride(), v8.stride()
+    check(lib.oscar_decode_layer_step(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), _DTYPES[q.dtype], token_strides[0], token_strides[1],
+        token_strides[2], n, hq, hk, d, rot_k.data_ptr(), rot_v.data_ptr(), rot_vt.data_ptr(), _clip_ok(k_clip_ratio),
+        _clip_ok(v_clip_ratio), k8.data_ptr(), v8.data_ptr(), k8.shape[0], k8.shape[1], kst[0], kst[1], kst[2],
+        vst[0], vst[1], vst[2], slot_mapping.data_ptr(), qsl_dev.data_ptr(), seqs_dev.data_ptr(), table.data_ptr(),
+        table.shape[0], table.stride(0), qsl_a.ctypes.data, seqs_a.ctypes.data, len(seqs), int(sink_eff),
+        int(recent_tokens), float(scale), stage_k.data_ptr(), stage_v.data_ptr(), owner.data_ptr(), owner.shape[0],
+        out.data_ptr(), token_strides[3], scratch.data_ptr(), scratch.numel(), _stream(q.device)))
+
+
 def merge_slab(output, lse, part, part_lse, start, ids) -> None:
     """In-place LSE merge of part into output[start:start+n] (or output[ids])."""
     dev = _require_cuda(output, lse, part, part_lse, ids)
