@@ -67,6 +67,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=6)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="skip the cfg4 / cfg5 measurements")
+    ap.add_argument("--only", choices=["cfg4", "cfg5", "split_kv"], default=None,
+                    help="run one secondary workload alone and print its JSON object (profiling)")
     ap.add_argument("--workspace-mib", type=int, default=None,
                     help="attention workspace bound of the backend (default: the OSCAR_ASCEND_STREAM_WORKSPACE_MIB "
                          "default, 128)")
@@ -776,6 +778,21 @@ def run_gpu(args):
     world, rank, dist, dev = init_dist()
     plan = shard_plan(world, rank, 8)
     pair = pair_groups(dist, world)
+    if args.only:
+        # one secondary workload alone (profiling runs): its JSON object, no headline
+        fn = {"cfg4": lambda: run_cfg4(torch, dev, args, dist, plan),
+              "cfg5": lambda: run_cfg5(torch, dev, args, dist, plan),
+              "split_kv": lambda: run_split_kv(torch, dev, args, dist, plan, pair)}[args.only]
+        if args.only == "split_kv" and pair is None:
+            raise SystemExit("--only split_kv needs 8 ranks (pairs of ranks per KV-head group)")
+        line = fn()
+        assert kernels.device_error(dev) == 0
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"only": args.only, **line}), flush=True)
+        return
     head = run_headline(torch, dev, args, world, rank, dist, plan)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

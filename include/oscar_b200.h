@@ -56,6 +56,17 @@ uint64_t oscar_launch_count(void);
  * the switch keeps each of them parity-tested.  Other values: status 1. */
 int oscar_set_attention_path(int path);
 
+/* Selects the rotation kernel for later oscar_rotate_rows* and layer-step
+ * calls in this process: 0 = automatic (batches of at least 2048 fp32 rows
+ * -- the attention output's o @ R_v^T -- whose output rows are 16-byte
+ * aligned on the tcgen05 kind::tf32 kernel; the k / v / q rotations, whose
+ * rounding the INT2 codes and the attention scores are sensitive to, on the
+ * fp32 FMA kernel), 1 = the FMA kernel only, 2 = the tensor-core kernel
+ * wherever the alignment allows.  The tensor-core kernel splits R (and fp32
+ * x) into two tf32 terms, so both compute x @ R to within a few fp32 ulps;
+ * the switch keeps both parity-tested.  Other values: status 1. */
+int oscar_set_rotation_path(int path);
+
 /* Synchronises `stream`, returns and clears the device-side bounds flag of the
  * current device: 0 = clean, otherwise a bitmask (1 = slot out of range,
  * 2 = block-table entry out of range, 8 = merge target row out of range,

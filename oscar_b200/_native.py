@@ -36,6 +36,7 @@ SIGNATURES = {
     "oscar_device_error": (ctypes.c_int, [_P]),
     "oscar_launch_count": (ctypes.c_uint64, []),
     "oscar_set_attention_path": (ctypes.c_int, [ctypes.c_int]),
+    "oscar_set_rotation_path": (ctypes.c_int, [ctypes.c_int]),
     "oscar_store_int2": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _F32, _F32, _P, _P, _I64, _I32,
                                         _I64, _I64, _I64, _I64, _I64, _I64, _P, _P]),
     "oscar_staging_invalidate": (ctypes.c_int, [_P, _I64, _P, _I64, _I32, _P]),

@@ -19,12 +19,14 @@
 #include "decode.cuh"
 #include "decode_tc.cuh"
 #include "rotate.cuh"
+#include "rotate_tc.cuh"
 #include "store.cuh"
 
 namespace {
 
 thread_local std::string g_last_error;
 std::atomic<uint64_t> g_launches{0};
+std::atomic<int> g_rotate_path{0};     // 0 auto, 1 the FMA kernel only, 2 the tensor-core kernel where it applies
 std::atomic<int> g_attention_path{0};  // 0 auto, 1 tile only, 2 mma.sync decode, 3 tensor-core decode (where eligible)
 
 int fail(int code, const char* fmt, ...) {
@@ -96,6 +98,12 @@ int oscar_abi_version(void) { return 1; }
 const char* oscar_last_error(void) { return g_last_error.c_str(); }
 
 uint64_t oscar_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int oscar_set_rotation_path(int path) {
+  if (path < 0 || path > 2) return fail(OSCAR_ERR_INVALID, "rotation path must be 0, 1 or 2");
+  g_rotate_path.store(path);
+  return OSCAR_OK;
+}
 
 int oscar_set_attention_path(int path) {
   if (path < 0 || path > 3)
@@ -1136,11 +1144,77 @@ int launch_rotate_d(const oscar::RotBatch& b, cudaStream_t s) {
   return cuda_status("rotate_rows_kernel");
 }
 
+// tcgen05 (kind::tf32, split precision) rotation of a batch, in 128-row tiles
+template <typename InT, typename OutT, int D>
+int launch_rotate_tc_d(const oscar::RotBatch& b16, cudaStream_t s) {
+  oscar::RotBatch b = b16;
+  int64_t tiles = 0;
+  for (int i = 0; i < b.n; ++i) {
+    b.tile_begin[i] = (int)tiles;
+    tiles += (b.seg[i].rows + oscar::kRtRows - 1) / oscar::kRtRows;
+  }
+  b.tile_begin[b.n] = (int)tiles;
+  constexpr size_t smem = sizeof(oscar::RtSmem<D>);
+  static thread_local int cfg_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cfg_dev != dev) {
+    cudaFuncSetAttribute(oscar::rotate_tc_kernel<InT, OutT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    cfg_dev = dev;
+  }
+  // persistent CTAs, one per SM: each column block gets SMs / blocks of them
+  constexpr int kBlocks = D / oscar::kRtCols;
+  const int per_block = std::max(1, device_info().sms / kBlocks);
+  dim3 grid((unsigned)std::min<int64_t>(tiles, per_block), (unsigned)kBlocks);
+  launch_pdl(oscar::rotate_tc_kernel<InT, OutT, D>, grid, dim3(oscar::kRtThreads), smem, s, b);
+  return cuda_status("rotate_tc_kernel");
+}
+
+// The tensor-core kernel for batches of at least kRotTcMinRows rows (path 0) or
+// always (path 2), when every output row is 16-byte aligned (it writes
+// 16-byte pieces); the FMA kernel otherwise.
+constexpr int64_t kRotTcMinRows = 2048;
+bool rotate_on_tc(const oscar::RotBatch& b, size_t out_es) {
+  const int path = g_rotate_path.load();
+  if (path == 1) return false;
+  int64_t rows = 0;
+  for (int i = 0; i < b.n; ++i) {
+    const oscar::RotSeg& g = b.seg[i];
+    rows += g.rows;
+    if (g.out != nullptr && ((reinterpret_cast<uintptr_t>(g.out) & 15) || (g.out_stride * (int64_t)out_es) % 16))
+      return false;
+    if (g.out_f32 != nullptr && ((reinterpret_cast<uintptr_t>(g.out_f32) & 15) || g.out_f32_stride % 4)) return false;
+  }
+  return path == 2 || rows >= kRotTcMinRows;
+}
+
 template <typename InT, typename OutT>
-int launch_rotate(const oscar::RotBatch& b, int d, cudaStream_t s) {
+int launch_rotate_fma(const oscar::RotBatch& b, int d, cudaStream_t s) {
   if (d == 256) return launch_rotate_d<InT, OutT, 256>(b, s);
   if (d == 128) return launch_rotate_d<InT, OutT, 128>(b, s);
   return launch_rotate_d<InT, OutT, 64>(b, s);
+}
+template <typename InT, typename OutT>
+int launch_rotate_tc(const oscar::RotBatch& b, int d, cudaStream_t s) {
+  if (d == 256) return launch_rotate_tc_d<InT, OutT, 256>(b, s);
+  if (d == 128) return launch_rotate_tc_d<InT, OutT, 128>(b, s);
+  return launch_rotate_tc_d<InT, OutT, 64>(b, s);
+}
+
+// Automatic choice: the tensor cores for large batches of fp32 rows (the
+// attention output's o @ R_v^T, rounded once more to the output dtype); the
+// FMA kernel, the closer of the two to an fp32 GEMM, for the k / v / q
+// rotations: a k or v element on an INT2 quantisation boundary, or a q element
+// on a bf16 rounding boundary next to an outlier channel, turns a rotation
+// error of a few fp32 ulps into a visible change of the attention, and the
+// tf32 split's error is several times the FMA kernel's.
+template <typename InT, typename OutT>
+int launch_rotate(const oscar::RotBatch& b, int d, cudaStream_t s) {
+  const int path = g_rotate_path.load();
+  if (rotate_on_tc(b, sizeof(OutT)) && (path == 2 || std::is_same<InT, float>::value))
+    return launch_rotate_tc<InT, OutT>(b, d, s);
+  return launch_rotate_fma<InT, OutT>(b, d, s);
 }
 
 // The kernel reads the rotation matrices before it waits for the launch in

@@ -476,6 +476,18 @@ def set_attention_path(path: str) -> None:
     check(_native.lib().oscar_set_attention_path(_PATHS[path]))
 
 
+_ROT_PATHS = {"auto": 0, "fma": 1, "tensor": 2}
+
+
+def set_rotation_path(path: str) -> None:
+    """Rotation kernel for rotate_rows / rotate_rows_many and the layer step:
+    "auto" (tcgen05 kind::tf32 with split precision for batches of at least
+    2048 fp32 rows -- the output rotation -- and fp32 FMAs for the k / v / q
+    rotations), "fma" or "tensor".  Both compute x @ R to within a few fp32
+    ulps."""
+    check(_native.lib().oscar_set_rotation_path(_ROT_PATHS[path]))
+
+
 def device_error(device=None) -> int:
     """Synchronise and return/clear the kernels' bounds-violation flag (debug)."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)

@@ -1,11 +1,23 @@
-"""The per-layer rotation kernel (x @ R and x @ R^T in fp32) against torch's
-fp64 product, for every dtype pair the backend uses and strided outputs."""
+"""The per-layer rotation kernels (x @ R and x @ R^T) against torch's fp64
+product, for every dtype pair the backend uses and strided outputs: the fp32
+FMA kernel and the tcgen05 kind::tf32 kernel with split precision (each test
+runs on both, through the process-wide rotation path)."""
 import pytest
 import torch
 
 from gpu_helpers import need_gpu
 
 pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(params=["fma", "tensor"], autouse=True)
+def rot_path(request):
+    from oscar_b200 import kernels
+
+    need_gpu()
+    kernels.set_rotation_path(request.param)
+    yield request.param
+    kernels.set_rotation_path("auto")
 
 
 @pytest.mark.parametrize("d", [64, 128, 256])
@@ -83,3 +95,25 @@ def test_rotation_output_used_as_the_next_rotation_matrix():
         kernels.rotate_rows(x, prod, out=out)  # reads prod as its rotation right after
         want = x.double() @ (r1.double() @ r2.double())
         torch.testing.assert_close(out.double(), want, atol=5e-5, rtol=5e-5)
+
+
+@pytest.mark.parametrize("xdt,odt", [(torch.bfloat16, torch.bfloat16), (torch.float32, torch.bfloat16)])
+def test_rotate_many_rows(xdt, odt, rot_path):
+    """3001 tokens x 6 heads (18006 rows, a partial last tile) from a strided
+    view of one buffer (the row-heads layout reaches the tensor-core kernel
+    through the layer step, tests/test_gpu_step.py)."""
+    from oscar_b200 import kernels
+
+    dev = need_gpu()
+    d, n, heads = 256, 3001, 6
+    g = torch.Generator(device="cpu").manual_seed(5)
+    rot = torch.linalg.qr(torch.randn(d, d, generator=g, dtype=torch.float64)).Q.float().to(dev)
+    buf = torch.randn(n, (heads + 2) * d, generator=g).to(dev, xdt)
+    x = buf[:, :heads * d].reshape(n, heads, d)
+    out = torch.empty(n, heads, d, dtype=odt, device=dev)
+    f32 = torch.empty(n, heads, d, dtype=torch.float32, device=dev)
+    kernels.rotate_rows(x, rot, out=out, out_f32=f32)
+    want = (x.double().reshape(-1, d) @ rot.double()).reshape(n, heads, d)
+    torch.testing.assert_close(f32.double(), want, atol=2e-5, rtol=2e-5)
+    torch.testing.assert_close(out, f32.to(odt), atol=0, rtol=0)
+    assert kernels.device_error(dev) == 0

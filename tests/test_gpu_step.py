@@ -31,12 +31,27 @@ def clone_state(case, dev, seed):
     return layer, (case.kc.clone(), case.vc.clone())
 
 
+@pytest.mark.parametrize("rot_path", ["auto", "tensor"])
 @pytest.mark.parametrize("fused_qkv", [False, True])
-def test_native_step_equals_per_kernel_forward(fused_qkv):
+def test_native_step_equals_per_kernel_forward(fused_qkv, rot_path):
+    """With rot_path "tensor" the rotations run on the tcgen05 kernel, whose
+    row-heads addressing (strided q / k / v, the output's token stride) the
+    native step uses and the per-kernel path does not."""
     from oscar_b200 import kernels
     from oscar_b200.synthetic import fill_caches, make_case
 
     dev = need_gpu()
+    kernels.set_rotation_path(rot_path)
+    try:
+        _run_native_vs_per_kernel(dev, fused_qkv)
+    finally:
+        kernels.set_rotation_path("auto")
+
+
+def _run_native_vs_per_kernel(dev, fused_qkv):
+    from oscar_b200 import kernels
+    from oscar_b200.synthetic import fill_caches, make_case
+
     hq, hk, d = 12, 2, 256
     prefixes = [3000, 700, 129, 2048]
     lengths = [4, 1, 3, 2]
