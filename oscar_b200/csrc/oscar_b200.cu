@@ -19,6 +19,7 @@
 #include "decode.cuh"
 #include "decode_tc.cuh"
 #include "rotate.cuh"
+#include "rotate_big.cuh"
 #include "rotate_tc.cuh"
 #include "store.cuh"
 
@@ -26,7 +27,7 @@ namespace {
 
 thread_local std::string g_last_error;
 std::atomic<uint64_t> g_launches{0};
-std::atomic<int> g_rotate_path{0};     // 0 auto, 1 the FMA kernel only, 2 the tensor-core kernel where it applies
+std::atomic<int> g_rotate_path{0};  // 0 auto, 1 16-row FMA tiles, 2 tensor cores, 3 128-row FMA tiles (where each applies)
 std::atomic<int> g_attention_path{0};  // 0 auto, 1 tile only, 2 mma.sync decode, 3 tensor-core decode (where eligible)
 
 int fail(int code, const char* fmt, ...) {
@@ -100,7 +101,7 @@ const char* oscar_last_error(void) { return g_last_error.c_str(); }
 uint64_t oscar_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int oscar_set_rotation_path(int path) {
-  if (path < 0 || path > 2) return fail(OSCAR_ERR_INVALID, "rotation path must be 0, 1 or 2");
+  if (path < 0 || path > 3) return fail(OSCAR_ERR_INVALID, "rotation path must be 0, 1, 2 or 3");
   g_rotate_path.store(path);
   return OSCAR_OK;
 }
@@ -1171,22 +1172,42 @@ int launch_rotate_tc_d(const oscar::RotBatch& b16, cudaStream_t s) {
   return cuda_status("rotate_tc_kernel");
 }
 
-// The tensor-core kernel for batches of at least kRotTcMinRows rows (path 0) or
-// always (path 2), when every output row is 16-byte aligned (it writes
-// 16-byte pieces); the FMA kernel otherwise.
+// automatic thresholds (rows of one segment): the tensor-core kernel from 2048
+// fp32 rows, the register-tiled FMA kernel from 16384 rows (128-row tiles: a
+// smaller segment leaves SMs idle and the 16-row tiles finish first)
 constexpr int64_t kRotTcMinRows = 2048;
-bool rotate_on_tc(const oscar::RotBatch& b, size_t out_es) {
-  const int path = g_rotate_path.load();
-  if (path == 1) return false;
-  int64_t rows = 0;
+constexpr int64_t kRotBigMinRows = 16384;
+
+// The tensor-core and the register-tiled kernels write 16-byte pieces of every
+// output row: rows (and their starts) must be 16-byte aligned.
+bool rotate_rows_aligned(const oscar::RotSeg& g, size_t out_es) {
+  if (g.out != nullptr && ((reinterpret_cast<uintptr_t>(g.out) & 15) || (g.out_stride * (int64_t)out_es) % 16))
+    return false;
+  return g.out_f32 == nullptr || !((reinterpret_cast<uintptr_t>(g.out_f32) & 15) || g.out_f32_stride % 4);
+}
+
+// register-tiled FMA rotation of a batch, in 128-row tiles (D = 128 or 256)
+template <typename InT, typename OutT, int D>
+int launch_rotate_big_d(const oscar::RotBatch& b16, cudaStream_t s) {
+  oscar::RotBatch b = b16;
+  int64_t tiles = 0;
   for (int i = 0; i < b.n; ++i) {
-    const oscar::RotSeg& g = b.seg[i];
-    rows += g.rows;
-    if (g.out != nullptr && ((reinterpret_cast<uintptr_t>(g.out) & 15) || (g.out_stride * (int64_t)out_es) % 16))
-      return false;
-    if (g.out_f32 != nullptr && ((reinterpret_cast<uintptr_t>(g.out_f32) & 15) || g.out_f32_stride % 4)) return false;
+    b.tile_begin[i] = (int)tiles;
+    tiles += (b.seg[i].rows + oscar::kRbRows - 1) / oscar::kRbRows;
   }
-  return path == 2 || rows >= kRotTcMinRows;
+  b.tile_begin[b.n] = (int)tiles;
+  constexpr size_t smem = sizeof(oscar::RbSmem);
+  static thread_local int cfg_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cfg_dev != dev) {
+    cudaFuncSetAttribute(oscar::rotate_big_kernel<InT, OutT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    cfg_dev = dev;
+  }
+  dim3 grid((unsigned)tiles, (unsigned)(D / oscar::kRbCols));
+  launch_pdl(oscar::rotate_big_kernel<InT, OutT, D>, grid, dim3(oscar::kRbThreads), smem, s, b);
+  return cuda_status("rotate_big_kernel");
 }
 
 template <typename InT, typename OutT>
@@ -1202,19 +1223,65 @@ int launch_rotate_tc(const oscar::RotBatch& b, int d, cudaStream_t s) {
   return launch_rotate_tc_d<InT, OutT, 64>(b, s);
 }
 
-// Automatic choice: the tensor cores for large batches of fp32 rows (the
-// attention output's o @ R_v^T, rounded once more to the output dtype); the
-// FMA kernel, the closer of the two to an fp32 GEMM, for the k / v / q
-// rotations: a k or v element on an INT2 quantisation boundary, or a q element
-// on a bf16 rounding boundary next to an outlier channel, turns a rotation
-// error of a few fp32 ulps into a visible change of the attention, and the
-// tf32 split's error is several times the FMA kernel's.
+// the segments of b that `keep` selects, re-tiled in 16-row tiles
+template <typename Pred>
+oscar::RotBatch rotate_subset(const oscar::RotBatch& b, Pred keep) {
+  oscar::RotBatch o{};
+  o.rot_early = b.rot_early;
+  int64_t tiles = 0;
+  for (int i = 0; i < b.n; ++i) {
+    if (!keep(i)) continue;
+    o.seg[o.n] = b.seg[i];
+    o.tile_begin[o.n] = (int)tiles;
+    tiles += (b.seg[i].rows + oscar::kRotRows - 1) / oscar::kRotRows;
+    ++o.n;
+  }
+  o.tile_begin[o.n] = (int)tiles;
+  return o;
+}
+
+// Kernel of each segment, by its own size (so that a tensor is rotated the
+// same way whatever it is batched with).  Automatic choice for large
+// segments: the tensor cores for fp32 rows (the attention output's o @ R_v^T,
+// rounded once more to the output dtype), the register-tiled FMA kernel for
+// the k / v / q rotations: a k or v element on an
+// INT2 quantisation boundary, or a q element on a bf16 rounding boundary next
+// to an outlier channel, turns a rotation error of a few fp32 ulps into a
+// visible change of the attention, and the tf32 split's error is several
+// times an fp32 FMA chain's.  Smaller segments take rotate.cuh's 16-row tiles.
+enum RotKernel { kRotSmall = 0, kRotBig = 1, kRotTc = 2 };
+template <typename InT>
+RotKernel rotate_kernel_of(const oscar::RotSeg& g, int d, size_t out_es, int path) {
+  const bool aligned = rotate_rows_aligned(g, out_es);
+  if (path == 1 || !aligned) return kRotSmall;
+  if (path == 2) return kRotTc;
+  if (path == 3) return d >= oscar::kRbCols ? kRotBig : kRotSmall;
+  if (std::is_same<InT, float>::value) return g.rows >= kRotTcMinRows ? kRotTc : kRotSmall;
+  return (g.rows >= kRotBigMinRows && d >= oscar::kRbCols) ? kRotBig : kRotSmall;
+}
+
 template <typename InT, typename OutT>
 int launch_rotate(const oscar::RotBatch& b, int d, cudaStream_t s) {
   const int path = g_rotate_path.load();
-  if (rotate_on_tc(b, sizeof(OutT)) && (path == 2 || std::is_same<InT, float>::value))
-    return launch_rotate_tc<InT, OutT>(b, d, s);
-  return launch_rotate_fma<InT, OutT>(b, d, s);
+  RotKernel which[oscar::kRotMaxSegs];
+  bool mixed = false;
+  for (int i = 0; i < b.n; ++i) {
+    which[i] = rotate_kernel_of<InT>(b.seg[i], d, sizeof(OutT), path);
+    mixed = mixed || which[i] != which[0];
+  }
+  auto run = [&](const oscar::RotBatch& sub, RotKernel k) -> int {
+    if (sub.n == 0) return OSCAR_OK;
+    if (k == kRotTc) return launch_rotate_tc<InT, OutT>(sub, d, s);
+    if (k == kRotBig)
+      return d == 256 ? launch_rotate_big_d<InT, OutT, 256>(sub, s) : launch_rotate_big_d<InT, OutT, 128>(sub, s);
+    return launch_rotate_fma<InT, OutT>(sub, d, s);
+  };
+  if (!mixed) return run(b, b.n > 0 ? which[0] : kRotSmall);
+  for (RotKernel k : {kRotSmall, kRotBig, kRotTc}) {
+    const int st = run(rotate_subset(b, [&](int i) { return which[i] == k; }), k);
+    if (st) return st;
+  }
+  return OSCAR_OK;
 }
 
 // The kernel reads the rotation matrices before it waits for the launch in

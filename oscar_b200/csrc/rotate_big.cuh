@@ -1,0 +1,177 @@
+// Per-layer rotation of large batches with fp32 FMAs, register-tiled: the
+// same arithmetic class as rotate.cuh (every product and sum an fp32 FMA, each
+// output one ordered chain over k), at a tile size that keeps the FMA pipe,
+// not shared memory, the limit.
+//
+// CTA = 128 rows x 128 output columns of one segment, 256 threads; thread
+// (ty, tx) = (tid / 16, tid % 16) accumulates rows {4 ty + i, 64 + 4 ty + i}
+// x columns {4 tx + j, 64 + 4 tx + j} (8 x 8) over k in chunks of 32: x
+// (converted to fp32, transposed to [k][row]) and R ([k][column]) are staged
+// in shared memory, double-buffered, so each k costs four 16-byte shared loads
+// per 64 FMAs.  Used for batches of at least 2048 rows (rotate.cuh's 16-row
+// tiles for smaller ones).
+#pragma once
+
+#include "common.cuh"
+#include "rotate.cuh"
+
+namespace oscar {
+
+constexpr int kRbRows = 128;
+constexpr int kRbCols = 128;
+constexpr int kRbK = 32;
+constexpr int kRbThreads = 256;
+
+struct RbSmem {
+  float xs[2][kRbK][kRbRows];  // x^T of the chunk
+  float rs[2][kRbK][kRbCols];  // R rows of the chunk (columns c0 ..)
+};
+
+// one 16-byte chunk of x -> fp32 values (8 of a 16-bit type, 4 of fp32)
+template <typename InT>
+struct RbIn {
+  static constexpr int kPer = 8;
+  static OSCAR_DEVINL void convert(const uint4& u, float* f) {
+    const InT* e = reinterpret_cast<const InT*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = Elem<InT>::to_f32(e[j]);
+  }
+};
+template <>
+struct RbIn<float> {
+  static constexpr int kPer = 4;
+  static OSCAR_DEVINL void convert(const uint4& u, float* f) {
+    f[0] = __uint_as_float(u.x);
+    f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z);
+    f[3] = __uint_as_float(u.w);
+  }
+};
+
+template <typename InT, typename OutT, int D>
+__global__ void __launch_bounds__(kRbThreads) rotate_big_kernel(const __grid_constant__ RotBatch b) {
+  pdl_release();
+  if (!b.rot_early) pdl_wait();
+  extern __shared__ __align__(16) uint8_t rb_raw[];
+  RbSmem& sm = *reinterpret_cast<RbSmem*>(rb_raw);
+  constexpr int kPer = RbIn<InT>::kPer;
+  constexpr int kCpr = kRbK / kPer;                       // 16-byte chunks per row of a chunk
+  constexpr int kXItems = kRbRows * kCpr / kRbThreads;    // x chunks per thread per k-chunk
+  constexpr int kRItems = kRbK * kRbCols / 4 / kRbThreads;  // float4 of R per thread per k-chunk
+  constexpr int kChunks = D / kRbK;
+  const int tid = threadIdx.x;
+  int si = 0;
+  while (si + 1 < b.n && (int)blockIdx.x >= b.tile_begin[si + 1]) ++si;
+  const RotSeg& sg = b.seg[si];
+  const int64_t r0 = (int64_t)((int)blockIdx.x - b.tile_begin[si]) * kRbRows;
+  const int c0 = blockIdx.y * kRbCols;
+  const float* rot = sg.rot;
+
+  // loaders: x chunk u of this thread = (row, 16-byte piece); R float4 u = (k, column group)
+  auto load_r = [&](int kc, float4 (&rr)[kRItems]) {
+#pragma unroll
+    for (int u = 0; u < kRItems; ++u) {
+      const int i = tid + kRbThreads * u;
+      const int k = i / (kRbCols / 4), c4 = i % (kRbCols / 4);
+      const int kk = kc * kRbK + k;
+      if (!sg.transpose) {
+        rr[u] = *reinterpret_cast<const float4*>(rot + (int64_t)kk * D + c0 + 4 * c4);
+      } else {
+        // R^T[kk][c] = R[c][kk]
+        rr[u] = make_float4(rot[(int64_t)(c0 + 4 * c4) * D + kk], rot[(int64_t)(c0 + 4 * c4 + 1) * D + kk],
+                            rot[(int64_t)(c0 + 4 * c4 + 2) * D + kk], rot[(int64_t)(c0 + 4 * c4 + 3) * D + kk]);
+      }
+    }
+  };
+  const InT* xsrc[kXItems];
+  bool xlive[kXItems];
+  pdl_wait();
+#pragma unroll
+  for (int u = 0; u < kXItems; ++u) {
+    const int i = tid + kRbThreads * u;
+    const int64_t row = r0 + i / kCpr;
+    xlive[u] = row < sg.rows;
+    xsrc[u] = static_cast<const InT*>(sg.x) + (xlive[u] ? rot_row(row, sg.heads, sg.x_stride, D) : 0) + kPer * (i % kCpr);
+  }
+  auto load_x = [&](int kc, uint4 (&xr)[kXItems]) {
+#pragma unroll
+    for (int u = 0; u < kXItems; ++u)
+      xr[u] = xlive[u] ? *reinterpret_cast<const uint4*>(xsrc[u] + kc * kRbK) : make_uint4(0u, 0u, 0u, 0u);
+  };
+  auto store = [&](int buf, const uint4 (&xr)[kXItems], const float4 (&rr)[kRItems]) {
+#pragma unroll
+    for (int u = 0; u < kXItems; ++u) {
+      const int i = tid + kRbThreads * u;
+      const int row = i / kCpr, kb = kPer * (i % kCpr);
+      float f[kPer];
+      RbIn<InT>::convert(xr[u], f);
+#pragma unroll
+      for (int e = 0; e < kPer; ++e) sm.xs[buf][kb + e][row] = f[e];
+    }
+#pragma unroll
+    for (int u = 0; u < kRItems; ++u) {
+      const int i = tid + kRbThreads * u;
+      const int k = i / (kRbCols / 4), c4 = i % (kRbCols / 4);
+      *reinterpret_cast<float4*>(&sm.rs[buf][k][4 * c4]) = rr[u];
+    }
+  };
+
+  const int ty = tid >> 4, tx = tid & 15;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+  {
+    uint4 xr[kXItems];
+    float4 rr[kRItems];
+    load_x(0, xr);
+    load_r(0, rr);
+    store(0, xr, rr);
+  }
+  __syncthreads();
+  for (int kc = 0; kc < kChunks; ++kc) {
+    const int buf = kc & 1;
+    uint4 xr[kXItems];
+    float4 rr[kRItems];
+    if (kc + 1 < kChunks) {
+      load_x(kc + 1, xr);
+      load_r(kc + 1, rr);
+    }
+#pragma unroll 8
+    for (int k = 0; k < kRbK; ++k) {
+      const float4 xa = *reinterpret_cast<const float4*>(&sm.xs[buf][k][4 * ty]);
+      const float4 xb = *reinterpret_cast<const float4*>(&sm.xs[buf][k][64 + 4 * ty]);
+      const float4 ra = *reinterpret_cast<const float4*>(&sm.rs[buf][k][4 * tx]);
+      const float4 rb = *reinterpret_cast<const float4*>(&sm.rs[buf][k][64 + 4 * tx]);
+      const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+      const float rv[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(xv[i], rv[j], acc[i][j]);
+    }
+    if (kc + 1 < kChunks) store(buf ^ 1, xr, rr);
+    __syncthreads();
+  }
+  OutT* out = static_cast<OutT*>(sg.out);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t row = r0 + (i < 4 ? 4 * ty + i : 64 + 4 * ty + (i - 4));
+    if (row >= sg.rows) continue;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int col = c0 + 64 * h + 4 * tx;
+      if (out != nullptr) {
+        OutT* o = out + rot_row(row, sg.heads, sg.out_stride, D) + col;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) rot_store<OutT>(o + j, acc[i][4 * h + j]);
+      }
+      if (sg.out_f32 != nullptr)
+        *reinterpret_cast<float4*>(sg.out_f32 + rot_row(row, sg.heads, sg.out_f32_stride, D) + col) =
+            make_float4(acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+    }
+  }
+}
+
+}  // namespace oscar

@@ -476,15 +476,17 @@ def set_attention_path(path: str) -> None:
     check(_native.lib().oscar_set_attention_path(_PATHS[path]))
 
 
-_ROT_PATHS = {"auto": 0, "fma": 1, "tensor": 2}
+_ROT_PATHS = {"auto": 0, "fma": 1, "tensor": 2, "fma_big": 3}
 
 
 def set_rotation_path(path: str) -> None:
     """Rotation kernel for rotate_rows / rotate_rows_many and the layer step:
-    "auto" (tcgen05 kind::tf32 with split precision for batches of at least
-    2048 fp32 rows -- the output rotation -- and fp32 FMAs for the k / v / q
-    rotations), "fma" or "tensor".  Both compute x @ R to within a few fp32
-    ulps."""
+    "auto" (per tensor, by its own size: tcgen05 kind::tf32 with split
+    precision for fp32 tensors of at least 2048 rows -- the output rotation --,
+    register-tiled fp32 FMAs for 16-bit ones of at least 16384 rows -- the
+    k / v / q rotations of long chunks --, 16-row FMA tiles for the rest), "fma" (16-row FMA tiles), "tensor" or "fma_big"
+    (register-tiled FMAs, D 128 or 256).  All compute x @ R to within a few
+    fp32 ulps."""
     check(_native.lib().oscar_set_rotation_path(_ROT_PATHS[path]))
 
 

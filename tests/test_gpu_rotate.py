@@ -1,7 +1,9 @@
 """The per-layer rotation kernels (x @ R and x @ R^T) against torch's fp64
 product, for every dtype pair the backend uses and strided outputs: the fp32
-FMA kernel and the tcgen05 kind::tf32 kernel with split precision (each test
-runs on both, through the process-wide rotation path)."""
+FMA kernel of 16-row tiles, the tcgen05 kind::tf32 kernel with split
+precision and the register-tiled FMA kernel of 128-row tiles (each test runs
+on all three, through the process-wide rotation path; D 64 always takes the
+16-row kernel on the last)."""
 import pytest
 import torch
 
@@ -10,7 +12,7 @@ from gpu_helpers import need_gpu
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["fma", "tensor"], autouse=True)
+@pytest.fixture(params=["fma", "tensor", "fma_big"], autouse=True)
 def rot_path(request):
     from oscar_b200 import kernels
 
