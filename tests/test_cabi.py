@@ -69,3 +69,22 @@ def test_host_side_validation_without_gpu(lib):
     assert st == _native.ERR_UNSUPPORTED
     st = lib.oscar_staging_write(None, None, 1, 1, 64, None, None, None, 0, 0, 0, None, None, None, 8, 4, None, 0, None)
     assert st == _native.ERR_INVALID and b"epoch" in lib.oscar_last_error()
+
+
+def test_shard_and_layer_step_host_validation(lib):
+    qsl = (ctypes.c_int32 * 2)(0, 4)
+    hist = (ctypes.c_int32 * 1)(100)
+    # history shards run the decode kernels: D 128 is refused before any CUDA call
+    st = lib.oscar_slab_attention_shard(None, 1, 4, 6, 1, 128, None, None, 4, 16, 0, 0, 0, 0, 0, 0, None, 1, 8,
+                                        qsl, hist, 1, 1.0, None, None, None, 0, None, None, None, 0, None)
+    assert st == _native.ERR_UNSUPPORTED
+    with pytest.raises(ValueError, match="decode kernels"):
+        _native.check(st)
+    # the layer step takes 16-bit activations only
+    st = lib.oscar_decode_layer_step(None, None, None, 0, 0, 0, 0, 4, 6, 1, 256, None, None, None, 0.0, 0.0, None,
+                                     None, 4, 16, 0, 0, 0, 0, 0, 0, None, None, None, None, 1, 8, qsl, hist, 1, 0,
+                                     256, 1.0, None, None, None, 1, None, 0, None, 0, None)
+    assert st == _native.ERR_UNSUPPORTED
+    assert lib.oscar_decode_layer_step_scratch(4, 6, 1, 256, _native.DTYPE_BF16) > 0
+    assert lib.oscar_set_rotation_path(7) == _native.ERR_INVALID
+    assert lib.oscar_set_rotation_path(0) == _native.OK
