@@ -1173,9 +1173,12 @@ int launch_rotate_tc_d(const oscar::RotBatch& b16, cudaStream_t s) {
 }
 
 // automatic thresholds (rows of one segment): the tensor-core kernel from 2048
-// fp32 rows, the register-tiled FMA kernel from 16384 rows (128-row tiles: a
-// smaller segment leaves SMs idle and the 16-row tiles finish first)
+// fp32 rows; the register-tiled FMA kernel in 64-row tiles from 6144 rows and
+// in 128-row tiles from 16384 rows.  A 64 x 128 tile takes about 27 us on its
+// SM, so below 6144 rows (D 256) the 16-row tiles finish first; a smaller
+// segment in 128-row tiles leaves SMs idle.
 constexpr int64_t kRotTcMinRows = 2048;
+constexpr int64_t kRotMidMinRows = 6144;
 constexpr int64_t kRotBigMinRows = 16384;
 
 // The tensor-core and the register-tiled kernels write 16-byte pieces of every
@@ -1186,27 +1189,27 @@ bool rotate_rows_aligned(const oscar::RotSeg& g, size_t out_es) {
   return g.out_f32 == nullptr || !((reinterpret_cast<uintptr_t>(g.out_f32) & 15) || g.out_f32_stride % 4);
 }
 
-// register-tiled FMA rotation of a batch, in 128-row tiles (D = 128 or 256)
-template <typename InT, typename OutT, int D>
+// register-tiled FMA rotation of a batch, in ROWS-row tiles (D = 128 or 256)
+template <typename InT, typename OutT, int D, int ROWS>
 int launch_rotate_big_d(const oscar::RotBatch& b16, cudaStream_t s) {
   oscar::RotBatch b = b16;
   int64_t tiles = 0;
   for (int i = 0; i < b.n; ++i) {
     b.tile_begin[i] = (int)tiles;
-    tiles += (b.seg[i].rows + oscar::kRbRows - 1) / oscar::kRbRows;
+    tiles += (b.seg[i].rows + ROWS - 1) / ROWS;
   }
   b.tile_begin[b.n] = (int)tiles;
-  constexpr size_t smem = sizeof(oscar::RbSmem);
+  constexpr size_t smem = sizeof(oscar::RbSmem<ROWS>);
   static thread_local int cfg_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (cfg_dev != dev) {
-    cudaFuncSetAttribute(oscar::rotate_big_kernel<InT, OutT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(oscar::rotate_big_kernel<InT, OutT, D, ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
     cfg_dev = dev;
   }
   dim3 grid((unsigned)tiles, (unsigned)(D / oscar::kRbCols));
-  launch_pdl(oscar::rotate_big_kernel<InT, OutT, D>, grid, dim3(oscar::kRbThreads), smem, s, b);
+  launch_pdl(oscar::rotate_big_kernel<InT, OutT, D, ROWS>, grid, dim3(oscar::kRbThreads), smem, s, b);
   return cuda_status("rotate_big_kernel");
 }
 
@@ -1249,15 +1252,16 @@ oscar::RotBatch rotate_subset(const oscar::RotBatch& b, Pred keep) {
 // to an outlier channel, turns a rotation error of a few fp32 ulps into a
 // visible change of the attention, and the tf32 split's error is several
 // times an fp32 FMA chain's.  Smaller segments take rotate.cuh's 16-row tiles.
-enum RotKernel { kRotSmall = 0, kRotBig = 1, kRotTc = 2 };
+enum RotKernel { kRotSmall = 0, kRotBig = 1, kRotTc = 2, kRotMid = 3 };
 template <typename InT>
 RotKernel rotate_kernel_of(const oscar::RotSeg& g, int d, size_t out_es, int path) {
   const bool aligned = rotate_rows_aligned(g, out_es);
   if (path == 1 || !aligned) return kRotSmall;
   if (path == 2) return kRotTc;
-  if (path == 3) return d >= oscar::kRbCols ? kRotBig : kRotSmall;
+  const RotKernel tiled = g.rows >= kRotBigMinRows ? kRotBig : kRotMid;
+  if (path == 3) return d >= oscar::kRbCols ? tiled : kRotSmall;
   if (std::is_same<InT, float>::value) return g.rows >= kRotTcMinRows ? kRotTc : kRotSmall;
-  return (g.rows >= kRotBigMinRows && d >= oscar::kRbCols) ? kRotBig : kRotSmall;
+  return (g.rows >= kRotMidMinRows && d >= oscar::kRbCols) ? tiled : kRotSmall;
 }
 
 template <typename InT, typename OutT>
@@ -1273,11 +1277,14 @@ int launch_rotate(const oscar::RotBatch& b, int d, cudaStream_t s) {
     if (sub.n == 0) return OSCAR_OK;
     if (k == kRotTc) return launch_rotate_tc<InT, OutT>(sub, d, s);
     if (k == kRotBig)
-      return d == 256 ? launch_rotate_big_d<InT, OutT, 256>(sub, s) : launch_rotate_big_d<InT, OutT, 128>(sub, s);
+      return d == 256 ? launch_rotate_big_d<InT, OutT, 256, 128>(sub, s)
+                      : launch_rotate_big_d<InT, OutT, 128, 128>(sub, s);
+    if (k == kRotMid)
+      return d == 256 ? launch_rotate_big_d<InT, OutT, 256, 64>(sub, s) : launch_rotate_big_d<InT, OutT, 128, 64>(sub, s);
     return launch_rotate_fma<InT, OutT>(sub, d, s);
   };
   if (!mixed) return run(b, b.n > 0 ? which[0] : kRotSmall);
-  for (RotKernel k : {kRotSmall, kRotBig, kRotTc}) {
+  for (RotKernel k : {kRotSmall, kRotMid, kRotBig, kRotTc}) {
     const int st = run(rotate_subset(b, [&](int i) { return which[i] == k; }), k);
     if (st) return st;
   }

@@ -3,13 +3,14 @@
 // output one ordered chain over k), at a tile size that keeps the FMA pipe,
 // not shared memory, the limit.
 //
-// CTA = 128 rows x 128 output columns of one segment, 256 threads; thread
-// (ty, tx) = (tid / 16, tid % 16) accumulates rows {4 ty + i, 64 + 4 ty + i}
-// x columns {4 tx + j, 64 + 4 tx + j} (8 x 8) over k in chunks of 32: x
-// (converted to fp32, transposed to [k][row]) and R ([k][column]) are staged
-// in shared memory, double-buffered, so each k costs four 16-byte shared loads
-// per 64 FMAs.  Used for batches of at least 2048 rows (rotate.cuh's 16-row
-// tiles for smaller ones).
+// CTA = ROWS (128 or 64) rows x 128 output columns of one segment, 256
+// threads; thread (ty, tx) = (tid / 16, tid % 16) accumulates rows
+// {4 ty + i, 64 + 4 ty + i} (only {4 ty + i} at ROWS 64) x columns
+// {4 tx + j, 64 + 4 tx + j} over k in chunks of 32: x (converted to fp32,
+// transposed to [k][row]) and R ([k][column]) are staged in shared memory,
+// double-buffered, so each k costs four (three) 16-byte shared loads per 64
+// (32) FMAs.  128-row tiles for long segments, 64-row tiles for mid-sized
+// ones (twice the CTAs on the SMs), rotate.cuh's 16-row tiles below that.
 #pragma once
 
 #include "common.cuh"
@@ -17,13 +18,13 @@
 
 namespace oscar {
 
-constexpr int kRbRows = 128;
 constexpr int kRbCols = 128;
 constexpr int kRbK = 32;
 constexpr int kRbThreads = 256;
 
+template <int ROWS>
 struct RbSmem {
-  float xs[2][kRbK][kRbRows];  // x^T of the chunk
+  float xs[2][kRbK][ROWS];     // x^T of the chunk
   float rs[2][kRbK][kRbCols];  // R rows of the chunk (columns c0 ..)
 };
 
@@ -48,22 +49,24 @@ struct RbIn<float> {
   }
 };
 
-template <typename InT, typename OutT, int D>
+template <typename InT, typename OutT, int D, int ROWS>
 __global__ void __launch_bounds__(kRbThreads) rotate_big_kernel(const __grid_constant__ RotBatch b) {
+  static_assert(ROWS == 128 || ROWS == 64, "row tiles of 128 or 64");
+  constexpr int kRg = ROWS / 64;  // groups of 4 rows per thread: rows 64 g + 4 ty + i
   pdl_release();
   if (!b.rot_early) pdl_wait();
   extern __shared__ __align__(16) uint8_t rb_raw[];
-  RbSmem& sm = *reinterpret_cast<RbSmem*>(rb_raw);
+  RbSmem<ROWS>& sm = *reinterpret_cast<RbSmem<ROWS>*>(rb_raw);
   constexpr int kPer = RbIn<InT>::kPer;
   constexpr int kCpr = kRbK / kPer;                       // 16-byte chunks per row of a chunk
-  constexpr int kXItems = kRbRows * kCpr / kRbThreads;    // x chunks per thread per k-chunk
+  constexpr int kXItems = ROWS * kCpr / kRbThreads;       // x chunks per thread per k-chunk
   constexpr int kRItems = kRbK * kRbCols / 4 / kRbThreads;  // float4 of R per thread per k-chunk
   constexpr int kChunks = D / kRbK;
   const int tid = threadIdx.x;
   int si = 0;
   while (si + 1 < b.n && (int)blockIdx.x >= b.tile_begin[si + 1]) ++si;
   const RotSeg& sg = b.seg[si];
-  const int64_t r0 = (int64_t)((int)blockIdx.x - b.tile_begin[si]) * kRbRows;
+  const int64_t r0 = (int64_t)((int)blockIdx.x - b.tile_begin[si]) * ROWS;
   const int c0 = blockIdx.y * kRbCols;
   const float* rot = sg.rot;
 
@@ -117,9 +120,9 @@ __global__ void __launch_bounds__(kRbThreads) rotate_big_kernel(const __grid_con
   };
 
   const int ty = tid >> 4, tx = tid & 15;
-  float acc[8][8];
+  float acc[4 * kRg][8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < 4 * kRg; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
   {
@@ -140,14 +143,20 @@ __global__ void __launch_bounds__(kRbThreads) rotate_big_kernel(const __grid_con
     }
 #pragma unroll 8
     for (int k = 0; k < kRbK; ++k) {
-      const float4 xa = *reinterpret_cast<const float4*>(&sm.xs[buf][k][4 * ty]);
-      const float4 xb = *reinterpret_cast<const float4*>(&sm.xs[buf][k][64 + 4 * ty]);
+      float xv[4 * kRg];
+#pragma unroll
+      for (int g = 0; g < kRg; ++g) {
+        const float4 xa = *reinterpret_cast<const float4*>(&sm.xs[buf][k][64 * g + 4 * ty]);
+        xv[4 * g] = xa.x;
+        xv[4 * g + 1] = xa.y;
+        xv[4 * g + 2] = xa.z;
+        xv[4 * g + 3] = xa.w;
+      }
       const float4 ra = *reinterpret_cast<const float4*>(&sm.rs[buf][k][4 * tx]);
       const float4 rb = *reinterpret_cast<const float4*>(&sm.rs[buf][k][64 + 4 * tx]);
-      const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
       const float rv[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < 4 * kRg; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(xv[i], rv[j], acc[i][j]);
     }
@@ -156,8 +165,8 @@ __global__ void __launch_bounds__(kRbThreads) rotate_big_kernel(const __grid_con
   }
   OutT* out = static_cast<OutT*>(sg.out);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int64_t row = r0 + (i < 4 ? 4 * ty + i : 64 + 4 * ty + (i - 4));
+  for (int i = 0; i < 4 * kRg; ++i) {
+    const int64_t row = r0 + 64 * (i / 4) + 4 * ty + (i % 4);
     if (row >= sg.rows) continue;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
