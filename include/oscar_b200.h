@@ -60,12 +60,13 @@ int oscar_set_attention_path(int path);
  * calls in this process, chosen per segment by the segment's own size: 0 =
  * automatic (fp32 segments of at least 2048 rows -- the attention output's
  * o @ R_v^T -- on the tcgen05 kind::tf32 kernel; 16-bit segments of at least
- * 16384 rows -- the k / v / q rotations, whose rounding the INT2 codes and
+ * 6144 rows -- the k / v / q rotations, whose rounding the INT2 codes and
  * the attention scores are sensitive to -- on the register-tiled fp32 FMA
- * kernel (D 128 or 256); the rest on the fp32 FMA kernel of 16-row tiles), 1 = the 16-row FMA kernel
- * only, 2 = the tensor-core kernel, 3 = the register-tiled FMA kernel (D 128
- * or 256).  The last two need 16-byte aligned output rows, else the 16-row
- * kernel runs.  The tensor-core kernel splits R (and fp32
+ * kernel (D 128 or 256; 64-row tiles below 16384 rows, 128-row tiles from
+ * there); the rest on the fp32 FMA kernel of 16-row tiles), 1 = the 16-row
+ * FMA kernel only, 2 = the tensor-core kernel, 3 = the register-tiled FMA
+ * kernel (D 128 or 256, tiles by size as above).  The last two need 16-byte
+ * aligned output rows, else the 16-row kernel runs.  The tensor-core kernel splits R (and fp32
  * x) into two tf32 terms, so both compute x @ R to within a few fp32 ulps;
  * the switch keeps both parity-tested.  Other values: status 1. */
 int oscar_set_rotation_path(int path);
