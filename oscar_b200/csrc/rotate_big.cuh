@@ -50,9 +50,10 @@ struct RbIn<float> {
 };
 
 template <typename InT, typename OutT, int D, int ROWS>
-__global__ void __launch_bounds__(kRbThreads) rotate_big_kernel(const __grid_constant__ RotBatch b) {
+__global__ void __launch_bounds__(kRbThreads, ROWS == 64 && sizeof(InT) == 2 ? 3 : 1) rotate_big_kernel(const __grid_constant__ RotBatch b) {
   static_assert(ROWS == 128 || ROWS == 64, "row tiles of 128 or 64");
   constexpr int kRg = ROWS / 64;  // groups of 4 rows per thread: rows 64 g + 4 ty + i
+  constexpr int kUnroll = ROWS == 64 ? kRbK : 8;  // k-steps per unrolled body (64-row tiles: within 80 registers)
   pdl_release();
   if (!b.rot_early) pdl_wait();
   extern __shared__ __align__(16) uint8_t rb_raw[];
@@ -141,19 +142,30 @@ __global__ void __launch_bounds__(kRbThreads) rotate_big_kernel(const __grid_con
       load_x(kc + 1, xr);
       load_r(kc + 1, rr);
     }
-#pragma unroll 8
+    // the fragments of k-step k + 1 are loaded while k-step k computes (two
+    // register slots): with one or two CTAs per SM the shared-memory latency
+    // is not hidden by other warps
+    float4 fx[2][kRg], fr[2][2];
+    auto frag = [&](int k, float4 (&x)[kRg], float4 (&r)[2]) {
+#pragma unroll
+      for (int g = 0; g < kRg; ++g) x[g] = *reinterpret_cast<const float4*>(&sm.xs[buf][k][64 * g + 4 * ty]);
+      r[0] = *reinterpret_cast<const float4*>(&sm.rs[buf][k][4 * tx]);
+      r[1] = *reinterpret_cast<const float4*>(&sm.rs[buf][k][64 + 4 * tx]);
+    };
+    frag(0, fx[0], fr[0]);
+#pragma unroll(kUnroll)
     for (int k = 0; k < kRbK; ++k) {
+      if (k + 1 < kRbK) frag(k + 1, fx[(k + 1) & 1], fr[(k + 1) & 1]);
       float xv[4 * kRg];
 #pragma unroll
       for (int g = 0; g < kRg; ++g) {
-        const float4 xa = *reinterpret_cast<const float4*>(&sm.xs[buf][k][64 * g + 4 * ty]);
+        const float4 xa = fx[k & 1][g];
         xv[4 * g] = xa.x;
         xv[4 * g + 1] = xa.y;
         xv[4 * g + 2] = xa.z;
         xv[4 * g + 3] = xa.w;
       }
-      const float4 ra = *reinterpret_cast<const float4*>(&sm.rs[buf][k][4 * tx]);
-      const float4 rb = *reinterpret_cast<const float4*>(&sm.rs[buf][k][64 + 4 * tx]);
+      const float4 ra = fr[k & 1][0], rb = fr[k & 1][1];
       const float rv[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
 #pragma unroll
       for (int i = 0; i < 4 * kRg; ++i)
