@@ -58,7 +58,7 @@ int oscar_set_attention_path(int path);
 
 /* Selects the rotation kernel for later oscar_rotate_rows* and layer-step
  * calls in this process, chosen per segment by the segment's own size: 0 =
- * automatic (fp32 segments of at least 2048 rows -- the attention output's
+ * automatic (fp32 segments of at least 2560 rows -- the attention output's
  * o @ R_v^T -- on the tcgen05 kind::tf32 kernel; 16-bit segments of at least
  * 6144 rows -- the k / v / q rotations, whose rounding the INT2 codes and
  * the attention scores are sensitive to -- on the register-tiled fp32 FMA

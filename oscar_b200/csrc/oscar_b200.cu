@@ -1172,12 +1172,13 @@ int launch_rotate_tc_d(const oscar::RotBatch& b16, cudaStream_t s) {
   return cuda_status("rotate_tc_kernel");
 }
 
-// automatic thresholds (rows of one segment): the tensor-core kernel from 2048
-// fp32 rows; the register-tiled FMA kernel in 64-row tiles from 6144 rows and
+// automatic thresholds (rows of one segment): the tensor-core kernel from 2560
+// fp32 rows (D 256: 22 us from 2048 to 3840 rows, where the 16-row tiles take
+// 18 to 31 us); the register-tiled FMA kernel in 64-row tiles from 6144 rows and
 // in 128-row tiles from 16384 rows.  A 64 x 128 tile takes about 27 us on its
 // SM, so below 6144 rows (D 256) the 16-row tiles finish first; a smaller
 // segment in 128-row tiles leaves SMs idle.
-constexpr int64_t kRotTcMinRows = 2048;
+constexpr int64_t kRotTcMinRows = 2560;
 constexpr int64_t kRotMidMinRows = 6144;
 constexpr int64_t kRotBigMinRows = 16384;
 

@@ -482,7 +482,7 @@ _ROT_PATHS = {"auto": 0, "fma": 1, "tensor": 2, "fma_big": 3}
 def set_rotation_path(path: str) -> None:
     """Rotation kernel for rotate_rows / rotate_rows_many and the layer step:
     "auto" (per tensor, by its own size: tcgen05 kind::tf32 with split
-    precision for fp32 tensors of at least 2048 rows -- the output rotation --,
+    precision for fp32 tensors of at least 2560 rows -- the output rotation --,
     register-tiled fp32 FMAs for 16-bit ones of at least 6144 rows -- the
     k / v / q rotations of long chunks; 64-row tiles below 16384 rows, 128-row
     tiles from there --, 16-row FMA tiles for the rest), "fma" (16-row FMA
